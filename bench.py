@@ -1,0 +1,476 @@
+"""Benchmark of the Cascade block data path on B200.
+
+Default workload (N=1): 65,536 Qwen2.5-7B-shaped KV blocks (917,504 B, fp16
+N(0,1) from a seeded generator), 25 % of them byte-identical copies of 64
+prefix blocks; one step = clear the store, batch_put every block in batches
+of 1024 (GPU SHA-256 + dedup + scatter into the HBM slab pool), then
+batch_get every stored block in a uniformly shuffled order (gather). Inputs
+(60 GB) are resident in HBM before the timed region and are far larger than
+L2, so no L2 flush is needed.
+
+value  = (bytes put + bytes got) / step time  [GB/s, 1e9]
+e2e    = same metric through the public API with pinned HOST buffers
+         (host->device copies of the blocks and device->host copies of the
+         results inside the timed region), on a bounded slice.
+--impl reference: the reference's own CPU path (compute_block_id with
+OpenMP + CascadeStore::put_batch/get_batch on its SHM tier), compiled from
+its sources into oracle/_ref, on a bounded slice of the same workload.
+
+With torchrun (N>1) every rank runs the same workload on its own GPU and
+store (independent replicas, weak scaling); rank 0 prints max-over-ranks
+timing.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "kcj-cascade-v6_b200"))
+sys.path.insert(0, ROOT)
+
+METRIC = "aggregate batch_put (incl. SHA256) + batch_get GB/s"
+GB = 1e9
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--blocks", type=int, default=65536)
+    p.add_argument("--batch", type=int, default=1024)
+    p.add_argument("--block-bytes", type=int, default=917504)
+    p.add_argument("--e2e-blocks", type=int, default=4096)
+    p.add_argument("--cpu-blocks", type=int, default=1024)
+    p.add_argument("--copy-engine", type=int, default=0)
+    p.add_argument("--hash-lanes", type=int, default=32)
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-cpu", action="store_true")
+    return p.parse_args()
+
+
+# ----------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while running."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        if shutil.which("nvidia-smi") is None:
+            return self
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits", "-lms", "200"],
+                                     stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 7:
+                try:
+                    rows.append((float(parts[0]), float(parts[1]), parts[3:7]))
+                except ValueError:
+                    pass
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1],
+                "samples": len(rows), "reasons": reasons}
+
+
+# --------------------------------------------------------------- workload
+
+def workload(args, rank):
+    from cascade_cpp import workloads as W
+    src, is_prefix = W.dedup_mix(args.blocks, 64, 0.25, 2024 + rank)
+    uniq = np.unique(src)
+    return src, is_prefix, uniq
+
+
+def gpu_blocks(args, rank, device):
+    """Unique blocks generated on the GPU (seeded); per-position pointers."""
+    import torch
+    src, is_prefix, uniq = workload(args, rank)
+    size = args.block_bytes
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    pool = torch.empty(len(uniq) * size, dtype=torch.uint8, device=device)
+    chunk = 4096 * size // 2
+    flat = pool.view(torch.float16)
+    for o in range(0, flat.numel(), chunk):
+        n = min(chunk, flat.numel() - o)
+        flat[o:o + n] = torch.randn(n, generator=g, device=device, dtype=torch.float16)
+    pos = np.searchsorted(uniq, src)
+    ptrs = np.uint64(pool.data_ptr()) + pos.astype(np.uint64) * np.uint64(size)
+    return pool, ptrs.astype(np.uint64), is_prefix.astype(np.uint8)
+
+
+def make_store(args, device_index, capacity):
+    import cascade_cpp
+    cfg = cascade_cpp.DistributedConfig()
+    cfg.gpu_capacity_per_device = capacity
+    cfg.dram_capacity = 0
+    cfg.device = device_index
+    cfg.copy_engine = args.copy_engine
+    cfg.index_log2 = 18
+    cfg.hash_lanes = args.hash_lanes
+    cfg.profile = True   # per-kernel CUDA-event timing for the roofline fields
+    cfg.dht = False      # one independent store per rank (replicas)
+    return cascade_cpp.DistributedStore(cfg)
+
+
+def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_memory=True):
+    """One step: put everything in batches, then get every stored key in a
+    shuffled order into out_buf (one batch at a time). Returns (put_s, get_s,
+    put_bytes, get_bytes) measured with CUDA events on the current stream."""
+    import torch
+    n = len(ptrs)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    keys_all = np.empty((n, 16), np.uint8)
+    ev[0].record()
+    for i in range(0, n, batch):
+        k, _ = store.put_ptrs(ptrs[i:i + batch], sizes[i:i + batch], device_memory,
+                              prefix=prefix[i:i + batch])
+        keys_all[i:i + batch] = k
+    ev[1].record()
+    uk = np.unique(keys_all.view(np.dtype((np.void, 16))).reshape(-1))
+    order = np.random.default_rng(rng_seed).permutation(len(uk))
+    keys = uk[order].view(np.uint8).reshape(-1, 16)
+    base = out_buf.data_ptr() if hasattr(out_buf, "data_ptr") else out_buf.ctypes.data
+    outs_b = np.uint64(base) + np.arange(batch, dtype=np.uint64) * np.uint64(size)
+    got = 0
+    for i in range(0, len(keys), batch):
+        kk = keys[i:i + batch]
+        m = len(kk)
+        s, f = store.get_ptrs(kk, outs_b[:m], np.full(m, size, np.uint64), device_memory)
+        got += int(s[(f & 0x0F) != 0].sum())
+    ev[2].record()
+    ev[2].synchronize()
+    put_s = ev[0].elapsed_time(ev[1]) / 1e3
+    get_s = ev[1].elapsed_time(ev[2]) / 1e3
+    return put_s, get_s, int(sizes.sum()), got
+
+
+def reduce_max(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def reduce_sum(x, world):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# --------------------------------------------------------------- baseline
+
+def cpu_reference(args, n_blocks, steps=1, threads=None):
+    """The reference's CPU path (oracle/_ref): OpenMP compute_block_id over
+    the batch, CascadeStore::put_batch into its SHM tier, shuffled
+    get_batch. Returns (GB/s, details)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle", "_ref"))
+    import cascade_ref
+    from cascade_cpp import workloads as W
+    size = args.block_bytes
+    src, is_prefix = W.dedup_mix(n_blocks, max(1, n_blocks // 64), 0.25, 77)
+    uniq = np.unique(src)
+    packed_u = np.empty(len(uniq) * size, np.uint8)
+    for i, s in enumerate(uniq):
+        packed_u[i * size:(i + 1) * size] = W.kv_block_fp16(int(s), size)
+    pos = np.searchsorted(uniq, src)
+    offsets = (pos * size).astype(np.uint64)
+    sizes = np.full(n_blocks, size, np.uint64)
+    threads = threads or os.cpu_count()
+    shm = f"/dev/shm/cascade_bench_{os.getpid()}"
+    cap = len(uniq) * size + (64 << 20)
+    out = np.empty(len(uniq) * size, np.uint8)
+    out_off = (np.arange(len(uniq)) * size).astype(np.uint64)
+    times = []
+    for _ in range(steps):
+        store = cascade_ref.CascadeStore(shm_capacity=cap, shm_path=shm)
+        t0 = time.perf_counter()
+        for i in range(0, n_blocks, args.batch):
+            ids = cascade_ref.compute_block_ids(packed_u, offsets[i:i + args.batch], sizes[i:i + args.batch],
+                                                threads)
+            store.put_batch(ids, packed_u, offsets[i:i + args.batch], sizes[i:i + args.batch])
+        t1 = time.perf_counter()
+        all_ids = list(dict.fromkeys(cascade_ref.compute_block_ids(packed_u, out_off, np.full(len(uniq), size,
+                                                                                            np.uint64), threads)))
+        order = np.random.default_rng(5).permutation(len(all_ids))
+        t2 = time.perf_counter()
+        for i in range(0, len(order), args.batch):
+            sel = order[i:i + args.batch]
+            found, _ = store.get_batch([all_ids[j] for j in sel], out, out_off[:len(sel)])
+            assert found == len(sel)
+        t3 = time.perf_counter()
+        times.append((t1 - t0, t3 - t2))
+        del store
+        shutil.rmtree(shm, ignore_errors=True)
+    put_s = float(np.median([t[0] for t in times]))
+    get_s = float(np.median([t[1] for t in times]))
+    put_b, get_b = n_blocks * size, len(uniq) * size
+    return (put_b + get_b) / (put_s + get_s) / GB, {
+        "put_gbs": put_b / put_s / GB, "get_gbs": get_b / get_s / GB, "cores": threads,
+        "sample": f"{n_blocks} x {size} B blocks (25% copies), batch {args.batch}"}
+
+
+# ------------------------------------------------------------------- main
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        ok = os.path.exists(os.path.join(ROOT, "oracle", "_ref"))
+        if not ok:
+            print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built"}))
+            return
+        vals = []
+        for _ in range(args.warmup):
+            cpu_reference(args, args.cpu_blocks)
+        t0 = time.perf_counter()
+        det = None
+        for _ in range(args.steps):
+            v, det = cpu_reference(args, args.cpu_blocks)
+            vals.append(v)
+        el = time.perf_counter() - t0
+        v = float(np.median(vals))
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic", "config": config_dict(args),
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": det["cores"], "kind": "reference",
+                             "sample": det["sample"], "put_gbs": round(det["put_gbs"], 3),
+                             "get_gbs": round(det["get_gbs"], 3)},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    size = args.block_bytes
+
+    pool, ptrs, prefix = gpu_blocks(args, rank, device)
+    sizes = np.full(len(ptrs), size, np.uint64)
+    n_unique = pool.numel() // size
+    store = make_store(args, local, n_unique * size + (256 << 20))
+    out_buf = torch.empty(args.batch * size, dtype=torch.uint8, device=device)
+
+    def sync_all():
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+
+    for w in range(args.warmup):
+        store.clear()
+        run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, w)
+    st0 = store._n.stats()
+    sync_all()
+    put_t = get_t = 0.0
+    put_b = get_b = 0
+    t_ev0 = torch.cuda.Event(enable_timing=True)
+    t_ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        t_ev0.record()
+        for s in range(args.steps):
+            store.clear()
+            ps, gs, pb, gb = run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, 100 + s)
+            put_t += ps
+            get_t += gs
+            put_b += pb
+            get_b += gb
+        t_ev1.record()
+        sync_all()
+    elapsed = t_ev0.elapsed_time(t_ev1) / 1e3
+    st1 = store._n.stats()
+    elapsed_max = reduce_max(elapsed, world)
+    total_bytes = reduce_sum(put_b + get_b, world)
+    value = total_bytes / elapsed_max / GB
+    put_gbs = reduce_sum(put_b / put_t, world) / GB
+    get_gbs = reduce_sum(get_b / get_t, world) / GB
+
+    peaks = {}
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        peaks = json.load(open(pk))
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+
+    def d(f):
+        return getattr(st1, f) - getattr(st0, f)
+
+    sha_s = d("sha_ns") / 1e9
+    sha_bytes_launch = d("sha_bytes") / max(d("sha_launches"), 1)
+    sha_achieved = d("sha_bytes") / sha_s / GB if sha_s else 0.0
+    gather_s = d("gather_ns") / 1e9
+    gather_alg = 2 * d("gather_bytes")
+    gather_achieved = gather_alg / gather_s / GB if gather_s else 0.0
+    scatter_s = d("scatter_ns") / 1e9
+    scatter_achieved = 2 * d("scatter_bytes") / scatter_s / GB if scatter_s else 0.0
+    launches = d("kernel_launches")
+
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded fp16 N(0,1) KV blocks generated on the GPU)",
+        "config": config_dict(args),
+        "batch_put_gbs": round(put_gbs, 3), "batch_get_gbs": round(get_gbs, 3),
+        "roofline": {
+            "kernel": "sha256_batch_kernel", "bound": "hbm", "achieved": round(sha_achieved, 2),
+            "peak": hbm_peak, "unit": "GB/s", "frac": round(sha_achieved / hbm_peak, 5),
+            "peak_source": peak_src, "traffic": None,
+            "bytes_per_launch": int(sha_bytes_launch),
+            "note": "bytes = block bytes read once per launch; binding limit is the SHA-256 chain latency "
+                    "(one serial chain per block, chains = batch size)",
+            "chain_bound": {"chains_per_launch": args.batch,
+                            "per_chain_MBps": round(sha_achieved * 1e3 / max(args.batch, 1), 2)},
+        },
+        "roofline_get": {
+            "kernel": "copy (gather)", "bound": "hbm", "achieved": round(gather_achieved, 2), "peak": hbm_peak,
+            "unit": "GB/s", "frac": round(gather_achieved / hbm_peak, 4), "peak_source": peak_src,
+            "bytes_per_launch": int(gather_alg / max(d("gather_launches"), 1)),
+        },
+        "roofline_put_scatter": {"achieved": round(scatter_achieved, 2), "unit": "GB/s",
+                                 "frac": round(scatter_achieved / hbm_peak, 4)},
+        "gpu_launches": int(launches),
+    }
+    line["clocks"] = clk.summary()
+
+    if rank == 0 and not args.no_sweep:
+        line["sweep"] = batch_sweep(args, store, ptrs, sizes, prefix, out_buf, size)
+    del pool
+    torch.cuda.empty_cache()
+    if not args.no_e2e:
+        line["e2e"] = e2e_run(args, rank, world, device, store)
+    if rank == 0 and not args.no_cpu:
+        try:
+            v, det = cpu_reference(args, args.cpu_blocks, steps=1)
+            line["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": det["cores"],
+                                    "kind": "reference", "sample": det["sample"],
+                                    "put_gbs": round(det["put_gbs"], 3), "get_gbs": round(det["get_gbs"], 3)}
+        except Exception as e:  # pragma: no cover
+            line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    store.close()
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def config_dict(args):
+    return {"workload": f"config2: {args.blocks} x {args.block_bytes} B Qwen2.5-7B KV blocks (fp16), 25% "
+                        f"byte-identical copies of 64 prefix blocks; step = clear + batch_put all (batch "
+                        f"{args.batch}) + batch_get all unique in uniform random order",
+            "blocks": args.blocks, "block_bytes": args.block_bytes, "batch": args.batch,
+            "l2": "inputs ~60 GB resident in HBM, >> 126 MB L2 (no flush needed)",
+            "copy_engine": {0: "tma", 1: "tma", 2: "lsu"}[args.copy_engine]}
+
+
+def batch_sweep(args, store, ptrs, sizes, prefix, out_buf, size):
+    """batch_put / batch_get GB/s at batch 64 / 256 / 1024 on an 8192-block
+    slice of the same stream."""
+    res = {}
+    n = min(8192, len(ptrs))
+    for b in (64, 256, 1024):
+        store.clear()
+        ps, gs, pb, gb = run_pass(store, ptrs[:n], sizes[:n], prefix[:n], b, out_buf, size, 7)
+        res[str(b)] = {"put_gbs": round(pb / ps / GB, 3), "get_gbs": round(gb / gs / GB, 3)}
+    store.clear()
+    return res
+
+
+def e2e_run(args, rank, world, device, store):
+    """Public API with pinned host buffers: H2D of every block and D2H of
+    every result inside the timed region."""
+    import torch
+    size = args.block_bytes
+    n = min(args.e2e_blocks, args.blocks)
+    from cascade_cpp import workloads as W
+    src, is_prefix = W.dedup_mix(n, 64, 0.25, 99 + rank)
+    uniq = np.unique(src)
+    host_u = torch.empty(len(uniq) * size, dtype=torch.uint8, pin_memory=True)
+    g = torch.Generator(device=device).manual_seed(5 + rank)
+    hv = host_u.view(torch.float16)
+    step = 256 * size // 2
+    for o in range(0, hv.numel(), step):
+        m = min(step, hv.numel() - o)
+        hv[o:o + m].copy_(torch.randn(m, generator=g, device=device, dtype=torch.float16))
+    pos = np.searchsorted(uniq, src)
+    ptrs = (np.uint64(host_u.data_ptr()) + pos.astype(np.uint64) * np.uint64(size)).astype(np.uint64)
+    sizes = np.full(n, size, np.uint64)
+    prefix = is_prefix.astype(np.uint8)
+    out = torch.empty(args.batch * size, dtype=torch.uint8, pin_memory=True)
+    store.clear()
+    run_pass(store, ptrs, sizes, prefix, args.batch, out, size, 1, device_memory=False)
+    times, pb, gb = [], 0, 0
+    for s in range(max(args.steps, 2)):
+        store.clear()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ps, gs, pb, gb = run_pass(store, ptrs, sizes, prefix, args.batch, out, size, 2 + s, device_memory=False)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    el = reduce_max(float(np.median(times)), world)
+    tot = reduce_sum(pb + gb, world)
+    store.clear()
+    return {"value": round(tot / el / GB, 3), "unit": "GB/s", "h2d_bytes_per_step": int(pb + 16 * len(uniq)),
+            "d2h_bytes_per_step": int(gb + 32 * n), "blocks": n,
+            "note": "pinned host buffers through batch_put/batch_get (put_ptrs/get_ptrs); bounded slice"}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,187 @@
+/*
+ * cascade_b200.h — C ABI of the B200-native Cascade block data path.
+ *
+ * One store per GPU per process. All array arguments are HOST arrays; the
+ * block pointers inside them (ptrs / outs) point to device memory
+ * (mem_kind = CB_MEM_DEVICE) or host memory (CB_MEM_HOST). Keys are the
+ * 16-byte binary form of the 32-hex BlockId (first 16 bytes of SHA-256).
+ * No function throws; every function returns a CB_* status and leaves a
+ * message for cb_last_error(). Calls on one store are serialised internally.
+ * `stream` is a cudaStream_t (NULL = the store's own stream); work is ordered
+ * after prior work on it and the call returns with its results final.
+ */
+#ifndef CASCADE_B200_H
+#define CASCADE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (reference returns bool: gpu_backend.cu:43-51) ------- */
+#define CB_OK 0
+#define CB_ERR_ARG 1      /* bad argument                                   */
+#define CB_ERR_CUDA 2     /* CUDA runtime error                             */
+#define CB_ERR_NOSPACE 3  /* HBM + DRAM tiers cannot hold the block         */
+#define CB_ERR_BUFSIZE 4  /* an output buffer is smaller than the block     */
+#define CB_ERR_TIMEOUT 5  /* a bounded device or collective wait ran out    */
+#define CB_ERR_NCCL 6     /* NCCL error                                     */
+#define CB_ERR_STATE 7    /* call not valid in the store's current state    */
+#define CB_ERR_DEVICE 8   /* a device-side check failed (bounds, index)     */
+
+/* ---- memory kind of the block pointers --------------------------------- */
+#define CB_MEM_DEVICE 0
+#define CB_MEM_HOST 1
+
+/* ---- put status per block ---------------------------------------------- */
+#define CB_PUT_STORED 0  /* new block stored                                */
+#define CB_PUT_DEDUP 1   /* key already stored (or earlier in the batch)    */
+#define CB_PUT_FAILED 2  /* no space in any tier                            */
+
+/* ---- get result code per block (low 4 bits = tier the block came from) - */
+#define CB_FOUND_MISS 0
+#define CB_FOUND_LOCAL_HBM 1
+#define CB_FOUND_LOCAL_DRAM 2
+#define CB_FOUND_REMOTE_HBM 3
+#define CB_FOUND_REMOTE_DRAM 4
+#define CB_FOUND_NOT_COPIED 0x80 /* found, but out_cap < size: nothing written */
+
+typedef struct cb_store cb_store;
+
+/* Mirrors DistributedConfig (include/cascade_distributed.hpp:186-213) and
+ * CascadeConfig (include/cascade.hpp:47-82) fields that apply to this path. */
+typedef struct cb_config {
+  uint64_t gpu_capacity_bytes;  /* HBM slab pool (gpu_capacity_per_device)  */
+  uint64_t dram_capacity_bytes; /* pinned DRAM arena (dram_capacity); 0=none */
+  int32_t device;               /* CUDA device ordinal                      */
+  int32_t dedup_enabled;        /* dedup_enabled                            */
+  int32_t semantic_eviction;    /* prefix-protected eviction                */
+  int32_t promote_on_hit;       /* move DRAM-tier hits back to HBM          */
+  int32_t index_log2;           /* initial device index slots = 2^index_log2 */
+  int32_t copy_engine;          /* 0 auto, 1 TMA bulk, 2 vector LSU         */
+  uint64_t staging_bytes;       /* device staging for host-memory callers   */
+  int32_t profile;              /* 1: time each kernel with CUDA events     */
+  int32_t hash_lanes;           /* SHA-256 chains per warp: 8, 16 or 32     */
+  uint64_t reserved[6];
+} cb_config;
+
+/* Mirrors DistributedStore::Stats (include/cascade_distributed.hpp:386-409). */
+typedef struct cb_stats {
+  uint64_t local_gpu_used, local_dram_used;
+  uint64_t cluster_gpu_used, cluster_dram_used;
+  uint64_t local_gpu_hits, local_dram_hits;
+  uint64_t remote_gpu_hits, remote_dram_hits;
+  uint64_t lustre_hits, misses;
+  uint64_t dedup_hits, dedup_bytes_saved;
+  uint64_t gpu_evictions, dram_evictions;
+  uint64_t prefix_blocks_protected, promotions_to_local;
+  uint64_t compression_savings;
+  uint64_t total_blocks, prefix_blocks;
+  /* B200 additions */
+  uint64_t evicted_bytes, promoted_bytes, dropped_blocks;
+  uint64_t kernel_launches; /* kernels this store launched                 */
+  /* per-kernel device time (cb_config.profile = 1): ns, bytes, launches     */
+  uint64_t sha_ns, sha_bytes, sha_launches;
+  uint64_t scatter_ns, scatter_bytes, scatter_launches;
+  uint64_t gather_ns, gather_bytes, gather_launches;
+  uint64_t tier_ns, tier_bytes, tier_launches;
+} cb_stats;
+
+/* Mirrors BlockLocation (include/cascade_distributed.hpp:62-80). */
+typedef struct cb_location {
+  int32_t node_id; /* owner rank                                            */
+  int32_t gpu_id;  /* device ordinal, -1 when the block is in the DRAM tier */
+  uint64_t offset; /* byte offset in the owner's HBM pool or DRAM arena     */
+  uint64_t size;
+  int32_t is_gpu;
+  int32_t is_prefix;
+} cb_location;
+
+/* Fills defaults (replaces the struct initialisers of DistributedConfig). */
+void cb_config_init(cb_config *cfg);
+
+/* Replaces DistributedStore::DistributedStore
+ * (src/distributed_backend.cpp:521-593) for one GPU of one rank. */
+int cb_create(const cb_config *cfg, cb_store **out);
+
+/* Replaces DistributedStore::~DistributedStore (src/distributed_backend.cpp:595). */
+int cb_destroy(cb_store *s);
+
+/* Message of the last failed call on this store (or of cb_create when s is
+ * NULL). Replaces the CUDA_CHECK fprintf of src/gpu_backend.cu:43-51. */
+const char *cb_last_error(const cb_store *s);
+
+/* Batched SHA-256 of n blocks on the GPU; digests_out = n*32 host bytes.
+ * Replaces n calls of compute_block_id (src/cascade_core.cpp:47-58) /
+ * python/bindings.cpp:176-179. */
+int cb_hash_batch(cb_store *s, const void *const *ptrs, const uint64_t *sizes, int32_t n,
+                  int32_t mem_kind, uint8_t *digests_out, void *stream);
+
+/* Batched put. keys_in = n*16 caller keys (NULL: hash every block on the GPU
+ * and use the digests). keys_out = n*16 (may be NULL), status_out = n
+ * CB_PUT_* (may be NULL). Dedup is sequential in batch order: a block is a
+ * dedup hit iff its key was stored before it.
+ * Replaces DistributedStore::put_batch (src/distributed_backend.cpp:813-841)
+ * and DistributedStore::put (src/distributed_backend.cpp:601-692). */
+int cb_put_batch(cb_store *s, const void *const *ptrs, const uint64_t *sizes,
+                 const uint8_t *is_prefix, const uint8_t *keys_in, int32_t n, int32_t mem_kind,
+                 uint8_t *keys_out, uint8_t *status_out, void *stream);
+
+/* Batched get into caller buffers outs[i] of out_caps[i] bytes.
+ * sizes_out[i] = block size when found; found_out[i] = CB_FOUND_* code.
+ * Replaces DistributedStore::get_batch (src/distributed_backend.cpp:844-870)
+ * and DistributedStore::get (src/distributed_backend.cpp:698-795). */
+int cb_get_batch(cb_store *s, const uint8_t *keys, int32_t n, void *const *outs,
+                 const uint64_t *out_caps, int32_t mem_kind, uint64_t *sizes_out,
+                 uint8_t *found_out, void *stream);
+
+/* found_out[i] = 1 when key i is stored in any tier.
+ * Replaces DistributedStore::contains (src/distributed_backend.cpp:797-802). */
+int cb_contains_batch(cb_store *s, const uint8_t *keys, int32_t n, uint8_t *found_out);
+
+/* Replaces DistributedStore::locate (src/distributed_backend.cpp:804-806). */
+int cb_locate(cb_store *s, const uint8_t *key, cb_location *out, int32_t *found);
+
+/* Demote least-recently-used HBM blocks (prefix blocks last) to the DRAM
+ * tier until `bytes` are free. Replaces DistributedStore::evict_gpu_to_dram
+ * (src/distributed_backend.cpp:876-941). */
+int cb_evict(cb_store *s, uint64_t bytes, uint64_t *evicted_bytes);
+
+/* Replaces DistributedStore::get_stats (src/distributed_backend.cpp:1384-1427). */
+int cb_get_stats(cb_store *s, cb_stats *out);
+
+/* Replaces DistributedStore::clear (src/distributed_backend.cpp:1452-1477). */
+int cb_clear(cb_store *s);
+
+/* Waits for all work of the store. Replaces GPUBackend::sync_all
+ * (src/gpu_backend.cu:556-562). */
+int cb_sync(cb_store *s);
+
+/* ---- multi-GPU DHT (replaces DistributedGPUBackend's MPI RMA tier,
+ *      src/distributed_backend.cpp:303-514, and the metadata replication of
+ *      sync_metadata, :1323-1382) ------------------------------------------ */
+
+/* Size of the opaque NCCL unique id blob. */
+#define CB_UID_BYTES 128
+
+/* Rank 0 creates the unique id; every rank passes the same blob. */
+int cb_dht_unique_id(uint8_t uid_out[CB_UID_BYTES]);
+
+/* Joins the DHT: NCCL communicator over `world` ranks, one GPU each; the HBM
+ * pools are exported with CUDA IPC and mapped into every peer. Collective. */
+int cb_dht_attach(cb_store *s, int32_t rank, int32_t world, const uint8_t uid[CB_UID_BYTES]);
+
+/* Collective barrier over the DHT (ncclAllReduce of one word).
+ * Replaces DistributedStore::barrier (src/distributed_backend.cpp:1310-1314). */
+int cb_dht_barrier(cb_store *s);
+
+/* Rank and world size (1-GPU stores: 0 and 1). */
+int cb_rank(const cb_store *s, int32_t *rank, int32_t *world);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CASCADE_B200_H */

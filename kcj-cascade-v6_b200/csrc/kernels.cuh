@@ -1,0 +1,54 @@
+// Launchers of the sm_100a kernels of the block data path.
+#pragma once
+
+#include "common.cuh"
+
+namespace cb {
+
+struct HashJob {
+  uint64_t ptr;   // device (or mapped host) address of the block
+  uint64_t size;  // bytes
+};
+
+// sha256.cu — digests: n * 8 words holding the 32 digest bytes in order.
+cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
+                                cudaStream_t stream);
+
+// copy.cu — batched copies. Descriptor i covers units
+// [unit_start[i], unit_start[i+1]) of kCopyUnit bytes each; a unit past the
+// descriptor's size is skipped. engine: 1 = TMA bulk (device memory only),
+// 2 = vector LSU. Descriptors with flags bit 0 (host memory) always take the
+// LSU path.
+cudaError_t launch_batch_copy(const CopyDesc *d_desc, const uint32_t *d_unit_start, int n,
+                              uint32_t total_units, int engine, unsigned *d_err, int num_sms,
+                              cudaStream_t stream);
+
+// index.cu — device index mutations and lookups.
+cudaError_t launch_index_insert(Slot *table, uint64_t mask, const IndexRec *recs, int n,
+                                unsigned *d_err, cudaStream_t stream);
+cudaError_t launch_index_update(Slot *table, uint64_t mask, const IndexRec *recs, int n,
+                                unsigned *d_err, cudaStream_t stream);
+cudaError_t launch_index_erase(Slot *table, uint64_t mask, const IndexRec *recs, int n,
+                               unsigned *d_err, cudaStream_t stream);
+
+// Lookup for gets: for each key resolves the source address in the HBM pool
+// (pool_base) or DRAM arena (dram_base), checks it against the arena sizes
+// and out_caps, and fills desc (size 0 when nothing is to be copied) and res.
+struct LookupArgs {
+  const Slot *table;
+  uint64_t mask;
+  const Key *keys;
+  const uint64_t *outs;
+  const uint64_t *caps;
+  const uint32_t *unit_start;  // copy units the host reserved per request
+  int n;
+  uint64_t pool_base, pool_bytes;
+  uint64_t dram_base, dram_bytes;
+  uint32_t code_hbm, code_dram;  // CB_FOUND_* codes to report per tier
+  CopyDesc *desc;
+  GetResult *res;
+  unsigned *err;
+};
+cudaError_t launch_index_lookup(const LookupArgs &a, cudaStream_t stream);
+
+}  // namespace cb

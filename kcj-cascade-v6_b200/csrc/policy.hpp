@@ -1,0 +1,177 @@
+// Host-side placement policy of the B200 store: extent allocators for the HBM
+// slab pool and the pinned DRAM arena, the authoritative block metadata, LRU
+// order, sequential dedup, and prefix-protected eviction / promotion planning.
+//
+// It never touches device memory: it only decides. The store turns its plans
+// into batched kernels (scatter, tier moves, index updates). Keeping it free of
+// CUDA lets the CPU test-suite drive it directly.
+//
+// Reference behaviour restated here:
+//   * dedup: DistributedStore::put / put_batch (src/distributed_backend.cpp:
+//     601-608, 813-841) - a block is a hit iff its key was stored earlier in
+//     stream order (including earlier in the same batch);
+//   * pool allocation: GPUMemoryPool::alloc/free (src/gpu_backend.cu:81-160)
+//     and DistributedDRAMBackend::allocate/deallocate
+//     (src/distributed_backend.cpp:88-158) - best fit with coalescing;
+//     here O(log n) with ordered maps instead of an O(n) list scan;
+//   * eviction: GPUBackend::evict_lru_semantic / evict_for_space
+//     (src/gpu_backend.cu:482-537) - never a prefix block while a non-prefix
+//     block is evictable, fall back to prefix blocks when nothing else is left;
+//     victims go to the DRAM tier (DistributedStore::evict_gpu_to_dram,
+//     src/distributed_backend.cpp:876-941);
+//   * DRAM eviction: DistributedDRAMBackend::evict_for_space
+//     (src/distributed_backend.cpp:240-284) - LRU, prefix blocks skipped, no
+//     fallback; with no Lustre tier an evicted DRAM block is dropped.
+// Victim order is exact LRU (the reference approximates it per shard,
+// src/cascade_core.cpp:160-221); order is not a parity target, the
+// protection rule is.
+#pragma once
+
+#include <stdint.h>
+
+#include <list>
+#include <map>
+#include <set>
+#include <unordered_map>
+#include <utility>
+#include <vector>
+
+namespace cb {
+
+struct HKey {
+  uint64_t lo, hi;
+  bool operator==(const HKey &o) const { return lo == o.lo && hi == o.hi; }
+};
+struct HKeyHash {
+  size_t operator()(const HKey &k) const { return (size_t)(k.hi ^ (k.lo * 0x9E3779B97F4A7C15ull)); }
+};
+
+// Best-fit extent allocator with coalescing (granule-aligned).
+class ExtentAllocator {
+ public:
+  ExtentAllocator() = default;
+  ExtentAllocator(uint64_t capacity, uint64_t granule) { reset(capacity, granule); }
+  void reset(uint64_t capacity, uint64_t granule);
+  // Returns the offset, or UINT64_MAX when no extent fits.
+  uint64_t alloc(uint64_t size);
+  void free(uint64_t off, uint64_t size);
+  uint64_t rounded(uint64_t size) const { return (size + granule_ - 1) / granule_ * granule_; }
+  uint64_t capacity() const { return capacity_; }
+  uint64_t free_bytes() const { return free_bytes_; }
+  uint64_t largest_free() const;
+  size_t num_extents() const { return by_off_.size(); }
+
+ private:
+  uint64_t capacity_ = 0, granule_ = 256, free_bytes_ = 0;
+  std::map<uint64_t, uint64_t> by_off_;          // offset -> size
+  std::set<std::pair<uint64_t, uint64_t>> by_sz_; // (size, offset)
+  void insert_extent(uint64_t off, uint64_t size);
+  void erase_extent(uint64_t off, uint64_t size);
+};
+
+enum : uint8_t { kTierHbm = 0, kTierDram = 1 };
+
+struct BlockMeta {
+  uint64_t off = 0;
+  uint64_t size = 0;
+  uint8_t tier = kTierHbm;
+  uint8_t prefix = 0;
+  uint8_t pending = 0;  // placed by the batch being planned; not evictable yet
+  uint64_t stamp = 0;   // recency (larger = more recent)
+  std::list<HKey>::iterator lru;
+};
+
+// A tier move the store executes: copy `size` bytes from (src_tier, src_off)
+// to (dst_tier, dst_off). Moves of one plan run in vector order.
+struct TierMove {
+  HKey key;
+  uint8_t src_tier, dst_tier;
+  uint64_t src_off, dst_off, size;
+};
+
+struct Placement {
+  int32_t idx;  // batch index
+  HKey key;
+  uint64_t off;  // offset in the tier's arena
+  uint64_t size;
+  uint8_t prefix;
+  uint8_t tier;  // kTierHbm normally; kTierDram when larger than the HBM pool
+};
+
+struct PutPlan {
+  std::vector<uint8_t> status;      // per item: 0 stored, 1 dedup, 2 failed
+  std::vector<Placement> places;    // new blocks to scatter into HBM
+  std::vector<TierMove> moves;      // demotions to run BEFORE the scatter
+  std::vector<HKey> dropped;        // blocks dropped from the store (index erase)
+  void clear() {
+    status.clear();
+    places.clear();
+    moves.clear();
+    dropped.clear();
+  }
+};
+
+struct PolicyCounters {
+  uint64_t dedup_hits = 0, dedup_bytes_saved = 0;
+  uint64_t gpu_evictions = 0, dram_evictions = 0;
+  uint64_t evicted_bytes = 0, promoted_bytes = 0, promotions = 0;
+  uint64_t dropped_blocks = 0, prefix_blocks = 0;
+};
+
+class Policy {
+ public:
+  Policy(uint64_t hbm_capacity, uint64_t dram_capacity, bool semantic_eviction,
+         uint64_t granule = 256);
+
+  // Sequential dedup + placement of a batch (see file comment). Placements
+  // stay pending until commit(); they are never chosen as victims inside the
+  // batch that placed them.
+  void plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *prefix, int n,
+                bool dedup_enabled, PutPlan &plan);
+  void commit();
+
+  // Bring a DRAM-tier block back to HBM (may demote others first).
+  // Appends the promotion move last. Returns false when it cannot fit.
+  bool plan_promote(const HKey &k, std::vector<TierMove> &moves, std::vector<HKey> &dropped);
+
+  // Demote HBM blocks until `bytes` of HBM are free (cb_evict).
+  uint64_t plan_evict(uint64_t bytes, std::vector<TierMove> &moves, std::vector<HKey> &dropped);
+
+  const BlockMeta *find(const HKey &k) const;
+  void touch(const HKey &k);  // mark most recently used
+  void clear();
+
+  uint64_t hbm_used() const { return hbm_used_; }
+  uint64_t dram_used() const { return dram_used_; }
+  uint64_t hbm_capacity() const { return hbm_cap_; }
+  uint64_t dram_capacity() const { return dram_cap_; }
+  size_t size() const { return map_.size(); }
+  const PolicyCounters &counters() const { return ctr_; }
+  void reset_counters() { ctr_ = PolicyCounters{}; }
+  const ExtentAllocator &hbm_alloc() const { return hbm_; }
+  template <class F>
+  void for_each(F f) const {
+    for (const auto &kv : map_) f(kv.first, kv.second);
+  }
+
+ private:
+  bool make_hbm_room(uint64_t size, std::vector<TierMove> &moves, std::vector<HKey> &dropped);
+  bool make_dram_room(uint64_t size, std::vector<HKey> &dropped);
+  bool demote_one(std::vector<TierMove> &moves, std::vector<HKey> &dropped);
+  bool pick_victim(uint8_t tier, bool prefix_fallback, HKey &out) const;
+  void drop(const HKey &k, std::vector<HKey> &dropped);
+
+  uint64_t hbm_cap_, dram_cap_;
+  bool semantic_;
+  ExtentAllocator hbm_, dram_;
+  uint64_t hbm_used_ = 0, dram_used_ = 0;  // logical bytes (reference used_)
+  std::unordered_map<HKey, BlockMeta, HKeyHash> map_;
+  // LRU lists, front = most recent: [tier][prefix]
+  std::list<HKey> lru_[2][2];
+  std::vector<HKey> pending_;
+  std::vector<std::pair<uint64_t, uint64_t>> deferred_free_;  // DRAM extents freed at commit
+  uint64_t clock_ = 0;
+  PolicyCounters ctr_;
+};
+
+}  // namespace cb

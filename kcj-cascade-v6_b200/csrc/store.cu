@@ -1,0 +1,888 @@
+// The B200 store behind the C ABI: one HBM slab pool + device index per GPU,
+// an optional pinned DRAM arena, and the host policy. Every batch becomes a
+// handful of launches: SHA-256 -> (host dedup/placement plan) -> tier moves ->
+// scatter -> index mutations for put; index lookup -> gather for get.
+//
+// Reference call stacks this replaces:
+//   put  : DistributedStore::put (src/distributed_backend.cpp:601-692) ->
+//          DistributedGPUBackend::put_local (:412-436) -> GPUBackend::put
+//          (src/gpu_backend.cu:300-351, one cudaMemcpyAsync per block)
+//   get  : DistributedStore::get (:698-795) -> get_local scans every GPU
+//          (:455-464) -> read_block_to_host (src/gpu_backend.cu:390-425)
+//   evict: DistributedStore::evict_gpu_to_dram (:876-941) ->
+//          GPUBackend::evict_for_space (src/gpu_backend.cu:514-537)
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "cascade_b200.h"
+#include "kernels.cuh"
+#include "policy.hpp"
+#include "store.hpp"
+
+namespace cb {
+
+thread_local std::string g_create_error;
+
+namespace {
+
+inline void from_hkey(const HKey &k, uint8_t *p) {
+  memcpy(p, &k.lo, 8);
+  memcpy(p + 8, &k.hi, 8);
+}
+
+inline uint64_t meta_word(uint64_t size, uint8_t prefix) {
+  return (size & kSizeMask) | (prefix ? kMetaPrefix : 0);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ buffers
+
+cudaError_t PinnedBuf::ensure(size_t bytes) {
+  if (bytes <= cap) return cudaSuccess;
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  cap = 0;
+  const size_t want = std::max<size_t>(align_up(bytes + bytes / 2, 4096), 1 << 20);
+  cudaError_t e = cudaHostAlloc(&ptr, want, cudaHostAllocPortable);
+  if (e == cudaSuccess) cap = want;
+  return e;
+}
+void PinnedBuf::release() {
+  if (ptr) cudaFreeHost(ptr);
+  ptr = nullptr;
+  cap = 0;
+}
+
+cudaError_t DevBuf::ensure(size_t bytes) {
+  if (bytes <= cap) return cudaSuccess;
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  cap = 0;
+  const size_t want = std::max<size_t>(align_up(bytes + bytes / 2, 4096), 1 << 20);
+  cudaError_t e = cudaMalloc(&ptr, want);
+  if (e == cudaSuccess) cap = want;
+  return e;
+}
+void DevBuf::release() {
+  if (ptr) cudaFree(ptr);
+  ptr = nullptr;
+  cap = 0;
+}
+
+// ------------------------------------------------------------ store
+
+int Store::fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  last_error = buf;
+  return code;
+}
+
+int Store::cuda_fail(cudaError_t e, const char *what) {
+  return fail(CB_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CB_TRY(call, what)                     \
+  do {                                         \
+    cudaError_t _e = (call);                   \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+Store::Store(const cb_config &c)
+    : cfg(c), policy(c.gpu_capacity_bytes, c.dram_capacity_bytes, c.semantic_eviction != 0) {}
+
+int Store::init() {
+  device = cfg.device;
+  int ndev = 0;
+  CB_TRY(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev) return fail(CB_ERR_ARG, "device %d out of range (%d)", device, ndev);
+  CB_TRY(cudaSetDevice(device), "cudaSetDevice");
+  CB_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device), "sm count");
+  CB_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking), "stream");
+  pool_bytes = policy.hbm_capacity() / 256 * 256;
+  if (pool_bytes) CB_TRY(cudaMalloc(&pool, pool_bytes), "HBM pool cudaMalloc");
+  CB_TRY(cudaMalloc(&d_err, sizeof(unsigned)), "error word");
+  CB_TRY(cudaMemset(d_err, 0, sizeof(unsigned)), "error word");
+  const int log2 = cfg.index_log2 > 0 ? cfg.index_log2 : 16;
+  CB_TRY(alloc_table((uint64_t)1 << log2), "index");
+  CB_TRY(h_err.ensure(64), "pinned");
+  profile = cfg.profile != 0;
+  hash_lanes = (cfg.hash_lanes == 8 || cfg.hash_lanes == 16) ? cfg.hash_lanes : 32;
+  CB_TRY(cudaEventCreate(&ev_a), "event");
+  CB_TRY(cudaEventCreate(&ev_b), "event");
+  return CB_OK;
+}
+
+Store::~Store() {
+  if (device >= 0) cudaSetDevice(device);
+  if (own_stream) cudaStreamSynchronize(own_stream);
+  dht_detach();
+  if (pool) cudaFree(pool);
+  if (table) cudaFree(table);
+  if (d_err) cudaFree(d_err);
+  if (dram_host) cudaFreeHost(dram_host);
+  d_scratch.release();
+  h_scratch.release();
+  h_out.release();
+  h_err.release();
+  d_staging.release();
+  if (ev_a) cudaEventDestroy(ev_a);
+  if (ev_b) cudaEventDestroy(ev_b);
+  if (own_stream) cudaStreamDestroy(own_stream);
+}
+
+cudaError_t Store::alloc_table(uint64_t slots) {
+  if (table) cudaFree(table);
+  table = nullptr;
+  cudaError_t e = cudaMalloc(&table, slots * sizeof(Slot));
+  if (e != cudaSuccess) return e;
+  table_slots = slots;
+  table_used = 0;
+  table_tombs = 0;
+  return cudaMemset(table, 0, slots * sizeof(Slot));
+}
+
+cudaError_t Store::ensure_dram() {
+  if (dram_host || policy.dram_capacity() == 0) return cudaSuccess;
+  dram_bytes = policy.dram_capacity() / 256 * 256;
+  cudaError_t e = cudaHostAlloc(reinterpret_cast<void **>(&dram_host), dram_bytes,
+                                cudaHostAllocMapped | cudaHostAllocPortable);
+  if (e != cudaSuccess) {
+    dram_host = nullptr;
+    return e;
+  }
+  return cudaHostGetDevicePointer(reinterpret_cast<void **>(&dram_dev), dram_host, 0);
+}
+
+// Grows (or compacts) the device index so that `incoming` more keys keep
+// the load factor at or below 1/2, rebuilding it from the host metadata.
+int Store::reserve_index(uint64_t incoming, cudaStream_t st) {
+  const uint64_t live = policy.size();
+  if ((table_used + table_tombs + incoming) * 2 <= table_slots) return CB_OK;
+  uint64_t slots = table_slots;
+  while ((live + incoming) * 2 > slots) slots *= 2;
+  CB_TRY(cudaStreamSynchronize(st), "sync before index rebuild");
+  CB_TRY(alloc_table(slots), "index rebuild alloc");
+  if (live == 0) return CB_OK;
+  std::vector<IndexRec> recs;
+  recs.reserve(live);
+  policy.for_each([&](const HKey &k, const BlockMeta &m) {
+    recs.push_back(IndexRec{k.lo, k.hi, m.off | (m.tier == kTierDram ? kLocDram : 0),
+                            meta_word(m.size, m.prefix)});
+  });
+  const size_t bytes = recs.size() * sizeof(IndexRec);
+  CB_TRY(h_scratch.ensure(bytes), "pinned scratch");
+  CB_TRY(d_scratch.ensure(bytes), "device scratch");
+  memcpy(h_scratch.ptr, recs.data(), bytes);
+  CB_TRY(cudaMemcpyAsync(d_scratch.ptr, h_scratch.ptr, bytes, cudaMemcpyHostToDevice, st), "H2D");
+  CB_TRY(launch_index_insert(table, table_slots - 1, static_cast<IndexRec *>(d_scratch.ptr),
+                             (int)recs.size(), d_err, st),
+         "index insert");
+  launches++;
+  CB_TRY(cudaStreamSynchronize(st), "index rebuild");
+  table_used = live;
+  return CB_OK;
+}
+
+// Reads and clears the device error word (after a stream sync).
+int Store::check_device_error(cudaStream_t st) {
+  CB_TRY(cudaMemcpyAsync(h_err.ptr, d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "D2H err");
+  CB_TRY(cudaStreamSynchronize(st), "stream sync");
+  const unsigned e = *static_cast<unsigned *>(h_err.ptr);
+  if (!e) return CB_OK;
+  CB_TRY(cudaMemsetAsync(d_err, 0, sizeof(unsigned), st), "clear err");
+  CB_TRY(cudaStreamSynchronize(st), "stream sync");
+  if (e & kErrTimeout) return fail(CB_ERR_TIMEOUT, "device wait timed out (error bits 0x%x)", e);
+  return fail(CB_ERR_DEVICE, "device-side check failed (error bits 0x%x)", e);
+}
+
+// ------------------------------------------------------------ packing
+
+// Lays out several device arrays in one pinned buffer so each call needs one
+// H2D copy; offsets are 256-byte aligned.
+struct Layout {
+  size_t off = 0;
+  size_t add(size_t bytes) {
+    off = align_up(off, 256);
+    const size_t o = off;
+    off += bytes;
+    return o;
+  }
+};
+
+// Copy descriptors + unit prefix for a list of (src, dst, size, flags).
+static uint32_t units_of(uint64_t size) {
+  return (uint32_t)((size + kCopyUnit - 1) / kCopyUnit);
+}
+
+// Executes tier moves (HBM->DRAM first, then DRAM->HBM), index updates for
+// moved blocks and index erases for dropped blocks, stream-ordered on st.
+int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped,
+                     cudaStream_t st) {
+  if (moves.empty() && dropped.empty()) return CB_OK;
+  bool need_dram = false;
+  for (const auto &m : moves) need_dram |= (m.src_tier == kTierDram || m.dst_tier == kTierDram);
+  if (need_dram) {
+    cudaError_t e = ensure_dram();
+    if (e != cudaSuccess) return cuda_fail(e, "pinned DRAM arena cudaHostAlloc");
+  }
+  std::vector<const TierMove *> wave[2];
+  for (const auto &m : moves) wave[m.dst_tier == kTierDram ? 0 : 1].push_back(&m);
+  const int nm = (int)moves.size(), nd = (int)dropped.size();
+  Layout L;
+  const size_t o_desc = L.add(sizeof(CopyDesc) * nm);
+  const size_t o_us0 = L.add(sizeof(uint32_t) * (wave[0].size() + 1));
+  const size_t o_us1 = L.add(sizeof(uint32_t) * (wave[1].size() + 1));
+  const size_t o_upd = L.add(sizeof(IndexRec) * nm);
+  const size_t o_era = L.add(sizeof(IndexRec) * nd);
+  CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
+  CB_TRY(d_scratch.ensure(L.off), "device scratch");
+  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
+  uint32_t *us[2] = {reinterpret_cast<uint32_t *>(h + o_us0), reinterpret_cast<uint32_t *>(h + o_us1)};
+  IndexRec *upd = reinterpret_cast<IndexRec *>(h + o_upd);
+  IndexRec *era = reinterpret_cast<IndexRec *>(h + o_era);
+  uint32_t total[2] = {0, 0};
+  uint64_t wave_bytes[2] = {0, 0};
+  int di = 0;
+  for (int w = 0; w < 2; ++w) {
+    for (size_t j = 0; j < wave[w].size(); ++j) {
+      const TierMove &m = *wave[w][j];
+      const uint64_t src = m.src_tier == kTierDram ? (uint64_t)dram_dev + m.src_off : (uint64_t)pool + m.src_off;
+      const uint64_t dst = m.dst_tier == kTierDram ? (uint64_t)dram_dev + m.dst_off : (uint64_t)pool + m.dst_off;
+      desc[di + j] = CopyDesc{src, dst, m.size, 1};
+      us[w][j] = total[w];
+      total[w] += units_of(m.size);
+      wave_bytes[w] += m.size;
+      const BlockMeta *bm = policy.find(m.key);
+      upd[di + j] = IndexRec{m.key.lo, m.key.hi, m.dst_off | (m.dst_tier == kTierDram ? kLocDram : 0),
+                             meta_word(m.size, bm ? bm->prefix : 0)};
+    }
+    us[w][wave[w].size()] = total[w];
+    di += (int)wave[w].size();
+  }
+  for (int j = 0; j < nd; ++j) era[j] = IndexRec{dropped[j].lo, dropped[j].hi, 0, 0};
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D moves");
+  const CopyDesc *ddesc = reinterpret_cast<const CopyDesc *>(d + o_desc);
+  for (int w = 0; w < 2; ++w) {
+    if (wave[w].empty()) continue;
+    const CopyDesc *wd = ddesc + (w ? wave[0].size() : 0);
+    const uint32_t *wu = reinterpret_cast<const uint32_t *>(d + (w ? o_us1 : o_us0));
+    const int wn = (int)wave[w].size();
+    CB_TRY(timed(3, wave_bytes[w], st,
+                 [&] { return launch_batch_copy(wd, wu, wn, total[w], 2, d_err, num_sms, st); }),
+           w ? "promote copy" : "demote copy");
+  }
+  if (nm) {
+    CB_TRY(launch_index_update(table, table_slots - 1, reinterpret_cast<const IndexRec *>(d + o_upd), nm,
+                               d_err, st),
+           "index update");
+    launches++;
+  }
+  if (nd) {
+    CB_TRY(launch_index_erase(table, table_slots - 1, reinterpret_cast<const IndexRec *>(d + o_era), nd,
+                              d_err, st),
+           "index erase");
+    launches++;
+  }
+  table_tombs += nd;
+  table_used -= std::min<uint64_t>(table_used, nd);
+  // The scratch buffers are reused by the next phase: wait for the copies
+  // of this phase's descriptors to be consumed.
+  CB_TRY(cudaStreamSynchronize(st), "moves");
+  return CB_OK;
+}
+
+// SHA-256 of device-resident blocks; digests (n*32 B) land in h_out.
+int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st) {
+  Layout L;
+  const size_t o_jobs = L.add(sizeof(HashJob) * n);
+  const size_t o_dig = L.add(32ull * n);
+  CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
+  CB_TRY(d_scratch.ensure(L.off), "device scratch");
+  CB_TRY(h_out.ensure(32ull * n), "pinned out");
+  HashJob *jobs = reinterpret_cast<HashJob *>(static_cast<uint8_t *>(h_scratch.ptr) + o_jobs);
+  uint64_t total = 0;
+  for (int i = 0; i < n; ++i) {
+    jobs[i] = HashJob{ptrs[i], sizes[i]};
+    total += sizes[i];
+  }
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  CB_TRY(cudaMemcpyAsync(d + o_jobs, jobs, sizeof(HashJob) * n, cudaMemcpyHostToDevice, st), "H2D jobs");
+  CB_TRY(timed(0, total, st,
+               [&] {
+                 return launch_sha256_batch(reinterpret_cast<const HashJob *>(d + o_jobs), n,
+                                            reinterpret_cast<uint32_t *>(d + o_dig), hash_lanes, st);
+               }),
+         "sha256 launch");
+  CB_TRY(cudaMemcpyAsync(h_out.ptr, d + o_dig, 32ull * n, cudaMemcpyDeviceToHost, st), "D2H digests");
+  CB_TRY(cudaStreamSynchronize(st), "sha256");
+  return CB_OK;
+}
+
+// ---------------------------------------------------------------- put
+
+int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                      const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
+                      cudaStream_t st) {
+  std::vector<HKey> keys(n);
+  if (keys_in) {
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(keys_in + 16 * i);
+  } else {
+    int rc = hash_device(ptrs, sizes, n, st);
+    if (rc) return rc;
+    const uint8_t *dig = static_cast<const uint8_t *>(h_out.ptr);
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32 * i);
+  }
+  int rc = reserve_index((uint64_t)n, st);
+  if (rc) return rc;
+  PutPlan &plan = put_plan;
+  policy.plan_put(keys.data(), sizes, is_prefix, n, cfg.dedup_enabled != 0, plan);
+  rc = run_moves(plan.moves, plan.dropped, st);
+  if (rc) return rc;
+
+  const int np = (int)plan.places.size();
+  if (np) {
+    bool need_dram = false;
+    for (const auto &p : plan.places) need_dram |= p.tier == kTierDram;
+    if (need_dram) {
+      cudaError_t e = ensure_dram();
+      if (e != cudaSuccess) return cuda_fail(e, "pinned DRAM arena cudaHostAlloc");
+    }
+    Layout L;
+    const size_t o_desc = L.add(sizeof(CopyDesc) * np);
+    const size_t o_us = L.add(sizeof(uint32_t) * (np + 1));
+    const size_t o_ins = L.add(sizeof(IndexRec) * np);
+    CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
+    CB_TRY(d_scratch.ensure(L.off), "device scratch");
+    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
+    uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
+    IndexRec *ins = reinterpret_cast<IndexRec *>(h + o_ins);
+    uint32_t total = 0;
+    uint64_t bytes = 0;
+    for (int j = 0; j < np; ++j) {
+      const Placement &p = plan.places[j];
+      bytes += p.size;
+      const bool dram = p.tier == kTierDram;
+      const uint64_t dst = dram ? (uint64_t)dram_dev + p.off : (uint64_t)pool + p.off;
+      desc[j] = CopyDesc{ptrs[p.idx], dst, p.size, dram ? 1u : 0u};
+      us[j] = total;
+      total += units_of(p.size);
+      ins[j] = IndexRec{p.key.lo, p.key.hi, p.off | (dram ? kLocDram : 0), meta_word(p.size, p.prefix)};
+    }
+    us[np] = total;
+    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D scatter");
+    CB_TRY(timed(1, bytes, st,
+                 [&] {
+                   return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_desc),
+                                            reinterpret_cast<const uint32_t *>(d + o_us), np, total,
+                                            copy_engine, d_err, num_sms, st);
+                 }),
+           "scatter");
+    CB_TRY(launch_index_insert(table, table_slots - 1, reinterpret_cast<const IndexRec *>(d + o_ins), np,
+                               d_err, st),
+           "index insert");
+    launches++;
+    table_used += np;
+  }
+  rc = check_device_error(st);  // also the final sync of the batch
+  policy.commit();
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) {
+    if (keys_out) from_hkey(keys[i], keys_out + 16 * i);
+    if (status_out) status_out[i] = plan.status[i];
+  }
+  return CB_OK;
+}
+
+// Host-memory blocks: copied into device staging in slices that fit it, each
+// slice then takes the device path (sequential dedup is preserved because
+// slices are processed in batch order).
+int Store::put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                    const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
+                    cudaStream_t st) {
+  const uint64_t cap = staging_capacity();
+  int i = 0;
+  std::vector<uint64_t> dptrs;
+  while (i < n) {
+    uint64_t bytes = 0;
+    int j = i;
+    while (j < n && (j == i || bytes + align_up(sizes[j], 256) <= cap)) bytes += align_up(sizes[j++], 256);
+    CB_TRY(d_staging.ensure(bytes), "device staging");
+    dptrs.resize(j - i);
+    uint64_t off = 0;
+    for (int k = i; k < j; ++k) {
+      dptrs[k - i] = (uint64_t)d_staging.ptr + off;
+      off += align_up(sizes[k], 256);
+    }
+    // Coalesce host-contiguous runs into single DMA copies.
+    int k = i;
+    while (k < j) {
+      int e = k + 1;
+      uint64_t run = sizes[k];
+      while (e < j && static_cast<const uint8_t *>(ptrs[k]) + (dptrs[e - i] - dptrs[k - i]) == ptrs[e] &&
+             dptrs[e - i] - dptrs[e - 1 - i] == sizes[e - 1]) {
+        run = dptrs[e - i] - dptrs[k - i] + sizes[e];
+        ++e;
+      }
+      if (run) CB_TRY(cudaMemcpyAsync(reinterpret_cast<void *>(dptrs[k - i]), ptrs[k], run,
+                                      cudaMemcpyHostToDevice, st),
+                      "H2D block");
+      k = e;
+    }
+    int rc = put_device(dptrs.data(), sizes + i, is_prefix ? is_prefix + i : nullptr,
+                        keys_in ? keys_in + 16 * i : nullptr, j - i, keys_out ? keys_out + 16 * i : nullptr,
+                        status_out ? status_out + i : nullptr, st);
+    if (rc) return rc;
+    i = j;
+  }
+  return CB_OK;
+}
+
+// ---------------------------------------------------------------- get
+
+int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const uint64_t *caps,
+                      uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
+  Layout L;
+  const size_t o_keys = L.add(16ull * n);
+  const size_t o_outs = L.add(8ull * n);
+  const size_t o_caps = L.add(8ull * n);
+  const size_t o_us = L.add(4ull * (n + 1));
+  const size_t o_desc = L.add(sizeof(CopyDesc) * n);
+  const size_t o_res = L.add(sizeof(GetResult) * n);
+  CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
+  CB_TRY(d_scratch.ensure(L.off), "device scratch");
+  CB_TRY(h_out.ensure(sizeof(GetResult) * n), "pinned out");
+  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  memcpy(h + o_keys, keys, 16ull * n);
+  memcpy(h + o_outs, outs, 8ull * n);
+  memcpy(h + o_caps, caps, 8ull * n);
+  uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
+  uint32_t total = 0;
+  uint64_t bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    us[i] = total;
+    const BlockMeta *m = policy.find(to_hkey(keys + 16 * i));
+    if (m && m->size <= caps[i]) {
+      total += units_of(m->size);
+      bytes += m->size;
+    }
+  }
+  us[n] = total;
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  CB_TRY(cudaMemcpyAsync(d, h, o_desc, cudaMemcpyHostToDevice, st), "H2D get");
+  LookupArgs a;
+  a.table = table;
+  a.mask = table_slots - 1;
+  a.keys = reinterpret_cast<const Key *>(d + o_keys);
+  a.outs = reinterpret_cast<const uint64_t *>(d + o_outs);
+  a.caps = reinterpret_cast<const uint64_t *>(d + o_caps);
+  a.unit_start = reinterpret_cast<const uint32_t *>(d + o_us);
+  a.n = n;
+  a.pool_base = (uint64_t)pool;
+  a.pool_bytes = pool_bytes;
+  a.dram_base = (uint64_t)dram_dev;
+  a.dram_bytes = dram_host ? dram_bytes : 0;
+  a.code_hbm = CB_FOUND_LOCAL_HBM;
+  a.code_dram = CB_FOUND_LOCAL_DRAM;
+  a.desc = reinterpret_cast<CopyDesc *>(d + o_desc);
+  a.res = reinterpret_cast<GetResult *>(d + o_res);
+  a.err = d_err;
+  CB_TRY(launch_index_lookup(a, st), "index lookup");
+  launches++;
+  if (total) {
+    CB_TRY(timed(2, bytes, st,
+                 [&] { return launch_batch_copy(a.desc, a.unit_start, n, total, copy_engine, d_err, num_sms, st); }),
+           "gather");
+  }
+  CB_TRY(cudaMemcpyAsync(h_out.ptr, d + o_res, sizeof(GetResult) * n, cudaMemcpyDeviceToHost, st),
+         "D2H results");
+  // LRU touches overlap the device work (CascadeStore::get touches on hit,
+  // src/cascade_core.cpp:1281).
+  for (int i = 0; i < n; ++i) policy.touch(to_hkey(keys + 16 * i));
+  int rc = check_device_error(st);
+  if (rc) return rc;
+  const GetResult *res = static_cast<const GetResult *>(h_out.ptr);
+  std::vector<HKey> promote;
+  for (int i = 0; i < n; ++i) {
+    sizes_out[i] = res[i].size;
+    found_out[i] = (uint8_t)res[i].code;
+    const uint32_t tier = res[i].code & 0x0f;
+    if (tier == CB_FOUND_MISS) {
+      misses++;
+    } else if (tier == CB_FOUND_LOCAL_HBM) {
+      local_gpu_hits++;
+    } else if (tier == CB_FOUND_LOCAL_DRAM) {
+      local_dram_hits++;
+      if (cfg.promote_on_hit) promote.push_back(to_hkey(keys + 16 * i));
+    }
+  }
+  if (!promote.empty()) {
+    // Promotion on a DRAM hit (CascadeStore::get -> promote_to_gpu,
+    // src/cascade_core.cpp:1303-1307, :1166-1185).
+    std::vector<TierMove> moves;
+    std::vector<HKey> dropped;
+    for (const HKey &k : promote) {
+      const BlockMeta *m = policy.find(k);
+      if (m && m->tier == kTierDram) policy.plan_promote(k, moves, dropped);
+    }
+    rc = run_moves(moves, dropped, st);
+    policy.commit();
+    if (rc) return rc;
+    rc = check_device_error(st);
+    if (rc) return rc;
+  }
+  return CB_OK;
+}
+
+int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps,
+                    uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
+  const uint64_t cap = staging_capacity();
+  std::vector<uint64_t> dptrs, dcaps;
+  int i = 0;
+  while (i < n) {
+    uint64_t bytes = 0;
+    int j = i;
+    while (j < n) {
+      const BlockMeta *m = policy.find(to_hkey(keys + 16 * j));
+      const uint64_t need = (m && m->size <= caps[j]) ? align_up(m->size, 256) : 0;
+      if (j > i && bytes + need > cap) break;
+      bytes += need;
+      ++j;
+    }
+    CB_TRY(d_staging.ensure(std::max<uint64_t>(bytes, 256)), "device staging");
+    dptrs.resize(j - i);
+    dcaps.resize(j - i);
+    uint64_t off = 0;
+    for (int k = i; k < j; ++k) {
+      const BlockMeta *m = policy.find(to_hkey(keys + 16 * k));
+      const uint64_t need = (m && m->size <= caps[k]) ? m->size : 0;
+      dptrs[k - i] = (uint64_t)d_staging.ptr + off;
+      dcaps[k - i] = m ? (m->size <= caps[k] ? m->size : 0) : 0;
+      off += align_up(need, 256);
+    }
+    int rc = get_device(keys + 16 * i, j - i, dptrs.data(), dcaps.data(), sizes_out + i, found_out + i, st);
+    if (rc) return rc;
+    // Report "not copied" against the caller's real capacity, then DMA the
+    // found blocks out, coalescing runs that are contiguous on both sides.
+    int k = i;
+    while (k < j) {
+      const bool ok = (found_out[k] & 0x0f) != CB_FOUND_MISS && sizes_out[k] <= caps[k];
+      if ((found_out[k] & 0x0f) != CB_FOUND_MISS && sizes_out[k] > caps[k]) {
+        found_out[k] = (uint8_t)((found_out[k] & 0x0f) | CB_FOUND_NOT_COPIED);
+      } else if ((found_out[k] & 0x0f) != CB_FOUND_MISS) {
+        found_out[k] &= 0x0f;
+      }
+      if (!ok) {
+        ++k;
+        continue;
+      }
+      int e = k + 1;
+      uint64_t run = sizes_out[k];
+      while (e < j && (found_out[e] & 0x0f) != CB_FOUND_MISS && sizes_out[e] <= caps[e] &&
+             static_cast<uint8_t *>(outs[k]) + (dptrs[e - i] - dptrs[k - i]) == outs[e] &&
+             dptrs[e - i] - dptrs[e - 1 - i] == sizes_out[e - 1]) {
+        run = dptrs[e - i] - dptrs[k - i] + sizes_out[e];
+        ++e;
+      }
+      if (run) CB_TRY(cudaMemcpyAsync(outs[k], reinterpret_cast<void *>(dptrs[k - i]), run,
+                                      cudaMemcpyDeviceToHost, st),
+                      "D2H block");
+      k = e;
+    }
+    CB_TRY(cudaStreamSynchronize(st), "D2H blocks");
+    i = j;
+  }
+  return CB_OK;
+}
+
+// ---------------------------------------------------------------- misc
+
+int Store::evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st) {
+  std::vector<TierMove> moves;
+  std::vector<HKey> dropped;
+  const uint64_t freed = policy.plan_evict(bytes, moves, dropped);
+  int rc = run_moves(moves, dropped, st);
+  policy.commit();
+  if (rc) return rc;
+  rc = check_device_error(st);
+  if (evicted) *evicted = freed;
+  return rc;
+}
+
+int Store::clear(cudaStream_t st) {
+  CB_TRY(cudaStreamSynchronize(st), "sync");
+  policy.clear();
+  CB_TRY(cudaMemsetAsync(table, 0, table_slots * sizeof(Slot), st), "index clear");
+  CB_TRY(cudaStreamSynchronize(st), "sync");
+  table_used = table_tombs = 0;
+  local_gpu_hits = local_dram_hits = remote_gpu_hits = remote_dram_hits = misses = 0;
+  return CB_OK;
+}
+
+void Store::fill_stats(cb_stats *o) const {
+  memset(o, 0, sizeof *o);
+  const PolicyCounters &c = policy.counters();
+  o->local_gpu_used = policy.hbm_used();
+  o->local_dram_used = policy.dram_used();
+  o->cluster_gpu_used = o->local_gpu_used;
+  o->cluster_dram_used = o->local_dram_used;
+  o->local_gpu_hits = local_gpu_hits;
+  o->local_dram_hits = local_dram_hits;
+  o->remote_gpu_hits = remote_gpu_hits;
+  o->remote_dram_hits = remote_dram_hits;
+  o->misses = misses;
+  o->dedup_hits = c.dedup_hits + remote_dedup_hits;
+  o->dedup_bytes_saved = c.dedup_bytes_saved + remote_dedup_bytes;
+  o->gpu_evictions = c.gpu_evictions;
+  o->dram_evictions = c.dram_evictions;
+  o->promotions_to_local = c.promotions;
+  o->total_blocks = policy.size();
+  o->prefix_blocks = c.prefix_blocks;
+  o->evicted_bytes = c.evicted_bytes;
+  o->promoted_bytes = c.promoted_bytes;
+  o->dropped_blocks = c.dropped_blocks;
+  o->kernel_launches = launches;
+  uint64_t *p = &o->sha_ns;  // sha, scatter, gather, tier: (ns, bytes, launches) each
+  for (int k = 0; k < 4; ++k) {
+    p[3 * k] = prof_ns[k];
+    p[3 * k + 1] = prof_bytes[k];
+    p[3 * k + 2] = prof_launches[k];
+  }
+}
+
+uint64_t Store::staging_capacity() const {
+  return cfg.staging_bytes ? cfg.staging_bytes : (1ull << 30);
+}
+
+}  // namespace cb
+
+// =================================================================== C ABI
+
+using cb::Store;
+
+struct cb_store {
+  Store *s;
+};
+
+namespace {
+
+cudaStream_t pick_stream(Store *s, void *stream) {
+  return stream ? static_cast<cudaStream_t>(stream) : s->own_stream;
+}
+
+template <class F>
+int guarded(cb_store *h, F f) {
+  if (!h || !h->s) return CB_ERR_ARG;
+  Store *s = h->s;
+  std::lock_guard<std::mutex> g(s->mu);
+  try {
+    cudaError_t e = cudaSetDevice(s->device);
+    if (e != cudaSuccess) return s->cuda_fail(e, "cudaSetDevice");
+    return f(s);
+  } catch (const std::bad_alloc &) {
+    return s->fail(CB_ERR_NOSPACE, "host allocation failed");
+  } catch (const std::exception &ex) {
+    return s->fail(CB_ERR_STATE, "%s", ex.what());
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+void cb_config_init(cb_config *c) {
+  if (!c) return;
+  memset(c, 0, sizeof *c);
+  c->gpu_capacity_bytes = 32ull << 30;  // DistributedConfig default
+  c->dram_capacity_bytes = 64ull << 30;
+  c->device = 0;
+  c->dedup_enabled = 1;
+  c->semantic_eviction = 1;
+  c->promote_on_hit = 1;
+  c->index_log2 = 16;
+  c->copy_engine = 0;
+  c->staging_bytes = 1ull << 30;
+}
+
+int cb_create(const cb_config *cfg, cb_store **out) {
+  if (!cfg || !out) return CB_ERR_ARG;
+  *out = nullptr;
+  Store *s = nullptr;
+  try {
+    s = new Store(*cfg);
+  } catch (...) {
+    cb::g_create_error = "host allocation failed";
+    return CB_ERR_NOSPACE;
+  }
+  s->copy_engine = cfg->copy_engine == 2 ? 2 : 1;
+  int rc = s->init();
+  if (rc) {
+    cb::g_create_error = s->last_error;
+    delete s;
+    return rc;
+  }
+  *out = new cb_store{s};
+  return CB_OK;
+}
+
+int cb_destroy(cb_store *h) {
+  if (!h) return CB_OK;
+  delete h->s;
+  delete h;
+  return CB_OK;
+}
+
+const char *cb_last_error(const cb_store *h) {
+  if (!h || !h->s) return cb::g_create_error.c_str();
+  return h->s->last_error.c_str();
+}
+
+int cb_hash_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, int32_t n,
+                  int32_t mem_kind, uint8_t *digests_out, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!ptrs || !sizes || !digests_out))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (n == 0) return CB_OK;
+    cudaStream_t st = pick_stream(s, stream);
+    if (mem_kind == CB_MEM_DEVICE) {
+      std::vector<uint64_t> p(n);
+      for (int i = 0; i < n; ++i) p[i] = (uint64_t)ptrs[i];
+      int rc = s->hash_device(p.data(), sizes, n, st);
+      if (rc) return rc;
+      memcpy(digests_out, s->h_out.ptr, 32ull * n);
+      return CB_OK;
+    }
+    // Host blocks: stage slices into device memory and hash them there.
+    const uint64_t cap = s->staging_capacity();
+    std::vector<uint64_t> p;
+    int i = 0;
+    while (i < n) {
+      uint64_t bytes = 0;
+      int j = i;
+      while (j < n && (j == i || bytes + cb::align_up(sizes[j], 256) <= cap)) bytes += cb::align_up(sizes[j++], 256);
+      cudaError_t e = s->d_staging.ensure(std::max<uint64_t>(bytes, 256));
+      if (e != cudaSuccess) return s->cuda_fail(e, "device staging");
+      p.resize(j - i);
+      uint64_t off = 0;
+      for (int k = i; k < j; ++k) {
+        p[k - i] = (uint64_t)s->d_staging.ptr + off;
+        if (sizes[k]) {
+          e = cudaMemcpyAsync(reinterpret_cast<void *>(p[k - i]), ptrs[k], sizes[k], cudaMemcpyHostToDevice, st);
+          if (e != cudaSuccess) return s->cuda_fail(e, "H2D block");
+        }
+        off += cb::align_up(sizes[k], 256);
+      }
+      int rc = s->hash_device(p.data(), sizes + i, j - i, st);
+      if (rc) return rc;
+      memcpy(digests_out + 32ull * i, s->h_out.ptr, 32ull * (j - i));
+      i = j;
+    }
+    return CB_OK;
+  });
+}
+
+int cb_put_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                 const uint8_t *keys_in, int32_t n, int32_t mem_kind, uint8_t *keys_out,
+                 uint8_t *status_out, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!ptrs || !sizes))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (n == 0) return CB_OK;
+    for (int i = 0; i < n; ++i)
+      if (sizes[i] > cb::kSizeMask) return s->fail(CB_ERR_ARG, "block %d too large", i);
+    cudaStream_t st = pick_stream(s, stream);
+    if (s->world > 1) return s->dht_put(ptrs, sizes, is_prefix, keys_in, n, mem_kind, keys_out, status_out, st);
+    if (mem_kind == CB_MEM_HOST) return s->put_host(ptrs, sizes, is_prefix, keys_in, n, keys_out, status_out, st);
+    std::vector<uint64_t> p(n);
+    for (int i = 0; i < n; ++i) p[i] = (uint64_t)ptrs[i];
+    return s->put_device(p.data(), sizes, is_prefix, keys_in, n, keys_out, status_out, st);
+  });
+}
+
+int cb_get_batch(cb_store *h, const uint8_t *keys, int32_t n, void *const *outs, const uint64_t *out_caps,
+                 int32_t mem_kind, uint64_t *sizes_out, uint8_t *found_out, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!keys || !outs || !out_caps || !sizes_out || !found_out)))
+      return s->fail(CB_ERR_ARG, "bad arguments");
+    if (n == 0) return CB_OK;
+    cudaStream_t st = pick_stream(s, stream);
+    if (s->world > 1) return s->dht_get(keys, n, outs, out_caps, mem_kind, sizes_out, found_out, st);
+    if (mem_kind == CB_MEM_HOST) return s->get_host(keys, n, outs, out_caps, sizes_out, found_out, st);
+    std::vector<uint64_t> o(n);
+    for (int i = 0; i < n; ++i) o[i] = (uint64_t)outs[i];
+    return s->get_device(keys, n, o.data(), out_caps, sizes_out, found_out, st);
+  });
+}
+
+int cb_contains_batch(cb_store *h, const uint8_t *keys, int32_t n, uint8_t *found_out) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!keys || !found_out))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (s->world > 1) return s->dht_contains(keys, n, found_out, s->own_stream);
+    for (int i = 0; i < n; ++i) found_out[i] = s->policy.find(cb::to_hkey(keys + 16 * i)) ? 1 : 0;
+    return CB_OK;
+  });
+}
+
+int cb_locate(cb_store *h, const uint8_t *key, cb_location *out, int32_t *found) {
+  return guarded(h, [&](Store *s) -> int {
+    if (!key || !out || !found) return s->fail(CB_ERR_ARG, "bad arguments");
+    const cb::BlockMeta *m = s->policy.find(cb::to_hkey(key));
+    *found = m ? 1 : 0;
+    memset(out, 0, sizeof *out);
+    if (!m) return CB_OK;
+    out->node_id = s->rank;
+    out->gpu_id = m->tier == cb::kTierHbm ? s->device : -1;
+    out->offset = m->off;
+    out->size = m->size;
+    out->is_gpu = m->tier == cb::kTierHbm;
+    out->is_prefix = m->prefix;
+    return CB_OK;
+  });
+}
+
+int cb_evict(cb_store *h, uint64_t bytes, uint64_t *evicted_bytes) {
+  return guarded(h, [&](Store *s) -> int { return s->evict(bytes, evicted_bytes, s->own_stream); });
+}
+
+int cb_get_stats(cb_store *h, cb_stats *out) {
+  return guarded(h, [&](Store *s) -> int {
+    if (!out) return s->fail(CB_ERR_ARG, "bad arguments");
+    s->fill_stats(out);
+    if (s->world > 1) return s->dht_cluster_usage(out);
+    return CB_OK;
+  });
+}
+
+int cb_clear(cb_store *h) {
+  return guarded(h, [&](Store *s) -> int { return s->clear(s->own_stream); });
+}
+
+int cb_sync(cb_store *h) {
+  return guarded(h, [&](Store *s) -> int {
+    cudaError_t e = cudaStreamSynchronize(s->own_stream);
+    if (e != cudaSuccess) return s->cuda_fail(e, "sync");
+    return CB_OK;
+  });
+}
+
+int cb_rank(const cb_store *h, int32_t *rank, int32_t *world) {
+  if (!h || !h->s || !rank || !world) return CB_ERR_ARG;
+  *rank = h->s->rank;
+  *world = h->s->world;
+  return CB_OK;
+}
+
+}  // extern "C"

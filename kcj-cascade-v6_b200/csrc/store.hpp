@@ -1,0 +1,147 @@
+// Store object behind the C ABI (one per GPU per process).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "cascade_b200.h"
+#include "common.cuh"
+#include "policy.hpp"
+
+namespace cb {
+
+struct PinnedBuf {
+  void *ptr = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t bytes);
+  void release();
+};
+
+struct DevBuf {
+  void *ptr = nullptr;
+  size_t cap = 0;
+  cudaError_t ensure(size_t bytes);
+  void release();
+};
+
+struct DhtState;  // dht.cu
+
+struct Store {
+  explicit Store(const cb_config &c);
+  ~Store();
+  int init();
+
+  cb_config cfg;
+  int device = -1;
+  int num_sms = 148;
+  int copy_engine = 1;  // 1 TMA bulk, 2 LSU
+  int hash_lanes = 32;  // chains per warp in the SHA-256 kernel
+  cudaStream_t own_stream = nullptr;
+
+  uint8_t *pool = nullptr;  // HBM slab pool
+  uint64_t pool_bytes = 0;
+  uint8_t *dram_host = nullptr;  // pinned DRAM arena (host address)
+  uint8_t *dram_dev = nullptr;   // same arena, device address
+  uint64_t dram_bytes = 0;
+
+  Slot *table = nullptr;
+  uint64_t table_slots = 0, table_used = 0, table_tombs = 0;
+  unsigned *d_err = nullptr;
+
+  PinnedBuf h_scratch, h_out, h_err;
+  DevBuf d_scratch, d_staging;
+
+  Policy policy;
+  PutPlan put_plan;
+  std::mutex mu;
+  std::string last_error;
+
+  uint64_t local_gpu_hits = 0, local_dram_hits = 0, remote_gpu_hits = 0, remote_dram_hits = 0,
+           misses = 0, remote_dedup_hits = 0, remote_dedup_bytes = 0;
+
+  int rank = 0, world = 1;
+  DhtState *dht = nullptr;
+
+  // Kernel accounting. kinds: 0 SHA-256, 1 scatter, 2 gather, 3 tier move.
+  bool profile = false;
+  cudaEvent_t ev_a = nullptr, ev_b = nullptr;
+  uint64_t launches = 0;
+  uint64_t prof_ns[4] = {0, 0, 0, 0}, prof_bytes[4] = {0, 0, 0, 0}, prof_launches[4] = {0, 0, 0, 0};
+
+  // Runs `launch` (one kernel) and, when profiling, times it with CUDA events
+  // recorded on the launching stream. `bytes` = payload bytes it processes.
+  template <class F>
+  cudaError_t timed(int kind, uint64_t bytes, cudaStream_t st, F launch) {
+    if (!profile) {
+      cudaError_t e = launch();
+      launches++;
+      return e;
+    }
+    cudaError_t e = cudaEventRecord(ev_a, st);
+    if (e != cudaSuccess) return e;
+    e = launch();
+    if (e != cudaSuccess) return e;
+    e = cudaEventRecord(ev_b, st);
+    if (e != cudaSuccess) return e;
+    e = cudaEventSynchronize(ev_b);
+    if (e != cudaSuccess) return e;
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, ev_a, ev_b);
+    prof_ns[kind] += (uint64_t)(ms * 1.0e6);
+    prof_bytes[kind] += bytes;
+    prof_launches[kind]++;
+    launches++;
+    return e;
+  }
+
+  int fail(int code, const char *fmt, ...);
+  int cuda_fail(cudaError_t e, const char *what);
+
+  cudaError_t alloc_table(uint64_t slots);
+  cudaError_t ensure_dram();
+  int reserve_index(uint64_t incoming, cudaStream_t st);
+  int check_device_error(cudaStream_t st);
+  int run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped,
+                cudaStream_t st);
+  int hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st);
+  int put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                 const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
+                 cudaStream_t st);
+  int put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+               const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
+               cudaStream_t st);
+  int get_device(const uint8_t *keys, int n, const uint64_t *outs, const uint64_t *caps,
+                 uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
+  int get_host(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps,
+               uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
+  int evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st);
+  int clear(cudaStream_t st);
+  void fill_stats(cb_stats *o) const;
+  uint64_t staging_capacity() const;
+
+  // dht.cu
+  int dht_attach(int rank, int world, const uint8_t *uid);
+  void dht_detach();
+  int dht_barrier();
+  int dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+              const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out,
+              uint8_t *status_out, cudaStream_t st);
+  int dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps, int mem_kind,
+              uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
+  int dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st);
+  int dht_cluster_usage(cb_stats *o);
+};
+
+inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+inline HKey to_hkey(const uint8_t *p) {
+  HKey k;
+  __builtin_memcpy(&k.lo, p, 8);
+  __builtin_memcpy(&k.hi, p + 8, 8);
+  return k;
+}
+
+}  // namespace cb

@@ -1,0 +1,217 @@
+"""ORACLE — test infrastructure only (see oracle/__init__.py).
+
+Sequential CPU restatement of the store semantics on the Cascade hot path:
+
+* ``block_id`` / ``block_ids``: compute_block_id
+  (cascade_Code/cpp/src/cascade_core.cpp:47-58) through the plain-C FIPS
+  180-4 restatement in ``sha256_oracle.c`` (ctypes).
+* ``SequentialStore``: DistributedStore::put (src/distributed_backend.cpp:
+  601-692; dedup check :604-608), put_batch (:813-841, sequential), get
+  (:698-795, bytes only), contains (:797-802), with the pybind return
+  conventions of python/bindings.cpp:152-161.
+* ``TierModel``: the prefix-protected demotion rule of
+  GPUBackend::evict_lru_semantic / evict_for_space (src/gpu_backend.cu:
+  482-537) and DistributedDRAMBackend::evict_for_space
+  (src/distributed_backend.cpp:240-284), with exact LRU order.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from collections import OrderedDict
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            subprocess.run(["make", "-C", _HERE, "all"], check=True, capture_output=True)
+        lib = C.CDLL(_LIB_PATH)
+        lib.oracle_sha256.argtypes = [C.c_void_p, C.c_uint64, C.c_void_p]
+        lib.oracle_sha256.restype = None
+        lib.oracle_sha256_batch.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
+        lib.oracle_sha256_batch.restype = None
+        lib.oracle_sha256_constants.argtypes = [C.c_void_p, C.c_void_p]
+        lib.oracle_sha256_constants.restype = None
+        _lib = lib
+    return _lib
+
+
+def sha256(data) -> bytes:
+    a = np.ascontiguousarray(np.frombuffer(bytes(data), np.uint8) if isinstance(data, (bytes, bytearray))
+                             else np.asarray(data, np.uint8))
+    out = np.empty(32, np.uint8)
+    _load().oracle_sha256(C.c_void_p(a.ctypes.data if a.size else 0), a.size, C.c_void_p(out.ctypes.data))
+    return out.tobytes()
+
+
+def sha256_batch(packed: np.ndarray, offsets, sizes) -> np.ndarray:
+    packed = np.ascontiguousarray(packed, np.uint8)
+    off = np.ascontiguousarray(offsets, np.uint64)
+    sz = np.ascontiguousarray(sizes, np.uint64)
+    out = np.empty((len(off), 32), np.uint8)
+    if len(off):
+        _load().oracle_sha256_batch(C.c_void_p(packed.ctypes.data), C.c_void_p(off.ctypes.data),
+                                    C.c_void_p(sz.ctypes.data), len(off), C.c_void_p(out.ctypes.data))
+    return out
+
+
+def block_id(data) -> str:
+    return sha256(data)[:16].hex()
+
+
+def constants() -> tuple[list[int], list[int]]:
+    k = np.empty(64, np.uint32)
+    h = np.empty(8, np.uint32)
+    _load().oracle_sha256_constants(C.c_void_p(k.ctypes.data), C.c_void_p(h.ctypes.data))
+    return [int(x) for x in k], [int(x) for x in h]
+
+
+class SequentialStore:
+    """Bytes-level model of one rank's DistributedStore."""
+
+    def __init__(self, dedup_enabled: bool = True):
+        self.dedup_enabled = dedup_enabled
+        self.blocks: dict[str, bytes] = {}
+        self.prefix: set[str] = set()
+        self.dedup_hits = 0
+        self.dedup_bytes_saved = 0
+        self.misses = 0
+
+    def put(self, block_id: str, data: bytes, is_prefix: bool = False) -> tuple[bool, int]:
+        """Returns (stored_ok, status) with status 0 new, 1 dedup hit."""
+        if block_id in self.blocks:
+            if self.dedup_enabled:
+                self.dedup_hits += 1
+                self.dedup_bytes_saved += len(data)
+            return True, 1
+        self.blocks[block_id] = bytes(data)
+        if is_prefix:
+            self.prefix.add(block_id)
+        return True, 0
+
+    def put_batch(self, ids, datas, is_prefix=None) -> list[int]:
+        flags = is_prefix or [False] * len(ids)
+        return [self.put(i, d, p)[1] for i, d, p in zip(ids, datas, flags)]
+
+    def get(self, block_id: str):
+        d = self.blocks.get(block_id)
+        if d is None:
+            self.misses += 1
+            return False, None
+        return True, d
+
+    def contains(self, block_id: str) -> bool:
+        return block_id in self.blocks
+
+
+class TierModel:
+    """HBM/DRAM placement under the prefix-protected LRU demotion rule.
+
+    Logical-capacity model (the reference checks ``used + size > capacity``,
+    src/gpu_backend.cu:307); allocation fragmentation is not modelled, so use
+    equal block sizes when comparing placements exactly.
+    """
+
+    def __init__(self, hbm_cap: int, dram_cap: int, semantic: bool = True):
+        self.hbm_cap, self.dram_cap, self.semantic = hbm_cap, dram_cap, semantic
+        self.hbm: OrderedDict[str, int] = OrderedDict()   # id -> size, last = MRU
+        self.dram: OrderedDict[str, int] = OrderedDict()
+        self.prefix: set[str] = set()
+        self.dropped: list[str] = []
+        self.evictions = 0
+
+    def _victim_hbm(self):
+        order = list(self.hbm.keys())
+        if self.semantic:
+            for k in order:
+                if k not in self.prefix:
+                    return k
+        return order[0] if order else None
+
+    def _room_dram(self, size: int) -> bool:
+        if self.dram_cap == 0 or size > self.dram_cap:
+            return False
+        while sum(self.dram.values()) + size > self.dram_cap:
+            cands = [k for k in self.dram if not (self.semantic and k in self.prefix)]
+            if not cands:
+                return False
+            v = cands[0]
+            del self.dram[v]
+            self.dropped.append(v)
+        return True
+
+    def _demote_one(self) -> bool:
+        v = self._victim_hbm()
+        if v is None:
+            return False
+        size = self.hbm.pop(v)
+        self.evictions += 1
+        if self._room_dram(size):
+            self.dram[v] = size
+        else:
+            self.dropped.append(v)
+        return True
+
+    def put(self, k: str, size: int, is_prefix: bool = False) -> str:
+        if k in self.hbm or k in self.dram:
+            return "dedup"
+        if is_prefix:
+            self.prefix.add(k)
+        while sum(self.hbm.values()) + size > self.hbm_cap:
+            if not self._demote_one():
+                break
+        if sum(self.hbm.values()) + size <= self.hbm_cap:
+            self.hbm[k] = size
+            return "hbm"
+        if self._room_dram(size):
+            self.dram[k] = size
+            return "dram"
+        return "failed"
+
+    def touch(self, k: str):
+        if k in self.hbm:
+            self.hbm.move_to_end(k)
+        elif k in self.dram:
+            self.dram.move_to_end(k)
+
+    def promote(self, k: str) -> bool:
+        if k not in self.dram:
+            return False
+        size = self.dram[k]
+        # the promoted block itself is never a DRAM victim while room is made
+        while sum(self.hbm.values()) + size > self.hbm_cap:
+            v = self._victim_hbm()
+            if v is None:
+                return False
+            vs = self.hbm.pop(v)
+            self.evictions += 1
+            cands_ok = self.dram_cap > 0 and vs <= self.dram_cap
+            while cands_ok and sum(self.dram.values()) + vs > self.dram_cap:
+                cands = [x for x in self.dram if x != k and not (self.semantic and x in self.prefix)]
+                if not cands:
+                    cands_ok = False
+                    break
+                del self.dram[cands[0]]
+                self.dropped.append(cands[0])
+            if cands_ok:
+                self.dram[v] = vs
+            else:
+                self.dropped.append(v)
+        del self.dram[k]
+        self.hbm[k] = size
+        return True
+
+    def tier(self, k: str) -> str | None:
+        if k in self.hbm:
+            return "hbm"
+        if k in self.dram:
+            return "dram"
+        return None

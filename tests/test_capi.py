@@ -1,0 +1,103 @@
+"""C-ABI library checks that need no GPU: it loads, exports every entry
+point include/cascade_b200.h declares, its struct layouts match the ctypes
+mirrors, and it fails cleanly (no crash) when no GPU is present."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import pytest
+
+from cascade_cpp import _lib as L
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+HEADER = os.path.join(ROOT, "include", "cascade_b200.h")
+
+
+def header_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(cb_\w+)\s*\(", src)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(L.LIB_PATH):
+        import sys
+        sys.path.insert(0, os.path.join(ROOT, "kcj-cascade-v6_b200"))
+        import build
+        build.build()
+    return L.load()
+
+
+def test_header_declares_expected_surface():
+    fns = header_functions()
+    for f in ["cb_create", "cb_destroy", "cb_put_batch", "cb_get_batch", "cb_hash_batch",
+              "cb_contains_batch", "cb_locate", "cb_evict", "cb_get_stats", "cb_clear",
+              "cb_dht_attach", "cb_dht_barrier", "cb_dht_unique_id"]:
+        assert f in fns
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(re.findall(r"\bT (cb_\w+)", out))
+    missing = [f for f in header_functions() if f not in exported]
+    assert not missing, missing
+    for f in header_functions():
+        assert hasattr(lib, f)
+
+
+def test_ctypes_signatures_cover_header():
+    assert sorted(n for n, _, _ in L.SIGNATURES) == header_functions()
+
+
+def test_struct_layouts_match_c(tmp_path):
+    prog = tmp_path / "layout.c"
+    prog.write_text(
+        '#include <stdio.h>\n#include <stddef.h>\n#include "cascade_b200.h"\n'
+        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu\\n\", sizeof(cb_config), sizeof(cb_stats),"
+        " sizeof(cb_location), offsetof(cb_config, staging_bytes), offsetof(cb_location, offset),"
+        " offsetof(cb_stats, dropped_blocks)); return 0;}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(prog), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    assert vals == [C.sizeof(L.cb_config), C.sizeof(L.cb_stats), C.sizeof(L.cb_location),
+                    L.cb_config.staging_bytes.offset, L.cb_location.offset.offset,
+                    L.cb_stats.dropped_blocks.offset]
+
+
+def test_config_defaults(lib):
+    cfg = L.cb_config()
+    lib.cb_config_init(C.byref(cfg))
+    assert cfg.gpu_capacity_bytes == 32 << 30  # DistributedConfig default
+    assert cfg.dram_capacity_bytes == 64 << 30
+    assert cfg.dedup_enabled == 1 and cfg.semantic_eviction == 1
+
+
+def test_create_without_gpu_fails_cleanly(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    cfg = L.cb_config()
+    lib.cb_config_init(C.byref(cfg))
+    h = C.c_void_p()
+    rc = lib.cb_create(C.byref(cfg), C.byref(h))
+    assert rc != L.CB_OK and not h.value
+    assert lib.cb_last_error(None)
+
+
+def test_null_arguments_rejected(lib):
+    assert lib.cb_put_batch(None, None, None, None, None, 1, 0, None, None, None) == L.CB_ERR_ARG
+    assert lib.cb_get_batch(None, None, 1, None, None, 0, None, None, None) == L.CB_ERR_ARG
+    assert lib.cb_destroy(None) == L.CB_OK
+
+
+def test_product_never_imports_oracle():
+    pkg = os.path.join(ROOT, "kcj-cascade-v6_b200")
+    for dirpath, _, files in os.walk(pkg):
+        for f in files:
+            if f.endswith((".py", ".cu", ".cuh", ".cpp", ".hpp")):
+                txt = open(os.path.join(dirpath, f)).read()
+                assert "import oracle" not in txt and "from oracle" not in txt, f
+                assert "sha256_oracle" not in txt, f

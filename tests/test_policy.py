@@ -1,0 +1,221 @@
+"""Host policy of the store (csrc/policy.cpp) on the CPU: extent allocator,
+sequential dedup, and prefix-protected demotion checked against the
+oracle's TierModel (restating src/gpu_backend.cu:482-537 and
+src/distributed_backend.cpp:240-284)."""
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle.store_oracle import SequentialStore, TierModel
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(ROOT, "kcj-cascade-v6_b200", "csrc")
+
+
+@pytest.fixture(scope="module")
+def ph(tmp_path_factory):
+    out = tmp_path_factory.mktemp("policy") / "libpolicy_harness.so"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-I{CSRC}",
+                    os.path.join(HERE, "native", "policy_harness.cpp"), os.path.join(CSRC, "policy.cpp"),
+                    "-o", str(out)], check=True)
+    lib = C.CDLL(str(out))
+    V, U64, I = C.c_void_p, C.c_uint64, C.c_int
+    lib.ph_create.restype = V
+    lib.ph_create.argtypes = [U64, U64, I]
+    lib.ph_destroy.argtypes = [V]
+    lib.ph_put.restype = I
+    lib.ph_put.argtypes = [V, V, V, V, I, I, V, V, I, V, C.POINTER(I), V, C.POINTER(I)]
+    lib.ph_find.restype = I
+    lib.ph_find.argtypes = [V, U64, U64, C.POINTER(U64)]
+    lib.ph_touch.argtypes = [V, U64, U64]
+    lib.ph_promote.restype = I
+    lib.ph_promote.argtypes = [V, U64, U64]
+    lib.ph_evict.restype = U64
+    lib.ph_evict.argtypes = [V, U64]
+    lib.ph_counters.argtypes = [V, V]
+    lib.ph_alloc_create.restype = V
+    lib.ph_alloc_create.argtypes = [U64]
+    lib.ph_alloc_destroy.argtypes = [V]
+    lib.ph_alloc.restype = U64
+    lib.ph_alloc.argtypes = [V, U64]
+    lib.ph_free.argtypes = [V, U64, U64]
+    for f in ("ph_alloc_free_bytes", "ph_alloc_extents", "ph_alloc_largest"):
+        getattr(lib, f).restype = U64
+        getattr(lib, f).argtypes = [V]
+    return lib
+
+
+class Pol:
+    def __init__(self, lib, hbm, dram, semantic=True):
+        self.lib, self.p = lib, lib.ph_create(hbm, dram, 1 if semantic else 0)
+        self.names = {}
+
+    def key(self, name):
+        k = self.names.setdefault(name, (len(self.names) + 1, 0xABC))
+        return k
+
+    def put(self, names, sizes, prefix=None, dedup=True):
+        n = len(names)
+        keys = np.array([self.key(x) for x in names], np.uint64).reshape(-1)
+        sz = np.array(sizes, np.uint64)
+        pf = np.array(prefix if prefix is not None else [0] * n, np.uint8)
+        st = np.zeros(n, np.uint8)
+        moves = np.zeros((4096, 6), np.uint64)
+        dropped = np.zeros((4096, 2), np.uint64)
+        places = np.zeros((max(n, 1), 4), np.uint64)
+        nd, npl = C.c_int(0), C.c_int(0)
+        nm = self.lib.ph_put(self.p, keys.ctypes.data, sz.ctypes.data, pf.ctypes.data, n, 1 if dedup else 0,
+                             st.ctypes.data, moves.ctypes.data, 4096, dropped.ctypes.data, C.byref(nd),
+                             places.ctypes.data, C.byref(npl))
+        return st.tolist(), moves[:nm], dropped[:nd.value], places[:npl.value]
+
+    def tier(self, name):
+        off = C.c_uint64(0)
+        lo, hi = self.key(name)
+        t = self.lib.ph_find(self.p, lo, hi, C.byref(off))
+        return {-1: None, 0: "hbm", 1: "dram"}[t]
+
+    def touch(self, name):
+        self.lib.ph_touch(self.p, *self.key(name))
+
+    def promote(self, name):
+        return self.lib.ph_promote(self.p, *self.key(name))
+
+    def counters(self):
+        out = np.zeros(10, np.uint64)
+        self.lib.ph_counters(self.p, out.ctypes.data)
+        return dict(zip(["hbm_used", "dram_used", "size", "dedup_hits", "dedup_bytes", "gpu_evictions",
+                         "dram_evictions", "dropped", "prefix_blocks", "promotions"], map(int, out)))
+
+
+def test_allocator_best_fit_and_coalesce(ph):
+    a = ph.ph_alloc_create(1 << 20)
+    offs = [ph.ph_alloc(a, 1000) for _ in range(10)]  # rounded to 1024
+    assert offs == [i * 1024 for i in range(10)]
+    for o in offs[2:5]:
+        ph.ph_free(a, o, 1000)
+    assert ph.ph_alloc_extents(a) == 2  # [2048, 5120) coalesced + tail
+    assert ph.ph_alloc(a, 3000) == 2048  # best fit into the 3 KiB hole
+    ph.ph_free(a, 2048, 3000)
+    for o in offs[:2] + offs[5:]:
+        ph.ph_free(a, o, 1000)
+    assert ph.ph_alloc_extents(a) == 1 and ph.ph_alloc_free_bytes(a) == 1 << 20
+    assert ph.ph_alloc(a, (1 << 20) + 1) == 2 ** 64 - 1
+    ph.ph_alloc_destroy(a)
+
+
+def test_allocator_random_never_overlaps(ph):
+    rng = np.random.default_rng(3)
+    cap = 1 << 24
+    a = ph.ph_alloc_create(cap)
+    live = {}
+    for step in range(3000):
+        if live and rng.random() < 0.45:
+            o = rng.choice(list(live))
+            ph.ph_free(a, int(o), int(live.pop(o)))
+        else:
+            s = int(rng.integers(1, 200_000))
+            o = ph.ph_alloc(a, s)
+            if o != 2 ** 64 - 1:
+                r = (s + 255) // 256 * 256
+                for lo, ls in live.items():
+                    lr = (ls + 255) // 256 * 256
+                    assert o + r <= lo or lo + lr <= o
+                assert o % 256 == 0 and o + r <= cap
+                live[o] = s
+    used = sum((s + 255) // 256 * 256 for s in live.values())
+    assert ph.ph_alloc_free_bytes(a) == cap - used
+    ph.ph_alloc_destroy(a)
+
+
+def test_sequential_dedup_matches_oracle(ph):
+    rng = np.random.default_rng(9)
+    names = [f"b{int(x)}" for x in rng.integers(0, 40, 300)]
+    pol = Pol(ph, 1 << 30, 0)
+    ora = SequentialStore()
+    got = []
+    for i in range(0, 300, 37):  # uneven batches
+        st, _, _, _ = pol.put(names[i:i + 37], [1000] * len(names[i:i + 37]))
+        got += st
+    want = [ora.put(n, b"x" * 1000)[1] for n in names]
+    assert got == want
+    c = pol.counters()
+    assert c["dedup_hits"] == ora.dedup_hits and c["dedup_bytes"] == ora.dedup_bytes_saved
+    assert c["size"] == len(set(names))
+
+
+def test_dedup_disabled_counts_nothing(ph):
+    pol = Pol(ph, 1 << 30, 0)
+    st, _, _, _ = pol.put(["a", "a", "b"], [10, 10, 10], dedup=False)
+    assert st == [0, 1, 0] and pol.counters()["dedup_hits"] == 0
+
+
+@pytest.mark.parametrize("semantic", [True, False])
+def test_demotion_matches_tier_model(ph, semantic):
+    S = 64 * 1024
+    rng = np.random.default_rng(4 if semantic else 5)
+    pol = Pol(ph, 10 * S, 25 * S, semantic=semantic)
+    model = TierModel(10 * S, 25 * S, semantic=semantic)
+    for step in range(200):
+        op = rng.random()
+        name = f"k{int(rng.integers(0, 60))}"
+        if op < 0.6:
+            pf = bool(rng.random() < 0.15)
+            st, moves, dropped, _ = pol.put([name], [S], [1 if pf else 0])
+            r = model.put(name, S, pf)
+            assert (st[0] == 1) == (r == "dedup")
+        elif op < 0.85:
+            pol.touch(name)
+            model.touch(name)
+        else:
+            if model.tier(name) == "dram":
+                assert pol.promote(name) >= 1
+                assert model.promote(name)
+        for k in list(pol.names):
+            assert pol.tier(k) == model.tier(k), (step, k)
+    c = pol.counters()
+    assert c["gpu_evictions"] == model.evictions
+    assert c["hbm_used"] == sum(model.hbm.values()) and c["dram_used"] == sum(model.dram.values())
+
+
+def test_prefix_never_evicted_while_nonprefix_evictable(ph):
+    S = 1 << 20
+    pol = Pol(ph, 4 * S, 100 * S)
+    pol.put(["p0", "p1"], [S, S], [1, 1])
+    for i in range(20):
+        _, moves, _, _ = pol.put([f"n{i}"], [S])
+        for mv in moves:
+            name = next(k for k, v in pol.names.items() if v == (int(mv[0]), int(mv[1])))
+            assert not name.startswith("p"), name
+    assert pol.tier("p0") == "hbm" and pol.tier("p1") == "hbm"
+
+
+def test_batch_never_evicts_its_own_placements(ph):
+    S = 1 << 20
+    pol = Pol(ph, 4 * S, 100 * S)
+    st, moves, _, places = pol.put([f"x{i}" for i in range(6)], [S] * 6)
+    # 4 fit in HBM; the other 2 cannot displace same-batch blocks -> DRAM tier
+    assert st == [0] * 6 and len(moves) == 0
+    assert [int(p[2]) for p in places] == [0, 0, 0, 0, 1, 1]
+
+
+def test_dram_full_drops_lru_nonprefix(ph):
+    S = 1 << 20
+    pol = Pol(ph, 2 * S, 2 * S)
+    for i in range(6):
+        pol.put([f"b{i}"], [S])
+    assert [pol.tier(f"b{i}") for i in range(6)] == [None, None, "dram", "dram", "hbm", "hbm"]
+    c = pol.counters()
+    assert c["dropped"] == 2 and c["dram_evictions"] == 2 and c["size"] == 4
+
+
+def test_explicit_evict(ph):
+    S = 1 << 20
+    pol = Pol(ph, 8 * S, 8 * S)
+    pol.put([f"b{i}" for i in range(8)], [S] * 8)
+    assert ph.ph_evict(pol.p, 3 * S) == 3 * S
+    assert [pol.tier(f"b{i}") for i in range(3)] == ["dram"] * 3
