@@ -145,8 +145,10 @@ int cb_contains_batch(cb_store *s, const uint8_t *keys, int32_t n, uint8_t *foun
 int cb_locate(cb_store *s, const uint8_t *key, cb_location *out, int32_t *found);
 
 /* Demote least-recently-used HBM blocks (prefix blocks last) to the DRAM
- * tier until `bytes` are free. Replaces DistributedStore::evict_gpu_to_dram
- * (src/distributed_backend.cpp:876-941). */
+ * tier until at least `bytes` have left HBM; *evicted_bytes = bytes moved.
+ * Replaces DistributedStore::evict_gpu_to_dram
+ * (src/distributed_backend.cpp:876-941, GPUBackend::evict_for_space
+ * src/gpu_backend.cu:514-537). */
 int cb_evict(cb_store *s, uint64_t bytes, uint64_t *evicted_bytes);
 
 /* Replaces DistributedStore::get_stats (src/distributed_backend.cpp:1384-1427). */

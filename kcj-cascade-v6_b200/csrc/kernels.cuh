@@ -11,8 +11,9 @@ struct HashJob {
 };
 
 // sha256.cu — digests: n * 8 words holding the 32 digest bytes in order.
+// One CTA (producer + consumer warp) per 32 blocks.
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
-                                cudaStream_t stream);
+                                unsigned *d_err, cudaStream_t stream);
 
 // copy.cu — batched copies. Descriptor i covers units
 // [unit_start[i], unit_start[i+1]) of kCopyUnit bytes each; a unit past the

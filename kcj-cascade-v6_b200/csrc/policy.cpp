@@ -302,9 +302,10 @@ bool Policy::plan_promote(const HKey &k, std::vector<TierMove> &moves,
 
 uint64_t Policy::plan_evict(uint64_t bytes, std::vector<TierMove> &moves,
                             std::vector<HKey> &dropped) {
+  // GPUBackend::evict_for_space (src/gpu_backend.cu:514-537): demote victims
+  // until at least `bytes` have left HBM (or nothing is left to demote).
   const uint64_t before = hbm_used_;
-  const uint64_t target = bytes >= hbm_cap_ ? 0 : hbm_cap_ - bytes;
-  while (hbm_used_ > target) {
+  while (before - hbm_used_ < bytes) {
     if (!demote_one(moves, dropped)) break;
   }
   return before - hbm_used_;

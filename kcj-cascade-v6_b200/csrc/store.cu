@@ -324,12 +324,11 @@ int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaS
   CB_TRY(timed(0, total, st,
                [&] {
                  return launch_sha256_batch(reinterpret_cast<const HashJob *>(d + o_jobs), n,
-                                            reinterpret_cast<uint32_t *>(d + o_dig), hash_lanes, st);
+                                            reinterpret_cast<uint32_t *>(d + o_dig), hash_lanes, d_err, st);
                }),
          "sha256 launch");
   CB_TRY(cudaMemcpyAsync(h_out.ptr, d + o_dig, 32ull * n, cudaMemcpyDeviceToHost, st), "D2H digests");
-  CB_TRY(cudaStreamSynchronize(st), "sha256");
-  return CB_OK;
+  return check_device_error(st);  // syncs; a timed-out hash is an error
 }
 
 // ---------------------------------------------------------------- put
