@@ -40,6 +40,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "aggregate batch_put (incl. SHA256) + batch_get GB/s"
 GB = 1e9
+SHA_TRAFFIC_PER_1024_LAUNCH = 711_190_272  # bytes, ncu capture (see roofline note)
 
 
 def parse():
@@ -372,7 +373,11 @@ def main():
         "roofline": {
             "kernel": "sha256_batch_kernel", "bound": "hbm", "achieved": round(sha_achieved, 2),
             "peak": hbm_peak, "unit": "GB/s", "frac": round(sha_achieved / hbm_peak, 5),
-            "peak_source": peak_src, "traffic": None,
+            "peak_source": peak_src,
+            # dram__bytes_read.sum + dram__bytes_write.sum of one 1024-block
+            # launch from the ncu capture in profiles/sha256_pc_kernel_1024x917504.md
+            # (704.9 MB + 6.3 MB; the 25 % copies are read from L2, not DRAM)
+            "traffic": SHA_TRAFFIC_PER_1024_LAUNCH if args.batch == 1024 else None,
             "bytes_per_launch": int(sha_bytes_launch),
             "note": "bytes = block bytes read once per launch; binding limit is the SHA-256 chain latency "
                     "(one serial chain per block, chains = batch size)",
