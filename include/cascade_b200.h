@@ -182,6 +182,26 @@ int cb_dht_barrier(cb_store *s);
 /* Rank and world size (1-GPU stores: 0 and 1). */
 int cb_rank(const cb_store *s, int32_t *rank, int32_t *world);
 
+/* ---- allocation-free hashing -------------------------------------------- */
+
+/* Most blocks one cb_hash_batch_noalloc call accepts (its fixed scratch). */
+#define CB_NOALLOC_MAX_BLOCKS 4096
+
+/* Batched SHA-256 that allocates nothing; no counterpart in the reference.
+ * For callers that may not allocate GPU memory while they run (an engine that
+ * reserved nearly all HBM for its own pool and forbids cudaMalloc during
+ * serving, or code inside an allocator callback): it needs no cb_store.
+ * Blocks (ptrs[i], sizes[i]) are device memory on `device`; digests_out is a
+ * caller-owned, 16-byte aligned device buffer of n*32 bytes. n above
+ * CB_NOALLOC_MAX_BLOCKS is rejected with CB_ERR_ARG. Its scratch is one
+ * static device array of ~66 KB that every GPU loading the library keeps
+ * until exit; all calls share it, so calls that overlap on the GPU race.
+ * The first call on a device looks up that array's address (make it before
+ * any stream capture). Results are final when the call returns; errors are
+ * reported by cb_last_error(NULL). */
+int cb_hash_batch_noalloc(int32_t device, const void *const *ptrs, const uint64_t *sizes, int32_t n,
+                          uint8_t *digests_out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

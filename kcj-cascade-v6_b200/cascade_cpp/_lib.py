@@ -105,7 +105,10 @@ SIGNATURES = [
     ("cb_dht_attach", C.c_int, [_P, C.c_int32, C.c_int32, _P]),
     ("cb_dht_barrier", C.c_int, [_P]),
     ("cb_rank", C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    ("cb_hash_batch_noalloc", C.c_int, [C.c_int32, _P, _P, C.c_int32, _P, _P]),
 ]
+
+CB_NOALLOC_MAX_BLOCKS = 4096
 
 
 def load(path: str = LIB_PATH) -> C.CDLL:
