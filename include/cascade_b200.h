@@ -182,6 +182,12 @@ int cb_dht_barrier(cb_store *s);
 /* Rank and world size (1-GPU stores: 0 and 1). */
 int cb_rank(const cb_store *s, int32_t *rank, int32_t *world);
 
+/* Owner rank of a key in a `world`-rank DHT: the first 8 key bytes read as a
+ * big-endian integer, modulo world. Host-only, no GPU needed. Replaces
+ * DistributedGPUBackend::get_target_node (src/distributed_backend.cpp:396-398),
+ * whose std::hash placement is not stable across builds. */
+int32_t cb_owner_rank(const uint8_t *key, int32_t world);
+
 /* ---- allocation-free hashing -------------------------------------------- */
 
 /* Most blocks one cb_hash_batch_noalloc call accepts (its fixed scratch). */

@@ -73,6 +73,12 @@ def key_to_block_id(key: bytes) -> str:
     return bytes(key).hex()
 
 
+def owner_rank(block_id: str, world: int) -> int:
+    """Rank that owns ``block_id`` in a ``world``-rank DHT (cb_owner_rank)."""
+    k = np.frombuffer(block_id_to_key(block_id), np.uint8).copy()
+    return int(_native_lib().cb_owner_rank(C.c_void_p(k.ctypes.data), int(world)))
+
+
 # ------------------------------------------------------------------ buffers
 
 def _block_view(data, writable: bool = False):
@@ -146,25 +152,23 @@ class _Native:
         n = len(ptrs)
         keys = np.empty((n, 16), np.uint8)
         status = np.empty(n, np.uint8)
-        if n:
-            self._check(self.lib.cb_put_batch(self.h, _ptr(ptrs), _ptr(sizes), _ptr(prefix), _ptr(keys_in), n,
-                                              kind, _ptr(keys), _ptr(status), self.stream_ptr(kind)))
+        # called even for n == 0: in a DHT every rank takes part in each batch
+        self._check(self.lib.cb_put_batch(self.h, _ptr(ptrs), _ptr(sizes), _ptr(prefix), _ptr(keys_in), n,
+                                          kind, _ptr(keys), _ptr(status), self.stream_ptr(kind)))
         return keys, status
 
     def get(self, keys, outs, caps, kind):
         n = len(keys)
         sizes = np.zeros(n, np.uint64)
         found = np.zeros(n, np.uint8)
-        if n:
-            self._check(self.lib.cb_get_batch(self.h, _ptr(keys), n, _ptr(outs), _ptr(caps), kind,
-                                              _ptr(sizes), _ptr(found), self.stream_ptr(kind)))
+        self._check(self.lib.cb_get_batch(self.h, _ptr(keys), n, _ptr(outs), _ptr(caps), kind,
+                                          _ptr(sizes), _ptr(found), self.stream_ptr(kind)))
         return sizes, found
 
     def contains(self, keys) -> np.ndarray:
         n = len(keys)
         found = np.zeros(n, np.uint8)
-        if n:
-            self._check(self.lib.cb_contains_batch(self.h, _ptr(keys), n, _ptr(found)))
+        self._check(self.lib.cb_contains_batch(self.h, _ptr(keys), n, _ptr(found)))
         return found
 
     def locate(self, key: bytes):
@@ -539,6 +543,10 @@ class DistributedStore(_StoreBase):
 
     def _attach_dht(self):
         import torch.distributed as dist
+        # The DHT's own collectives are a few bytes; keep NCCL off NVLink
+        # multicast (NVLS) so a rank that dies cannot leave a bound multicast
+        # object behind on the other GPUs.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         if not dist.is_initialized():
             dist.init_process_group(backend="gloo", init_method="env://")
         rank, world = dist.get_rank(), dist.get_world_size()

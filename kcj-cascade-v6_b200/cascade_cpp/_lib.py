@@ -106,6 +106,7 @@ SIGNATURES = [
     ("cb_dht_barrier", C.c_int, [_P]),
     ("cb_rank", C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     ("cb_hash_batch_noalloc", C.c_int, [C.c_int32, _P, _P, C.c_int32, _P, _P]),
+    ("cb_owner_rank", C.c_int32, [_P, C.c_int32]),
 ]
 
 CB_NOALLOC_MAX_BLOCKS = 4096

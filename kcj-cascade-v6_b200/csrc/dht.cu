@@ -1,32 +1,677 @@
-// Multi-GPU hash-sharded DHT (placeholder until the NCCL path lands).
+// Multi-GPU hash-sharded DHT: the B200 form of DistributedGPUBackend's
+// remote tier (src/distributed_backend.cpp:303-514) and of the replicated
+// location index that sync_metadata maintains with MPI_Allgatherv
+// (:1323-1382).
+//
+// One process per GPU, W ranks. Owner(block) = first 8 ID bytes (big-endian)
+// mod W. Each rank's HBM slab pool and device index are exported with CUDA
+// IPC and mapped into every other rank at attach time, so payloads move by
+// direct peer loads/stores over NVLink; only 16-32-byte lookup records travel
+// through NCCL (grouped send/recv = all-to-all, preceded by an all-gather of
+// the per-peer counts). No TMA multicast is used; peer payload reads may use
+// non-multicast TMA loads, peer payload writes use plain vector stores.
+//
+// batch_put : local SHA-256 -> requests to owners -> owners dedup in
+//             (source rank, batch index) order, allocate, insert into their
+//             index, reply {status, offset} -> writers copy new blocks into
+//             the owners' pools -> closing all-reduce (barrier).
+// batch_get : keys to owners -> owner index lookup kernel -> replies
+//             {location, meta} -> gather kernel reading the owners' pools ->
+//             closing all-reduce.
+// Every collective call is made by all ranks in the same order. Waits are
+// bounded: a collective that does not finish within the timeout aborts the
+// communicator and returns CB_ERR_TIMEOUT.
+#include <nccl.h>
+#include <string.h>
+
+#include <algorithm>
+#include <chrono>
+#include <thread>
+#include <vector>
+
+#include "kernels.cuh"
 #include "store.hpp"
 
 namespace cb {
 
-struct DhtState {};
+namespace {
 
-int Store::dht_attach(int, int, const uint8_t *) {
-  return fail(CB_ERR_STATE, "multi-GPU DHT not available in this build");
+struct PutReq {
+  uint64_t klo, khi, size, flags;  // flags bit 0: prefix
+};
+struct PutRep {
+  uint64_t loc;  // offset | kLocDram
+  uint32_t status;
+  uint32_t pad;
+};
+struct Export {
+  cudaIpcMemHandle_t pool, table;
+  uint64_t pool_bytes, table_slots;
+  int32_t device, pad;
+};
+
+inline uint64_t be_owner(const HKey &k, int world) {
+  return (uint64_t)owner_of(Key{k.lo, k.hi}, world);
 }
-void Store::dht_detach() {}
-int Store::dht_barrier() { return CB_OK; }
-int Store::dht_put(const void *const *, const uint64_t *, const uint8_t *, const uint8_t *, int, int,
-                   uint8_t *, uint8_t *, cudaStream_t) {
-  return fail(CB_ERR_STATE, "multi-GPU DHT not available in this build");
+
+}  // namespace
+
+struct DhtState {
+  ncclComm_t comm = nullptr;
+  int W = 1, me = 0;
+  std::vector<uint64_t> pool, pool_bytes, table, slots;
+  std::vector<int> device;
+  std::vector<void *> opened;
+  DevBuf d_send, d_recv, d_misc;
+  PinnedBuf h_send, h_recv, h_misc;
+  double timeout_s = 600.0;
+};
+
+// ------------------------------------------------------------ plumbing
+
+int Store::dht_nccl(int r, const char *what) {
+  if (r == ncclSuccess) return CB_OK;
+  if (r == ncclInProgress) {
+    const auto t0 = std::chrono::steady_clock::now();
+    ncclResult_t st = ncclInProgress;
+    while (st == ncclInProgress) {
+      if (ncclCommGetAsyncError(dht->comm, &st) != ncclSuccess) break;
+      if (st != ncclInProgress) break;
+      if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > dht->timeout_s) {
+        ncclCommAbort(dht->comm);
+        dht->comm = nullptr;
+        return fail(CB_ERR_TIMEOUT, "%s: NCCL call did not complete", what);
+      }
+      std::this_thread::yield();
+    }
+    if (st == ncclSuccess) return CB_OK;
+    r = st;
+  }
+  return fail(CB_ERR_NCCL, "%s: %s", what, ncclGetErrorString((ncclResult_t)r));
 }
-int Store::dht_get(const uint8_t *, int, void *const *, const uint64_t *, int, uint64_t *, uint8_t *,
-                   cudaStream_t) {
-  return fail(CB_ERR_STATE, "multi-GPU DHT not available in this build");
+
+// Waits for the stream while watching the communicator (bounded).
+int Store::dht_sync(cudaStream_t st) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(st);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) return cuda_fail(e, "DHT stream");
+    ncclResult_t ar = ncclSuccess;
+    ncclCommGetAsyncError(dht->comm, &ar);
+    if (ar != ncclSuccess && ar != ncclInProgress) {
+      ncclCommAbort(dht->comm);
+      dht->comm = nullptr;
+      return fail(CB_ERR_NCCL, "DHT collective failed: %s", ncclGetErrorString(ar));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > dht->timeout_s) {
+      ncclCommAbort(dht->comm);
+      dht->comm = nullptr;
+      return fail(CB_ERR_TIMEOUT, "DHT collective timed out");
+    }
+    std::this_thread::yield();
+  }
+  return CB_OK;
 }
-int Store::dht_contains(const uint8_t *, int, uint8_t *, cudaStream_t) {
-  return fail(CB_ERR_STATE, "multi-GPU DHT not available in this build");
+
+// All-gather of the per-destination counts: on return rcount[r] = number of
+// records rank r sends to this rank.
+int Store::dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st) {
+  const int W = dht->W;
+  CB_TRY_CUDA(dht->h_misc.ensure(4ull * W * (W + 1)), "pinned");
+  CB_TRY_CUDA(dht->d_misc.ensure(4ull * W * (W + 1)), "device");
+  uint32_t *h = static_cast<uint32_t *>(dht->h_misc.ptr);
+  uint32_t *d = static_cast<uint32_t *>(dht->d_misc.ptr);
+  memcpy(h, scount, 4ull * W);
+  CB_TRY_CUDA(cudaMemcpyAsync(d, h, 4ull * W, cudaMemcpyHostToDevice, st), "H2D counts");
+  int rc = dht_nccl(ncclAllGather(d, d + W, (size_t)W, ncclUint32, dht->comm, st), "ncclAllGather(counts)");
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(h + W, d + W, 4ull * W * W, cudaMemcpyDeviceToHost, st), "D2H counts");
+  rc = dht_sync(st);
+  if (rc) return rc;
+  for (int r = 0; r < W; ++r) rcount[r] = h[W + r * W + dht->me];
+  return CB_OK;
 }
-int Store::dht_cluster_usage(cb_stats *) { return CB_OK; }
+
+// Variable all-to-all of fixed-size records (grouped ncclSend/ncclRecv).
+int Store::dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount,
+                         size_t rec, cudaStream_t st) {
+  const int W = dht->W;
+  int rc = dht_nccl(ncclGroupStart(), "ncclGroupStart");
+  if (rc) return rc;
+  size_t so = 0, ro = 0;
+  for (int r = 0; r < W; ++r) {
+    if (scount[r]) {
+      rc = dht_nccl(ncclSend(static_cast<const uint8_t *>(d_send) + so, scount[r] * rec, ncclUint8, r, dht->comm, st),
+                    "ncclSend");
+      if (rc) return rc;
+    }
+    if (rcount[r]) {
+      rc = dht_nccl(ncclRecv(static_cast<uint8_t *>(d_recv) + ro, rcount[r] * rec, ncclUint8, r, dht->comm, st),
+                    "ncclRecv");
+      if (rc) return rc;
+    }
+    so += scount[r] * rec;
+    ro += rcount[r] * rec;
+  }
+  return dht_nccl(ncclGroupEnd(), "ncclGroupEnd");
+}
+
+int Store::dht_barrier() {
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
+  int rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, own_stream),
+                    "ncclAllReduce(barrier)");
+  if (rc) return rc;
+  return dht_sync(own_stream);
+}
+
+// ------------------------------------------------------------ attach
+
+int Store::dht_attach(int r, int W, const uint8_t *uid) {
+  if (world > 1 || dht) return fail(CB_ERR_STATE, "already attached to a DHT");
+  if (W < 2 || r < 0 || r >= W) return fail(CB_ERR_ARG, "bad rank/world");
+  if (!pool) return fail(CB_ERR_STATE, "a DHT member needs an HBM pool (gpu_capacity_bytes > 0)");
+  // The index is mapped by peers: size it once, it is never reallocated.
+  const int want_log2 = std::max(cfg.index_log2 > 0 ? cfg.index_log2 : 16, 20);
+  if (table_slots < (1ull << want_log2)) {
+    int rc = CB_OK;
+    if (policy.size() == 0) {
+      CB_TRY_CUDA(alloc_table(1ull << want_log2), "index");
+    } else {
+      rc = reserve_index((1ull << want_log2) / 2, own_stream);
+      if (rc) return rc;
+    }
+  }
+  dht = new DhtState;
+  dht->W = W;
+  dht->me = r;
+  ncclUniqueId id;
+  memcpy(&id, uid, sizeof id);
+  ncclConfig_t nc = NCCL_CONFIG_INITIALIZER;
+  nc.blocking = 0;
+  int rc = dht_nccl(ncclCommInitRankConfig(&dht->comm, W, id, r, &nc), "ncclCommInitRankConfig");
+  if (rc) {
+    delete dht;
+    dht = nullptr;
+    return rc;
+  }
+  Export ex;
+  memset(&ex, 0, sizeof ex);
+  CB_TRY_CUDA(cudaIpcGetMemHandle(&ex.pool, pool), "cudaIpcGetMemHandle(pool)");
+  CB_TRY_CUDA(cudaIpcGetMemHandle(&ex.table, table), "cudaIpcGetMemHandle(index)");
+  ex.pool_bytes = pool_bytes;
+  ex.table_slots = table_slots;
+  ex.device = device;
+  CB_TRY_CUDA(dht->h_misc.ensure(sizeof(Export) * (W + 1)), "pinned");
+  CB_TRY_CUDA(dht->d_misc.ensure(sizeof(Export) * (W + 1)), "device");
+  uint8_t *h = static_cast<uint8_t *>(dht->h_misc.ptr);
+  uint8_t *d = static_cast<uint8_t *>(dht->d_misc.ptr);
+  memcpy(h, &ex, sizeof ex);
+  CB_TRY_CUDA(cudaMemcpyAsync(d, h, sizeof ex, cudaMemcpyHostToDevice, own_stream), "H2D export");
+  rc = dht_nccl(ncclAllGather(d, d + sizeof(Export), sizeof(Export), ncclUint8, dht->comm, own_stream),
+                "ncclAllGather(exports)");
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(h + sizeof(Export), d + sizeof(Export), sizeof(Export) * W, cudaMemcpyDeviceToHost,
+                              own_stream),
+              "D2H exports");
+  rc = dht_sync(own_stream);
+  if (rc) return rc;
+  dht->pool.assign(W, 0);
+  dht->pool_bytes.assign(W, 0);
+  dht->table.assign(W, 0);
+  dht->slots.assign(W, 0);
+  dht->device.assign(W, -1);
+  for (int p = 0; p < W; ++p) {
+    Export e;
+    memcpy(&e, h + sizeof(Export) * (p + 1), sizeof e);
+    dht->pool_bytes[p] = e.pool_bytes;
+    dht->slots[p] = e.table_slots;
+    dht->device[p] = e.device;
+    if (p == r) {
+      dht->pool[p] = (uint64_t)pool;
+      dht->table[p] = (uint64_t)table;
+      continue;
+    }
+    void *pp = nullptr, *pt = nullptr;
+    CB_TRY_CUDA(cudaIpcOpenMemHandle(&pp, e.pool, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(pool)");
+    dht->opened.push_back(pp);
+    CB_TRY_CUDA(cudaIpcOpenMemHandle(&pt, e.table, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(index)");
+    dht->opened.push_back(pt);
+    dht->pool[p] = (uint64_t)pp;
+    dht->table[p] = (uint64_t)pt;
+  }
+  rank = r;
+  world = W;
+  policy.set_direct_dram_placement(false);
+  return CB_OK;
+}
+
+void Store::dht_detach() {
+  if (!dht) return;
+  if (dht->comm) {
+    ncclCommAbort(dht->comm);  // no collective on the way out: peers may be gone
+    dht->comm = nullptr;
+  }
+  for (void *p : dht->opened) cudaIpcCloseMemHandle(p);
+  dht->d_send.release();
+  dht->d_recv.release();
+  dht->d_misc.release();
+  dht->h_send.release();
+  dht->h_recv.release();
+  dht->h_misc.release();
+  delete dht;
+  dht = nullptr;
+}
+
+// ------------------------------------------------------------ put
+
+int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                   const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out, uint8_t *status_out,
+                   cudaStream_t st) {
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  const int W = dht->W, me = dht->me;
+  // 0. device addresses of the blocks (host blocks: one staging area)
+  std::vector<uint64_t> dptr(n);
+  if (mem_kind == CB_MEM_HOST) {
+    uint64_t total = 0;
+    for (int i = 0; i < n; ++i) total += align_up(sizes[i], 256);
+    CB_TRY_CUDA(d_staging.ensure(std::max<uint64_t>(total, 256)), "device staging");
+    uint64_t off = 0;
+    for (int i = 0; i < n; ++i) {
+      dptr[i] = (uint64_t)d_staging.ptr + off;
+      if (sizes[i])
+        CB_TRY_CUDA(cudaMemcpyAsync(reinterpret_cast<void *>(dptr[i]), ptrs[i], sizes[i], cudaMemcpyHostToDevice, st),
+                    "H2D block");
+      off += align_up(sizes[i], 256);
+    }
+  } else {
+    for (int i = 0; i < n; ++i) dptr[i] = (uint64_t)ptrs[i];
+  }
+  // 1. keys
+  std::vector<HKey> keys(n);
+  if (keys_in) {
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(keys_in + 16 * i);
+  } else if (n) {
+    int rc = hash_device(dptr.data(), sizes, n, st);
+    if (rc) return rc;
+    const uint8_t *dig = static_cast<const uint8_t *>(h_out.ptr);
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32 * i);
+  }
+  // 2. bucket by owner (batch order inside each bucket)
+  std::vector<uint32_t> scount(W, 0), rcount(W, 0);
+  std::vector<int> order(n);
+  for (int i = 0; i < n; ++i) scount[be_owner(keys[i], W)]++;
+  {
+    std::vector<uint32_t> pos(W, 0);
+    for (int r = 1; r < W; ++r) pos[r] = pos[r - 1] + scount[r - 1];
+    for (int i = 0; i < n; ++i) order[pos[be_owner(keys[i], W)]++] = i;
+  }
+  int rc = dht_counts(scount.data(), rcount.data(), st);
+  if (rc) return rc;
+  uint32_t nrecv = 0;
+  for (int r = 0; r < W; ++r) nrecv += rcount[r];
+  // 3. requests to owners
+  CB_TRY_CUDA(dht->h_send.ensure(sizeof(PutReq) * std::max(n, 1)), "pinned");
+  CB_TRY_CUDA(dht->d_send.ensure(sizeof(PutReq) * std::max(n, 1)), "device");
+  CB_TRY_CUDA(dht->h_recv.ensure(sizeof(PutReq) * std::max<uint32_t>(nrecv, 1)), "pinned");
+  CB_TRY_CUDA(dht->d_recv.ensure(sizeof(PutReq) * std::max<uint32_t>(nrecv, 1)), "device");
+  PutReq *sreq = static_cast<PutReq *>(dht->h_send.ptr);
+  for (int j = 0; j < n; ++j) {
+    const int i = order[j];
+    sreq[j] = PutReq{keys[i].lo, keys[i].hi, sizes[i], (is_prefix && is_prefix[i]) ? 1ull : 0ull};
+  }
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->d_send.ptr, sreq, sizeof(PutReq) * n, cudaMemcpyHostToDevice, st), "H2D req");
+  rc = dht_alltoallv(dht->d_send.ptr, scount.data(), dht->d_recv.ptr, rcount.data(), sizeof(PutReq), st);
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->h_recv.ptr, dht->d_recv.ptr, sizeof(PutReq) * nrecv, cudaMemcpyDeviceToHost, st),
+              "D2H req");
+  rc = dht_sync(st);
+  if (rc) return rc;
+  // 4. owner: sequential dedup + placement in (source rank, index) order
+  const PutReq *rreq = static_cast<const PutReq *>(dht->h_recv.ptr);
+  std::vector<HKey> okeys(nrecv);
+  std::vector<uint64_t> osizes(nrecv);
+  std::vector<uint8_t> oprefix(nrecv);
+  for (uint32_t j = 0; j < nrecv; ++j) {
+    okeys[j] = HKey{rreq[j].klo, rreq[j].khi};
+    osizes[j] = rreq[j].size;
+    oprefix[j] = (uint8_t)(rreq[j].flags & 1);
+  }
+  rc = reserve_index(nrecv, st);
+  if (rc) return rc;
+  PutPlan &plan = put_plan;
+  policy.plan_put(okeys.data(), osizes.data(), oprefix.data(), (int)nrecv, cfg.dedup_enabled != 0, plan);
+  rc = run_moves(plan.moves, plan.dropped, st);
+  if (rc) {
+    policy.commit();
+    return rc;
+  }
+  std::vector<PutRep> reps(nrecv);
+  for (uint32_t j = 0; j < nrecv; ++j) reps[j] = PutRep{0, plan.status[j], 0};
+  std::vector<IndexRec> ins;
+  ins.reserve(plan.places.size());
+  for (const Placement &p : plan.places) {
+    const uint64_t loc = p.off | (p.tier == kTierDram ? kLocDram : 0);
+    reps[p.idx].loc = loc;
+    ins.push_back(IndexRec{p.key.lo, p.key.hi, loc, (p.size & kSizeMask) | (p.prefix ? kMetaPrefix : 0)});
+  }
+  policy.commit();
+  // replies reuse the request buffers (PutRep <= PutReq)
+  memcpy(dht->h_recv.ptr, reps.data(), sizeof(PutRep) * nrecv);
+  if (!ins.empty()) {
+    CB_TRY_CUDA(h_scratch.ensure(sizeof(IndexRec) * ins.size()), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(sizeof(IndexRec) * ins.size()), "device");
+    memcpy(h_scratch.ptr, ins.data(), sizeof(IndexRec) * ins.size());
+    CB_TRY_CUDA(cudaMemcpyAsync(d_scratch.ptr, h_scratch.ptr, sizeof(IndexRec) * ins.size(), cudaMemcpyHostToDevice,
+                                st),
+                "H2D index");
+    CB_TRY_CUDA(launch_index_insert(table, table_slots - 1, static_cast<const IndexRec *>(d_scratch.ptr),
+                                    (int)ins.size(), d_err, st),
+                "index insert");
+    launches++;
+    table_used += ins.size();
+  }
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->d_recv.ptr, dht->h_recv.ptr, sizeof(PutRep) * nrecv, cudaMemcpyHostToDevice, st),
+              "H2D rep");
+  // 5. replies back to the writers
+  rc = dht_alltoallv(dht->d_recv.ptr, rcount.data(), dht->d_send.ptr, scount.data(), sizeof(PutRep), st);
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->h_send.ptr, dht->d_send.ptr, sizeof(PutRep) * n, cudaMemcpyDeviceToHost, st),
+              "D2H rep");
+  rc = dht_sync(st);
+  if (rc) return rc;
+  // 6. writers copy new blocks into the owners' pools
+  std::vector<PutRep> mine(static_cast<const PutRep *>(dht->h_send.ptr), static_cast<const PutRep *>(dht->h_send.ptr) + n);
+  std::vector<CopyDesc> desc;
+  std::vector<uint32_t> us;
+  uint32_t total = 0;
+  uint64_t bytes = 0;
+  std::vector<uint8_t> status(n, CB_PUT_FAILED);
+  for (int j = 0; j < n; ++j) {
+    const int i = order[j];
+    const int owner = (int)be_owner(keys[i], W);
+    status[i] = (uint8_t)mine[j].status;
+    if (mine[j].status == CB_PUT_DEDUP) {
+      remote_dedup_hits += cfg.dedup_enabled ? 1 : 0;
+      remote_dedup_bytes += cfg.dedup_enabled ? sizes[i] : 0;
+    }
+    if (mine[j].status != CB_PUT_STORED || !sizes[i]) continue;
+    if (mine[j].loc & kLocDram) {  // only owner-local DRAM placements are reachable
+      status[i] = CB_PUT_FAILED;
+      continue;
+    }
+    const uint64_t dst = dht->pool[owner] + (mine[j].loc & kLocOffMask);
+    us.push_back(total);
+    desc.push_back(CopyDesc{dptr[i], dst, sizes[i], owner == me ? 0u : 1u});
+    total += (uint32_t)((sizes[i] + kCopyUnit - 1) / kCopyUnit);
+    bytes += sizes[i];
+  }
+  if (!desc.empty()) {
+    us.push_back(total);
+    const size_t o_us = align_up(sizeof(CopyDesc) * desc.size(), 256);
+    const size_t need = o_us + 4 * us.size();
+    CB_TRY_CUDA(h_scratch.ensure(need), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(need), "device");
+    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    memcpy(h, desc.data(), sizeof(CopyDesc) * desc.size());
+    memcpy(h + o_us, us.data(), 4 * us.size());
+    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, need, cudaMemcpyHostToDevice, st), "H2D scatter");
+    const int nd = (int)desc.size();
+    CB_TRY_CUDA(timed(1, bytes, st,
+                      [&] {
+                        // peer stores: the LSU engine keeps far more bytes in
+                        // flight than one TMA lane per SM can for plain stores
+                        return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d),
+                                                 reinterpret_cast<const uint32_t *>(d + o_us), nd, total, 2, d_err,
+                                                 num_sms, st);
+                      }),
+                "scatter");
+  }
+  // 7. closing barrier: every writer's copies precede every later op
+  CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
+  rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
+                "ncclAllReduce(put barrier)");
+  if (rc) return rc;
+  rc = dht_sync(st);
+  if (rc) return rc;
+  rc = check_device_error(st);
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) {
+    if (keys_out) memcpy(keys_out + 16 * i, &keys[i], 16);
+    if (status_out) status_out[i] = status[i];
+  }
+  return CB_OK;
+}
+
+// ------------------------------------------------------------ lookup
+
+// Sends keys to their owners, runs the owner lookup kernel, returns for each
+// key (in the caller's order) {location, meta} in reps (host) and the owner.
+int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, std::vector<int> &owner,
+                      cudaStream_t st) {
+  const int W = dht->W;
+  std::vector<uint32_t> scount(W, 0), rcount(W, 0);
+  std::vector<int> order(n);
+  owner.assign(n, 0);
+  for (int i = 0; i < n; ++i) {
+    owner[i] = (int)be_owner(to_hkey(keys + 16 * i), W);
+    scount[owner[i]]++;
+  }
+  {
+    std::vector<uint32_t> pos(W, 0);
+    for (int r = 1; r < W; ++r) pos[r] = pos[r - 1] + scount[r - 1];
+    for (int i = 0; i < n; ++i) order[pos[owner[i]]++] = i;
+  }
+  int rc = dht_counts(scount.data(), rcount.data(), st);
+  if (rc) return rc;
+  uint32_t nrecv = 0;
+  for (int r = 0; r < W; ++r) nrecv += rcount[r];
+  const size_t smax = std::max<size_t>(n, 1), rmax = std::max<size_t>(nrecv, 1);
+  CB_TRY_CUDA(dht->h_send.ensure(16 * smax), "pinned");
+  CB_TRY_CUDA(dht->d_send.ensure(16 * smax), "device");
+  CB_TRY_CUDA(dht->h_recv.ensure(16 * rmax), "pinned");
+  CB_TRY_CUDA(dht->d_recv.ensure(16 * rmax + 16 * rmax), "device");
+  uint8_t *hs = static_cast<uint8_t *>(dht->h_send.ptr);
+  for (int j = 0; j < n; ++j) memcpy(hs + 16 * j, keys + 16 * order[j], 16);
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->d_send.ptr, hs, 16ull * n, cudaMemcpyHostToDevice, st), "H2D keys");
+  uint8_t *rk = static_cast<uint8_t *>(dht->d_recv.ptr);  // received keys
+  uint64_t *rr = reinterpret_cast<uint64_t *>(rk + 16 * rmax);  // replies
+  rc = dht_alltoallv(dht->d_send.ptr, scount.data(), rk, rcount.data(), 16, st);
+  if (rc) return rc;
+  CB_TRY_CUDA(launch_index_serve(table, table_slots - 1, reinterpret_cast<const Key *>(rk), (int)nrecv, rr, st),
+              "index serve");
+  launches++;
+  // keys this owner served, for its LRU order (read after the sync below)
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->h_recv.ptr, rk, 16ull * nrecv, cudaMemcpyDeviceToHost, st), "D2H served keys");
+  rc = dht_alltoallv(rr, rcount.data(), dht->d_send.ptr, scount.data(), 16, st);
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(hs, dht->d_send.ptr, 16ull * n, cudaMemcpyDeviceToHost, st), "D2H replies");
+  rc = dht_sync(st);
+  if (rc) return rc;
+  const uint8_t *served = static_cast<const uint8_t *>(dht->h_recv.ptr);
+  for (uint32_t j = 0; j < nrecv; ++j) policy.touch(to_hkey(served + 16 * j));
+  reps.assign(2ull * n, 0);
+  const uint64_t *hr = reinterpret_cast<const uint64_t *>(hs);
+  for (int j = 0; j < n; ++j) {
+    reps[2ull * order[j]] = hr[2ull * j];
+    reps[2ull * order[j] + 1] = hr[2ull * j + 1];
+  }
+  return CB_OK;
+}
+
+int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps, int mem_kind,
+                   uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  const int me = dht->me;
+  std::vector<uint64_t> reps;
+  std::vector<int> owner;
+  int rc = dht_lookup(keys, n, reps, owner, st);
+  if (rc) return rc;
+  // host outputs: gather into staging, then DMA out
+  std::vector<uint64_t> dst(n);
+  if (mem_kind == CB_MEM_HOST) {
+    uint64_t total = 0;
+    for (int i = 0; i < n; ++i) {
+      const uint64_t sz = reps[2ull * i + 1] & kSizeMask;
+      total += (reps[2ull * i + 1] && sz <= caps[i]) ? align_up(sz, 256) : 0;
+    }
+    CB_TRY_CUDA(d_staging.ensure(std::max<uint64_t>(total, 256)), "device staging");
+    uint64_t off = 0;
+    for (int i = 0; i < n; ++i) {
+      const uint64_t sz = reps[2ull * i + 1] & kSizeMask;
+      dst[i] = (uint64_t)d_staging.ptr + off;
+      off += (reps[2ull * i + 1] && sz <= caps[i]) ? align_up(sz, 256) : 0;
+    }
+  } else {
+    for (int i = 0; i < n; ++i) dst[i] = (uint64_t)outs[i];
+  }
+  std::vector<CopyDesc> desc;
+  std::vector<uint32_t> us;
+  uint32_t total = 0;
+  uint64_t bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    const uint64_t meta = reps[2ull * i + 1], loc = reps[2ull * i];
+    const uint64_t sz = meta & kSizeMask;
+    const bool dram = (loc & kLocDram) != 0;
+    const bool local = owner[i] == me;
+    sizes_out[i] = 0;
+    if (!(meta & kMetaOccupied)) {
+      found_out[i] = CB_FOUND_MISS;
+      misses++;
+      continue;
+    }
+    sizes_out[i] = sz;
+    found_out[i] = dram ? (local ? CB_FOUND_LOCAL_DRAM : CB_FOUND_REMOTE_DRAM)
+                        : (local ? CB_FOUND_LOCAL_HBM : CB_FOUND_REMOTE_HBM);
+    if (local && !dram) local_gpu_hits++;
+    if (local && dram) local_dram_hits++;
+    if (!local && !dram) remote_gpu_hits++;
+    if (!local && dram) remote_dram_hits++;
+    if (sz > caps[i] || (dram && !local)) {  // too small, or a peer's pinned DRAM (not mapped here)
+      found_out[i] |= CB_FOUND_NOT_COPIED;
+      continue;
+    }
+    if (!sz) continue;
+    const uint64_t off = loc & kLocOffMask;
+    const uint64_t src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
+    us.push_back(total);
+    // peer and pinned-host sources are read with plain (coherent) loads
+    desc.push_back(CopyDesc{src, dst[i], sz, (dram || !local) ? 1u : 0u});
+    total += (uint32_t)((sz + kCopyUnit - 1) / kCopyUnit);
+    bytes += sz;
+  }
+  if (!desc.empty()) {
+    us.push_back(total);
+    const size_t o_us = align_up(sizeof(CopyDesc) * desc.size(), 256);
+    const size_t need = o_us + 4 * us.size();
+    CB_TRY_CUDA(h_scratch.ensure(need), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(need), "device");
+    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    memcpy(h, desc.data(), sizeof(CopyDesc) * desc.size());
+    memcpy(h + o_us, us.data(), 4 * us.size());
+    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, need, cudaMemcpyHostToDevice, st), "H2D gather");
+    const int nd = (int)desc.size();
+    CB_TRY_CUDA(timed(2, bytes, st,
+                      [&] {
+                        // many warps per SM keep enough peer loads in flight
+                        return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d),
+                                                 reinterpret_cast<const uint32_t *>(d + o_us), nd, total, 2, d_err,
+                                                 num_sms, st);
+                      }),
+                "gather");
+  }
+  // owners must not reuse pool extents before every reader is done
+  CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
+  rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
+                "ncclAllReduce(get barrier)");
+  if (rc) return rc;
+  if (mem_kind == CB_MEM_HOST) {
+    for (int i = 0; i < n; ++i) {
+      if ((found_out[i] & 0x0f) == CB_FOUND_MISS || (found_out[i] & CB_FOUND_NOT_COPIED) || !sizes_out[i]) continue;
+      CB_TRY_CUDA(cudaMemcpyAsync(outs[i], reinterpret_cast<void *>(dst[i]), sizes_out[i], cudaMemcpyDeviceToHost, st),
+                  "D2H block");
+    }
+  }
+  rc = dht_sync(st);
+  if (rc) return rc;
+  return check_device_error(st);
+}
+
+int Store::dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st) {
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  std::vector<uint64_t> reps;
+  std::vector<int> owner;
+  int rc = dht_lookup(keys, n, reps, owner, st);
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) found_out[i] = (reps[2ull * i + 1] & kMetaOccupied) ? 1 : 0;
+  return CB_OK;
+}
+
+// One-sided probe of the owner's index through its peer mapping (locate is
+// not collective in the reference either: it reads local metadata).
+int Store::dht_locate(const uint8_t *key, cb_location *out, int32_t *found) {
+  if (!dht) return fail(CB_ERR_STATE, "DHT not attached");
+  const HKey k = to_hkey(key);
+  const int o = (int)be_owner(k, dht->W);
+  CB_TRY_CUDA(h_scratch.ensure(64), "pinned");
+  CB_TRY_CUDA(d_scratch.ensure(64), "device");
+  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  memcpy(h, key, 16);
+  CB_TRY_CUDA(cudaMemcpyAsync(d, h, 16, cudaMemcpyHostToDevice, own_stream), "H2D key");
+  CB_TRY_CUDA(launch_index_serve(reinterpret_cast<const Slot *>(dht->table[o]), dht->slots[o] - 1,
+                                 reinterpret_cast<const Key *>(d), 1, reinterpret_cast<uint64_t *>(d + 16), own_stream),
+              "index probe");
+  launches++;
+  CB_TRY_CUDA(cudaMemcpyAsync(h + 16, d + 16, 16, cudaMemcpyDeviceToHost, own_stream), "D2H probe");
+  CB_TRY_CUDA(cudaStreamSynchronize(own_stream), "probe");
+  uint64_t loc, meta;
+  memcpy(&loc, h + 16, 8);
+  memcpy(&meta, h + 24, 8);
+  memset(out, 0, sizeof *out);
+  *found = (meta & kMetaOccupied) ? 1 : 0;
+  if (!*found) return CB_OK;
+  out->node_id = o;
+  out->is_gpu = (loc & kLocDram) ? 0 : 1;
+  out->gpu_id = out->is_gpu ? dht->device[o] : -1;
+  out->offset = loc & kLocOffMask;
+  out->size = meta & kSizeMask;
+  out->is_prefix = (meta & kMetaPrefix) ? 1 : 0;
+  return CB_OK;
+}
+
+int Store::dht_cluster_usage(cb_stats *o) {
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  CB_TRY_CUDA(dht->h_misc.ensure(64), "pinned");
+  CB_TRY_CUDA(dht->d_misc.ensure(64), "device");
+  uint64_t *h = static_cast<uint64_t *>(dht->h_misc.ptr);
+  h[0] = o->local_gpu_used;
+  h[1] = o->local_dram_used;
+  CB_TRY_CUDA(cudaMemcpyAsync(dht->d_misc.ptr, h, 16, cudaMemcpyHostToDevice, own_stream), "H2D usage");
+  int rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 2, ncclUint64, ncclSum, dht->comm, own_stream),
+                    "ncclAllReduce(usage)");
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(h, dht->d_misc.ptr, 16, cudaMemcpyDeviceToHost, own_stream), "D2H usage");
+  rc = dht_sync(own_stream);
+  if (rc) return rc;
+  o->cluster_gpu_used = h[0];
+  o->cluster_dram_used = h[1];
+  return CB_OK;
+}
 
 }  // namespace cb
 
 extern "C" {
-int cb_dht_unique_id(uint8_t *) { return CB_ERR_STATE; }
-int cb_dht_attach(cb_store *, int32_t, int32_t, const uint8_t *) { return CB_ERR_STATE; }
-int cb_dht_barrier(cb_store *) { return CB_OK; }
+
+int cb_dht_unique_id(uint8_t *uid_out) {
+  if (!uid_out) return CB_ERR_ARG;
+  ncclUniqueId id;
+  if (ncclGetUniqueId(&id) != ncclSuccess) return CB_ERR_NCCL;
+  memcpy(uid_out, &id, sizeof id);
+  return CB_OK;
 }
+
+}  // extern "C"

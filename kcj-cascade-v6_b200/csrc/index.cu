@@ -126,6 +126,30 @@ __global__ void index_lookup_kernel(LookupArgs a) {
   a.res[i] = res;
 }
 
+// Owner side of a DHT lookup: for each received key, its slot's location
+// and meta words (meta = 0 when absent). `table` may be a peer's index
+// mapped into this process (one-sided probes).
+__global__ void index_serve_kernel(const Slot *table, uint64_t mask, const Key *__restrict__ keys, int n,
+                                   uint64_t *__restrict__ reps) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const Key k = keys[i];
+  const uint64_t h = slot_hash(k);
+  uint64_t loc = 0, meta = 0;
+  for (uint64_t probe = 0; probe <= mask; ++probe) {
+    const Slot *s = &table[(h + probe) & mask];
+    const uint64_t m = load_meta(s);
+    if (m == 0) break;
+    if ((m & kMetaOccupied) && s->klo == k.lo && s->khi == k.hi) {
+      loc = s->loc;
+      meta = m;
+      break;
+    }
+  }
+  reps[2 * i] = loc;
+  reps[2 * i + 1] = meta;
+}
+
 inline int blocks_for(int n) { return (n + kThreads - 1) / kThreads; }
 
 }  // namespace
@@ -148,6 +172,13 @@ cudaError_t launch_index_erase(Slot *table, uint64_t mask, const IndexRec *recs,
                                unsigned *d_err, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   index_erase_kernel<<<blocks_for(n), kThreads, 0, stream>>>(table, mask, recs, n, d_err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_index_serve(const Slot *table, uint64_t mask, const Key *keys, int n, uint64_t *reps,
+                               cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  index_serve_kernel<<<blocks_for(n), kThreads, 0, stream>>>(table, mask, keys, n, reps);
   return cudaGetLastError();
 }
 

@@ -52,4 +52,9 @@ struct LookupArgs {
 };
 cudaError_t launch_index_lookup(const LookupArgs &a, cudaStream_t stream);
 
+// DHT owner lookup: reps[2i] = location word, reps[2i+1] = meta word
+// (0 when the key is absent).
+cudaError_t launch_index_serve(const Slot *table, uint64_t mask, const Key *keys, int n, uint64_t *reps,
+                               cudaStream_t stream);
+
 }  // namespace cb

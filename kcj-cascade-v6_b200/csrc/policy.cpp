@@ -226,7 +226,7 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
     if (make_hbm_room(size, plan.moves, plan.dropped)) {
       off = hbm_.alloc(size);
     }
-    if (off == UINT64_MAX) {
+    if (off == UINT64_MAX && direct_dram_) {
       // Larger than the whole HBM pool (or every HBM block pending): the
       // reference's put still succeeds through its DRAM copy
       // (distributed_backend.cpp:643-652).

@@ -149,6 +149,9 @@ class Policy {
   const PolicyCounters &counters() const { return ctr_; }
   void reset_counters() { ctr_ = PolicyCounters{}; }
   const ExtentAllocator &hbm_alloc() const { return hbm_; }
+  // When false, a new block that cannot get HBM fails instead of landing in
+  // the DRAM tier (DHT mode: remote writers can only reach HBM pools).
+  void set_direct_dram_placement(bool on) { direct_dram_ = on; }
   template <class F>
   void for_each(F f) const {
     for (const auto &kv : map_) f(kv.first, kv.second);
@@ -163,6 +166,7 @@ class Policy {
 
   uint64_t hbm_cap_, dram_cap_;
   bool semantic_;
+  bool direct_dram_ = true;
   ExtentAllocator hbm_, dram_;
   uint64_t hbm_used_ = 0, dram_used_ = 0;  // logical bytes (reference used_)
   std::unordered_map<HKey, BlockMeta, HKeyHash> map_;

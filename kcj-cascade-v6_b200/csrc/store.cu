@@ -170,6 +170,12 @@ cudaError_t Store::ensure_dram() {
 int Store::reserve_index(uint64_t incoming, cudaStream_t st) {
   const uint64_t live = policy.size();
   if ((table_used + table_tombs + incoming) * 2 <= table_slots) return CB_OK;
+  if (dht) {
+    // Peers map this index: it is never reallocated while attached.
+    if ((live + incoming) <= table_slots - table_slots / 8) return CB_OK;
+    return fail(CB_ERR_NOSPACE, "device index full (%llu slots); raise index_log2",
+                (unsigned long long)table_slots);
+  }
   uint64_t slots = table_slots;
   while ((live + incoming) * 2 > slots) slots *= 2;
   CB_TRY(cudaStreamSynchronize(st), "sync before index rebuild");
@@ -625,11 +631,17 @@ int Store::evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st) {
 
 int Store::clear(cudaStream_t st) {
   CB_TRY(cudaStreamSynchronize(st), "sync");
+  if (dht) {  // collective, like DistributedStore::clear (barrier before and after)
+    int rc = dht_barrier();
+    if (rc) return rc;
+  }
   policy.clear();
   CB_TRY(cudaMemsetAsync(table, 0, table_slots * sizeof(Slot), st), "index clear");
   CB_TRY(cudaStreamSynchronize(st), "sync");
   table_used = table_tombs = 0;
   local_gpu_hits = local_dram_hits = remote_gpu_hits = remote_dram_hits = misses = 0;
+  remote_dedup_hits = remote_dedup_bytes = 0;
+  if (dht) return dht_barrier();
   return CB_OK;
 }
 
@@ -645,8 +657,10 @@ void Store::fill_stats(cb_stats *o) const {
   o->remote_gpu_hits = remote_gpu_hits;
   o->remote_dram_hits = remote_dram_hits;
   o->misses = misses;
-  o->dedup_hits = c.dedup_hits + remote_dedup_hits;
-  o->dedup_bytes_saved = c.dedup_bytes_saved + remote_dedup_bytes;
+  // Dedup hits belong to the rank that put the block (like the reference's
+  // per-rank counters); in a DHT the owner's policy sees other ranks' puts.
+  o->dedup_hits = dht ? remote_dedup_hits : c.dedup_hits;
+  o->dedup_bytes_saved = dht ? remote_dedup_bytes : c.dedup_bytes_saved;
   o->gpu_evictions = c.gpu_evictions;
   o->dram_evictions = c.dram_evictions;
   o->promotions_to_local = c.promotions;
@@ -799,11 +813,12 @@ int cb_put_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, co
                  uint8_t *status_out, void *stream) {
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && (!ptrs || !sizes))) return s->fail(CB_ERR_ARG, "bad arguments");
-    if (n == 0) return CB_OK;
     for (int i = 0; i < n; ++i)
       if (sizes[i] > cb::kSizeMask) return s->fail(CB_ERR_ARG, "block %d too large", i);
     cudaStream_t st = pick_stream(s, stream);
+    // DHT calls are collective: a rank with nothing to put still takes part.
     if (s->world > 1) return s->dht_put(ptrs, sizes, is_prefix, keys_in, n, mem_kind, keys_out, status_out, st);
+    if (n == 0) return CB_OK;
     if (mem_kind == CB_MEM_HOST) return s->put_host(ptrs, sizes, is_prefix, keys_in, n, keys_out, status_out, st);
     std::vector<uint64_t> p(n);
     for (int i = 0; i < n; ++i) p[i] = (uint64_t)ptrs[i];
@@ -816,9 +831,9 @@ int cb_get_batch(cb_store *h, const uint8_t *keys, int32_t n, void *const *outs,
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && (!keys || !outs || !out_caps || !sizes_out || !found_out)))
       return s->fail(CB_ERR_ARG, "bad arguments");
-    if (n == 0) return CB_OK;
     cudaStream_t st = pick_stream(s, stream);
     if (s->world > 1) return s->dht_get(keys, n, outs, out_caps, mem_kind, sizes_out, found_out, st);
+    if (n == 0) return CB_OK;
     if (mem_kind == CB_MEM_HOST) return s->get_host(keys, n, outs, out_caps, sizes_out, found_out, st);
     std::vector<uint64_t> o(n);
     for (int i = 0; i < n; ++i) o[i] = (uint64_t)outs[i];
@@ -838,6 +853,7 @@ int cb_contains_batch(cb_store *h, const uint8_t *keys, int32_t n, uint8_t *foun
 int cb_locate(cb_store *h, const uint8_t *key, cb_location *out, int32_t *found) {
   return guarded(h, [&](Store *s) -> int {
     if (!key || !out || !found) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (s->dht) return s->dht_locate(key, out, found);
     const cb::BlockMeta *m = s->policy.find(cb::to_hkey(key));
     *found = m ? 1 : 0;
     memset(out, 0, sizeof *out);
@@ -875,6 +891,23 @@ int cb_sync(cb_store *h) {
     if (e != cudaSuccess) return s->cuda_fail(e, "sync");
     return CB_OK;
   });
+}
+
+int cb_dht_attach(cb_store *h, int32_t rank, int32_t world, const uint8_t *uid) {
+  return guarded(h, [&](Store *s) -> int {
+    if (!uid) return s->fail(CB_ERR_ARG, "bad arguments");
+    return s->dht_attach(rank, world, uid);
+  });
+}
+
+int cb_dht_barrier(cb_store *h) {
+  return guarded(h, [&](Store *s) -> int { return s->world > 1 ? s->dht_barrier() : CB_OK; });
+}
+
+int32_t cb_owner_rank(const uint8_t *key, int32_t world) {
+  if (!key || world <= 0) return -1;
+  const cb::HKey k = cb::to_hkey(key);
+  return cb::owner_of(cb::Key{k.lo, k.hi}, world);
 }
 
 int cb_rank(const cb_store *h, int32_t *rank, int32_t *world) {

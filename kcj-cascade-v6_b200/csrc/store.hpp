@@ -11,6 +11,13 @@
 #include "common.cuh"
 #include "policy.hpp"
 
+// Returns from a Store member with CB_ERR_CUDA on a CUDA error.
+#define CB_TRY_CUDA(call, what)                          \
+  do {                                                   \
+    cudaError_t _e = (call);                             \
+    if (_e != cudaSuccess) return cuda_fail(_e, what);   \
+  } while (0)
+
 namespace cb {
 
 struct PinnedBuf {
@@ -126,6 +133,14 @@ struct Store {
   int dht_attach(int rank, int world, const uint8_t *uid);
   void dht_detach();
   int dht_barrier();
+  int dht_nccl(int nccl_result, const char *what);
+  int dht_sync(cudaStream_t st);
+  int dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st);
+  int dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount, size_t rec,
+                    cudaStream_t st);
+  int dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, std::vector<int> &owner,
+                 cudaStream_t st);
+  int dht_locate(const uint8_t *key, cb_location *out, int32_t *found);
   int dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
               const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out,
               uint8_t *status_out, cudaStream_t st);

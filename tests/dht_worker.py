@@ -1,0 +1,102 @@
+"""One rank of the multi-GPU DHT parity check (run by tests/test_gpu_dht.py
+through torch.distributed.run, one process per GPU). Exits non-zero on any
+mismatch with the DhtOracle."""
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "kcj-cascade-v6_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import cascade_cpp  # noqa: E402
+from oracle import store_oracle as O  # noqa: E402
+from oracle.dht_oracle import DhtOracle, owner  # noqa: E402
+
+
+def batches(world, seed):
+    rng = np.random.default_rng(seed)
+    sizes = [0, 1, 63, 64, 65, 4096, 65537, 917504, 300_003, 5000]
+    pool = [rng.integers(0, 256, int(sizes[i % len(sizes)]), dtype=np.uint8) for i in range(48)]
+    items = []
+    for r in range(world):
+        sel = rng.integers(0, 48, 64)
+        items.append([(int(s), bool(s % 7 == 0)) for s in sel])
+    return pool, items
+
+
+def main():
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("gloo")
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", local)
+    cfg = cascade_cpp.DistributedConfig()
+    cfg.gpu_capacity_per_device = 1 << 30
+    cfg.dram_capacity = 0
+    cfg.device = local
+    store = cascade_cpp.DistributedStore(cfg)
+    assert store.rank == rank and store.world_size == world
+
+    pool, items = batches(world, 11)
+    ids_all = [[O.block_id(pool[s]) for s, _ in items[r]] for r in range(world)]
+    ora = DhtOracle(world)
+    want_status = ora.put_round([[(ids_all[r][i], pool[s].tobytes(), pf) for i, (s, pf) in enumerate(items[r])]
+                                 for r in range(world)])
+
+    # round 1: device tensors, GPU hashing
+    blocks = [torch.from_numpy(pool[s].copy()).to(dev) for s, _ in items[rank]]
+    ids, status = store.batch_put(blocks, is_prefix=[pf for _, pf in items[rank]], return_status=True)
+    assert ids == ids_all[rank], "ids"
+    assert status == want_status[rank], ("status", status, want_status[rank])
+    st = store.get_stats()
+    assert st.dedup_hits == ora.dedup_hits[rank], ("dedup", st.dedup_hits, ora.dedup_hits[rank])
+
+    # every rank reads every stored block, shuffled, into device buffers
+    uniq = sorted({b for r in range(world) for b in ids_all[r]})
+    order = np.random.default_rng(rank).permutation(len(uniq))
+    req = [uniq[j] for j in order]
+    by_id = {O.block_id(p): p for p in pool}
+    outs = [torch.empty(len(by_id[b]), dtype=torch.uint8, device=dev) for b in req]
+    found, sizes = store.batch_get(req, outs)
+    assert all(found), "found"
+    for b, o, s in zip(req, outs, sizes):
+        assert s == len(by_id[b]) and np.array_equal(o.cpu().numpy(), by_id[b]), ("bytes", b)
+    # host-memory outputs too
+    houts = [np.empty(len(by_id[b]), np.uint8) for b in req[:20]]
+    found, sizes = store.batch_get(req[:20], houts)
+    assert all(found) and all(np.array_equal(h, by_id[b]) for h, b in zip(houts, req[:20])), "host get"
+
+    # contains / locate / miss
+    missing = "f" * 32
+    got = store.batch_get([missing], [torch.empty(16, dtype=torch.uint8, device=dev)])
+    assert got[0] == [False], "miss"
+    assert store.contains(uniq[0]) and not store.contains(missing)
+    loc = store.locate(uniq[0])
+    assert loc is not None and loc.node_id == owner(uniq[0], world) and loc.is_gpu
+    assert store.locate(missing) is None
+
+    # round 2: host numpy blocks, everything is already stored
+    ids2, status2 = store.batch_put([pool[s] for s, _ in items[rank]], return_status=True)
+    assert ids2 == ids_all[rank] and status2 == [1] * len(ids2), "round 2"
+
+    # cluster usage sums the shards; total blocks per owner add up
+    st = store.get_stats()
+    t = torch.tensor([st.total_blocks, st.local_gpu_used], dtype=torch.int64)
+    dist.all_reduce(t)
+    assert int(t[0]) == len(uniq), ("total_blocks", int(t[0]), len(uniq))
+    assert st.cluster_gpu_used == int(t[1])
+
+    store.clear()
+    assert not store.contains(uniq[0])
+    store.barrier()
+    store.close()
+    dist.destroy_process_group()
+    print(f"rank {rank}: DHT parity ok ({len(uniq)} unique blocks)", flush=True)
+
+
+if __name__ == "__main__":
+    main()

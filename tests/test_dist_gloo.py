@@ -1,0 +1,107 @@
+"""N>1 host-side logic on CPU: two gloo ranks run the DHT routing protocol
+(owner = cb_owner_rank, per-owner buckets in batch order, counts all-gather,
+all-to-all of requests, owner-side sequential dedup in (source rank, index)
+order) and must reach exactly the sequential DhtOracle's decisions."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.distributed as dist  # noqa: E402
+import torch.multiprocessing as mp  # noqa: E402
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _batches(world):
+    """Per-rank batches with cross-rank and intra-rank duplicates."""
+    rng = np.random.default_rng(7)
+    pool = [rng.integers(0, 256, 512, dtype=np.uint8).tobytes() for _ in range(24)]
+    items = []
+    for r in range(world):
+        sel = rng.integers(0, 24, 40)
+        items.append([(int(s), bool(s % 5 == 0)) for s in sel])
+    return pool, items
+
+
+def _alltoallv(recv, send, rank, world):
+    """Grouped point-to-point exchange (what the library does with
+    ncclGroupStart / ncclSend / ncclRecv / ncclGroupEnd)."""
+    reqs = []
+    for r in range(world):
+        if r == rank:
+            recv[r].copy_(send[r])
+            continue
+        if send[r].numel():
+            reqs.append(dist.isend(send[r].contiguous(), r))
+        if recv[r].numel():
+            reqs.append(dist.irecv(recv[r], r))
+    for q in reqs:
+        q.wait()
+
+
+def _worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import cascade_cpp
+    from oracle import store_oracle as O
+    from oracle.dht_oracle import owner as oracle_owner
+
+    pool, items = _batches(world)
+    mine = [(O.block_id(pool[s]), pool[s], pf) for s, pf in items[rank]]
+    # routing: owner per block (the C ABI's rule) in batch order
+    owners = [cascade_cpp.owner_rank(b, world) for b, _, _ in mine]
+    assert owners == [oracle_owner(b, world) for b, _, _ in mine]
+    buckets = [[i for i, o in enumerate(owners) if o == r] for r in range(world)]
+    counts = torch.tensor([len(b) for b in buckets], dtype=torch.int64)
+    allc = [torch.zeros(world, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(allc, counts)
+    rcount = [int(allc[r][rank]) for r in range(world)]
+    # requests: (index, id bytes, size) records, all-to-all
+    send = [torch.tensor([[i] + list(bytes.fromhex(mine[i][0])) for i in b], dtype=torch.int64).reshape(-1, 17)
+            for b in buckets]
+    recv = [torch.zeros((rcount[r], 17), dtype=torch.int64) for r in range(world)]
+    _alltoallv(recv, send, rank, world)
+    # owner: sequential dedup in (source rank, index) order
+    shard = O.SequentialStore()
+    replies = []
+    for r in range(world):
+        rep = []
+        for row in recv[r].tolist():
+            bid = bytes(row[1:]).hex()
+            rep.append([row[0], shard.put(bid, b"x")[1]])
+        replies.append(torch.tensor(rep, dtype=torch.int64).reshape(-1, 2))
+    back = [torch.zeros((len(buckets[r]), 2), dtype=torch.int64) for r in range(world)]
+    _alltoallv(back, replies, rank, world)
+    status = [None] * len(mine)
+    for r in range(world):
+        for idx, st in back[r].tolist():
+            status[idx] = st
+    out[rank] = status
+    dist.destroy_process_group()
+
+
+def test_dht_protocol_two_gloo_ranks():
+    world = 2
+    port = _free_port()
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_worker, args=(world, port, out), nprocs=world, start_method="spawn", join=True)
+    from oracle import store_oracle as O
+    from oracle.dht_oracle import DhtOracle
+    pool, items = _batches(world)
+    ora = DhtOracle(world)
+    want = ora.put_round([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
+    for r in range(world):
+        assert out[r] == want[r], r
+    # cross-rank duplicates exist and the lowest (rank, index) copy is stored
+    assert sum(map(sum, want)) > 0
