@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 METRIC = "aggregate batch_put (incl. SHA256) + batch_get GB/s"
 GB = 1e9
 SHA_TRAFFIC_PER_1024_LAUNCH = 711_190_272  # bytes, ncu capture (see roofline note)
+NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool (nominal 900)
 
 
 def parse():
@@ -59,6 +60,11 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--workload", default="config2", choices=["config2", "zipf"])
+    p.add_argument("--zipf-blocks-per-gpu", type=int, default=20000)
+    p.add_argument("--zipf-block-bytes", type=int, default=5242880)
+    p.add_argument("--zipf-batch", type=int, default=512)
+    p.add_argument("--zipf-alpha", type=float, default=1.1)
     return p.parse_args()
 
 
@@ -141,17 +147,17 @@ def gpu_blocks(args, rank, device):
     return pool, ptrs.astype(np.uint64), is_prefix.astype(np.uint8)
 
 
-def make_store(args, device_index, capacity):
+def make_store(args, device_index, capacity, dht=False):
     import cascade_cpp
     cfg = cascade_cpp.DistributedConfig()
     cfg.gpu_capacity_per_device = capacity
     cfg.dram_capacity = 0
     cfg.device = device_index
     cfg.copy_engine = args.copy_engine
-    cfg.index_log2 = 18
+    cfg.index_log2 = 18 if not dht else 20
     cfg.hash_lanes = args.hash_lanes
     cfg.profile = True   # per-kernel CUDA-event timing for the roofline fields
-    cfg.dht = False      # one independent store per rank (replicas)
+    cfg.dht = dht        # N>1: one hash-sharded store over all ranks
     return cascade_cpp.DistributedStore(cfg)
 
 
@@ -304,10 +310,15 @@ def main():
     torch.cuda.set_device(device)
     size = args.block_bytes
 
+    if args.workload == "zipf":
+        return zipf_main(args, rank, world, local, device)
     pool, ptrs, prefix = gpu_blocks(args, rank, device)
     sizes = np.full(len(ptrs), size, np.uint64)
     n_unique = pool.numel() // size
-    store = make_store(args, local, n_unique * size + (256 << 20))
+    # DHT (N>1): an owner holds ~1/W of every rank's unique blocks; leave
+    # room for the owner imbalance of a random hash placement.
+    cap = n_unique * size + (256 << 20) if world == 1 else int(n_unique * size * 1.15) + (1 << 30)
+    store = make_store(args, local, cap, dht=world > 1)
     out_buf = torch.empty(args.batch * size, dtype=torch.uint8, device=device)
 
     def sync_all():
@@ -393,10 +404,25 @@ def main():
                                  "frac": round(scatter_achieved / hbm_peak, 4)},
         "gpu_launches": int(launches),
     }
+    if world > 1:
+        # remote gets cross NVLink: bytes received per GPU / gather time,
+        # against the measured 770 GB/s peer copy per direction
+        remote_b = d("remote_gpu_hits") * size
+        nv = remote_b / gather_s / GB if gather_s else 0.0
+        nv_min = reduce_max(-nv, world) * -1.0
+        line["roofline_nvlink"] = {"kernel": "copy_lsu (peer-load gather)", "bound": "nvlink",
+                                   "achieved_per_gpu_min": round(nv_min, 2), "achieved_rank0": round(nv, 2),
+                                   "peak": NVLINK_PEER_GBS, "unit": "GB/s",
+                                   "frac": round(nv_min / NVLINK_PEER_GBS, 4),
+                                   "remote_fraction": round(d("remote_gpu_hits") / max(1, d("remote_gpu_hits")
+                                                                                         + d("local_gpu_hits")), 4)}
+        line["config"]["parallelism"] = f"hash-sharded DHT over {world} GPUs (owner = ID mod {world})"
     line["clocks"] = clk.summary()
 
-    if rank == 0 and not args.no_sweep:
-        line["sweep"] = batch_sweep(args, store, ptrs, sizes, prefix, out_buf, size)
+    if not args.no_sweep:
+        sw = batch_sweep(args, store, ptrs, sizes, prefix, out_buf, size)  # collective in a DHT
+        if rank == 0:
+            line["sweep"] = sw
     del pool
     torch.cuda.empty_cache()
     if not args.no_e2e:
@@ -414,6 +440,98 @@ def main():
     store.close()
     if world > 1:
         torch.distributed.destroy_process_group()
+
+
+def zipf_main(args, rank, world, local, device):
+    """Config 4: hash-sharded DHT of Qwen2.5-72B-shaped blocks (5,242,880 B,
+    bf16 N(0,1) generated on the GPU). Every rank puts --zipf-blocks-per-gpu
+    blocks (weak scaling: 20,000 per GPU = 160,000 at 8 GPUs), then each step
+    every rank batch_gets --zipf-batch keys drawn from a bounded Zipf(alpha)
+    over all ranks' keys (seeded rank->key permutation); ~(W-1)/W of the
+    fetches are NVLink peer reads."""
+    import torch
+    import torch.distributed as dist
+    from cascade_cpp import workloads as W
+    size, nb, gb = args.zipf_block_bytes, args.zipf_blocks_per_gpu, args.zipf_batch
+    cap = int(nb * size * 1.12) + (1 << 30)
+    store = make_store(args, local, cap, dht=world > 1)
+    pb = 256
+    buf = torch.empty(pb * size, dtype=torch.uint8, device=device)
+    g = torch.Generator(device=device).manual_seed(7000 + rank)
+    keys = np.empty((nb, 16), np.uint8)
+    t0 = time.perf_counter()
+    for i in range(0, nb, pb):
+        m = min(pb, nb - i)
+        buf[:m * size].view(torch.bfloat16).copy_(
+            torch.randn(m * size // 2, generator=g, device=device, dtype=torch.bfloat16))
+        ptrs = (np.uint64(buf.data_ptr()) + np.arange(m, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+        k, _ = store.put_ptrs(ptrs, np.full(m, size, np.uint64), True)
+        keys[i:i + m] = k
+    torch.cuda.synchronize()
+    populate_s = time.perf_counter() - t0
+    del buf
+    torch.cuda.empty_cache()
+    if world > 1:
+        kt = torch.from_numpy(keys).to(device)
+        parts = [torch.empty_like(kt) for _ in range(world)]
+        dist.all_gather(parts, kt)
+        gkeys = torch.cat(parts).cpu().numpy()
+    else:
+        gkeys = keys
+    total_steps = args.warmup + args.steps
+    draws = W.zipf_keys(len(gkeys), total_steps * gb, args.zipf_alpha, seed=100 + rank)
+    out = torch.empty(gb * size, dtype=torch.uint8, device=device)
+    outs = (np.uint64(out.data_ptr()) + np.arange(gb, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+    caps = np.full(gb, size, np.uint64)
+    for s in range(args.warmup):
+        store.get_ptrs(gkeys[draws[s * gb:(s + 1) * gb]], outs, caps, True)
+    st0 = store._n.stats()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    got = 0
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for s in range(args.warmup, total_steps):
+            sz, f = store.get_ptrs(gkeys[draws[s * gb:(s + 1) * gb]], outs, caps, True)
+            got += int(sz[(f & 0x0F) != 0].sum())
+        ev1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    el = reduce_max(ev0.elapsed_time(ev1) / 1e3, world)
+    st1 = store._n.stats()
+    tot = reduce_sum(got, world)
+    d = {f: getattr(st1, f) - getattr(st0, f) for f in ("remote_gpu_hits", "local_gpu_hits", "gather_ns",
+                                                        "gather_bytes", "kernel_launches")}
+    remote_b = d["remote_gpu_hits"] * size
+    gather_s = d["gather_ns"] / 1e9
+    nv = remote_b / gather_s / GB if gather_s else 0.0
+    nv_min = -reduce_max(-nv, world)
+    # owner egress imbalance: requests served per owner this run
+    line = {
+        "metric": "aggregate batch_get GB/s (config 4: DHT, Zipf keys)", "value": round(tot / el / GB, 3),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(el / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded bf16 N(0,1) blocks generated on the GPU)",
+        "config": {"workload": f"config4: {nb} x {size} B Qwen2.5-72B KV blocks per GPU ({nb * world} total), "
+                               f"batch_get of {gb} keys per rank per step, Zipf alpha {args.zipf_alpha}",
+                   "parallelism": f"hash-sharded DHT over {world} GPUs" if world > 1 else "single store",
+                   "l2": "every step reads 2.7 GB per GPU >> L2"},
+        "populate_s": round(populate_s, 2),
+        "remote_fraction": round(d["remote_gpu_hits"] / max(1, d["remote_gpu_hits"] + d["local_gpu_hits"]), 4),
+        "roofline": {"kernel": "copy_lsu (peer-load gather)", "bound": "nvlink" if world > 1 else "hbm",
+                     "achieved": round(nv_min if world > 1 else 2 * d["gather_bytes"] / gather_s / GB, 2),
+                     "peak": NVLINK_PEER_GBS if world > 1 else None, "unit": "GB/s",
+                     "frac": round(nv_min / NVLINK_PEER_GBS, 4) if world > 1 else None},
+        "gpu_launches": int(d["kernel_launches"]), "clocks": clk.summary(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    store.close()
+    if world > 1:
+        dist.destroy_process_group()
 
 
 def config_dict(args):
