@@ -180,16 +180,19 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
     keys = uk[order].view(np.uint8).reshape(-1, 16)
     base = out_buf.data_ptr() if hasattr(out_buf, "data_ptr") else out_buf.ctypes.data
     outs_b = np.uint64(base) + np.arange(batch, dtype=np.uint64) * np.uint64(size)
-    got = 0
+    got = remote = 0
     for i in range(0, len(keys), batch):
         kk = keys[i:i + batch]
         m = len(kk)
         s, f = store.get_ptrs(kk, outs_b[:m], np.full(m, size, np.uint64), device_memory)
-        got += int(s[(f & 0x0F) != 0].sum())
+        ok = (f & 0x0F) != 0
+        got += int(s[ok].sum())
+        remote += int(s[(f & 0x0F) == 3].sum())  # CB_FOUND_REMOTE_HBM: crossed NVLink
     ev[2].record()
     ev[2].synchronize()
     put_s = ev[0].elapsed_time(ev[1]) / 1e3
     get_s = ev[1].elapsed_time(ev[2]) / 1e3
+    run_pass.remote_bytes = getattr(run_pass, "remote_bytes", 0) + remote
     return put_s, get_s, int(sizes.sum()), got
 
 
@@ -331,6 +334,7 @@ def main():
         run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, w)
     st0 = store._n.stats()
     sync_all()
+    run_pass.remote_bytes = 0
     put_t = get_t = 0.0
     put_b = get_b = 0
     t_ev0 = torch.cuda.Event(enable_timing=True)
@@ -347,6 +351,7 @@ def main():
         t_ev1.record()
         sync_all()
     elapsed = t_ev0.elapsed_time(t_ev1) / 1e3
+    remote_b = run_pass.remote_bytes
     st1 = store._n.stats()
     elapsed_max = reduce_max(elapsed, world)
     total_bytes = reduce_sum(put_b + get_b, world)
@@ -407,15 +412,15 @@ def main():
     if world > 1:
         # remote gets cross NVLink: bytes received per GPU / gather time,
         # against the measured 770 GB/s peer copy per direction
-        remote_b = d("remote_gpu_hits") * size
         nv = remote_b / gather_s / GB if gather_s else 0.0
         nv_min = reduce_max(-nv, world) * -1.0
         line["roofline_nvlink"] = {"kernel": "copy_lsu (peer-load gather)", "bound": "nvlink",
                                    "achieved_per_gpu_min": round(nv_min, 2), "achieved_rank0": round(nv, 2),
                                    "peak": NVLINK_PEER_GBS, "unit": "GB/s",
                                    "frac": round(nv_min / NVLINK_PEER_GBS, 4),
-                                   "remote_fraction": round(d("remote_gpu_hits") / max(1, d("remote_gpu_hits")
-                                                                                         + d("local_gpu_hits")), 4)}
+                                   "note": "remote bytes received per GPU / gather kernel time (the gather also "
+                                           "moves the local 1/W from HBM)",
+                                   "remote_fraction": round(remote_b / max(1, get_b), 4)}
         line["config"]["parallelism"] = f"hash-sharded DHT over {world} GPUs (owner = ID mod {world})"
     line["clocks"] = clk.summary()
 
