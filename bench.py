@@ -60,7 +60,10 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", default="config2", choices=["config2", "zipf"])
+    p.add_argument("--workload", default="config2", choices=["config2", "zipf", "spill"])
+    p.add_argument("--spill-blocks", type=int, default=40000)
+    p.add_argument("--spill-hbm-gb", type=float, default=120.0)
+    p.add_argument("--spill-dram-gb", type=float, default=100.0)
     p.add_argument("--zipf-blocks-per-gpu", type=int, default=20000)
     p.add_argument("--zipf-block-bytes", type=int, default=5242880)
     p.add_argument("--zipf-batch", type=int, default=512)
@@ -315,6 +318,8 @@ def main():
 
     if args.workload == "zipf":
         return zipf_main(args, rank, world, local, device)
+    if args.workload == "spill":
+        return spill_main(args, rank, world, local, device)
     pool, ptrs, prefix = gpu_blocks(args, rank, device)
     sizes = np.full(len(ptrs), size, np.uint64)
     n_unique = pool.numel() // size
@@ -537,6 +542,131 @@ def zipf_main(args, rank, world, local, device):
     store.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def host_link_peaks(device, nbytes=4 << 30, reps=3):
+    """Pinned host<->device copy bandwidth (copy engines), GB/s."""
+    import torch
+    h = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dbuf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    res = {}
+    for name, dst, src in (("h2d", dbuf, h), ("d2h", h, dbuf)):
+        dst.copy_(src, non_blocking=True)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            dst.copy_(src, non_blocking=True)
+        e1.record()
+        e1.synchronize()
+        res[name] = nbytes * reps / (e0.elapsed_time(e1) / 1e3) / GB
+    del h, dbuf
+    torch.cuda.empty_cache()
+    return res
+
+
+def spill_main(args, rank, world, local, device):
+    """Config 3: 40,000 Qwen2.5-72B-shaped blocks (5,242,880 B bf16) into a
+    120 GB HBM pool with a pinned DRAM tier; 10 % of the blocks (seeded) are
+    prefix-protected. Put everything (LRU demotions to DRAM run as mapped-host
+    copy kernels), then batch_get Zipf(1.1) keys; DRAM hits are promoted back
+    to HBM (each promotion demotes an LRU block). Every get batch is checked:
+    the bytes returned must hash (GPU SHA-256) to the requested ID."""
+    import torch
+    import cascade_cpp
+    from cascade_cpp import workloads as W
+    size, nb = args.zipf_block_bytes, args.spill_blocks
+    peaks = host_link_peaks(device)
+    cfg = cascade_cpp.DistributedConfig()
+    cfg.gpu_capacity_per_device = int(args.spill_hbm_gb * 1e9)
+    cfg.dram_capacity = int(args.spill_dram_gb * 1e9)
+    cfg.device = local
+    cfg.profile = True
+    cfg.dht = False
+    cfg.index_log2 = 17
+    store = cascade_cpp.DistributedStore(cfg)
+    rng = np.random.default_rng(33)
+    prefix = (rng.random(nb) < 0.10).astype(np.uint8)
+    pb = 256
+    buf = torch.empty(pb * size, dtype=torch.uint8, device=device)
+    g = torch.Generator(device=device).manual_seed(33)
+    keys = np.empty((nb, 16), np.uint8)
+    s0 = store._n.stats()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(0, nb, pb):
+        m = min(pb, nb - i)
+        buf[:m * size].view(torch.bfloat16).copy_(
+            torch.randn(m * size // 2, generator=g, device=device, dtype=torch.bfloat16))
+        ptrs = (np.uint64(buf.data_ptr()) + np.arange(m, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+        k, st = store.put_ptrs(ptrs, np.full(m, size, np.uint64), True, prefix=prefix[i:i + m])
+        assert (st == 0).all(), "put failed"
+        keys[i:i + m] = k
+    torch.cuda.synchronize()
+    put_s = time.perf_counter() - t0
+    s1 = store._n.stats()
+    del buf
+    torch.cuda.empty_cache()
+    # prefix protection: no prefix block may sit in DRAM while HBM holds a
+    # non-prefix block
+    in_dram = [store.locate(k.tobytes().hex()) for k in keys]
+    pf_dram = sum(1 for j, l in enumerate(in_dram) if prefix[j] and not l.is_gpu)
+    np_hbm = sum(1 for j, l in enumerate(in_dram) if not prefix[j] and l.is_gpu)
+    gb = args.zipf_batch
+    total_steps = args.warmup + args.steps
+    draws = W.zipf_keys(nb, total_steps * gb, args.zipf_alpha, seed=34)
+    out = torch.empty(gb * size, dtype=torch.uint8, device=device)
+    outs = (np.uint64(out.data_ptr()) + np.arange(gb, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+    caps = np.full(gb, size, np.uint64)
+    hasher = cascade_cpp._hasher(local)
+    for s in range(args.warmup):
+        kk = keys[draws[s * gb:(s + 1) * gb]]
+        sz, f = store.get_ptrs(kk, outs, caps, True)
+        assert ((f & 0x0F) != 0).all()
+        dig = hasher.hash(outs, caps, 0)  # bytes returned hash to the requested IDs
+        assert np.array_equal(dig[:, :16], kk), "get returned wrong bytes"
+    s2 = store._n.stats()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    got = 0
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for s in range(args.warmup, total_steps):
+            sz, f = store.get_ptrs(keys[draws[s * gb:(s + 1) * gb]], outs, caps, True)
+            got += int(sz[(f & 0x0F) != 0].sum())
+        ev1.record()
+        torch.cuda.synchronize()
+    get_s = ev0.elapsed_time(ev1) / 1e3
+    s3 = store._n.stats()
+
+    def dd(a, b, f):
+        return getattr(b, f) - getattr(a, f)
+
+    ev_b, ev_ns = dd(s0, s1, "tier_bytes"), dd(s0, s1, "tier_ns")
+    pr_b, pr_ns = dd(s2, s3, "tier_bytes"), dd(s2, s3, "tier_ns")
+    line = {
+        "metric": "tier moves (config 3: HBM <-> pinned DRAM spill)", "value": round(got / get_s / GB, 3),
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(get_s / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded bf16 N(0,1) blocks generated on the GPU)",
+        "config": {"workload": f"config3: {nb} x {size} B Qwen2.5-72B blocks ({nb * size / 1e9:.1f} GB), HBM pool "
+                               f"{args.spill_hbm_gb} GB, pinned DRAM {args.spill_dram_gb} GB, 10% prefix, "
+                               f"batch_get {gb} Zipf({args.zipf_alpha}) keys per step, promotion on DRAM hit"},
+        "value_is": "batch_get GB/s in the timed steps (DRAM hits promoted inline)",
+        "put_phase": {"seconds": round(put_s, 2), "gb_put": round(nb * size / 1e9, 1),
+                      "gpu_evictions": dd(s0, s1, "gpu_evictions"), "evicted_gb": round(ev_b / 1e9, 2),
+                      "evict_kernel_gbs": round(ev_b / ev_ns, 2) if ev_ns else None,
+                      "prefix_blocks_in_dram": pf_dram, "nonprefix_blocks_in_hbm": np_hbm},
+        "get_phase": {"local_gpu_hits": dd(s2, s3, "local_gpu_hits"), "local_dram_hits": dd(s2, s3, "local_dram_hits"),
+                      "promotions": dd(s2, s3, "promotions_to_local"), "tier_moved_gb": round(pr_b / 1e9, 2),
+                      "tier_kernel_gbs": round(pr_b / pr_ns, 2) if pr_ns else None},
+        "roofline": {"kernel": "copy_lsu (mapped pinned host)", "bound": "host link",
+                     "achieved": round(ev_b / ev_ns, 2) if ev_ns else None,
+                     "peak": round(peaks["d2h"], 2), "unit": "GB/s",
+                     "frac": round((ev_b / ev_ns) / peaks["d2h"], 4) if ev_ns else None,
+                     "peak_source": "measured pinned D2H copy in this run", "h2d_peak": round(peaks["h2d"], 2)},
+        "gpu_launches": dd(s2, s3, "kernel_launches"), "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    store.close()
 
 
 def config_dict(args):

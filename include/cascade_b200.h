@@ -7,8 +7,9 @@
  * 16-byte binary form of the 32-hex BlockId (first 16 bytes of SHA-256).
  * No function throws; every function returns a CB_* status and leaves a
  * message for cb_last_error(). Calls on one store are serialised internally.
- * `stream` is a cudaStream_t (NULL = the store's own stream); work is ordered
- * after prior work on it and the call returns with its results final.
+ * `stream` is a cudaStream_t (NULL = the store's own stream, which is ordered
+ * with the legacy default stream); work is ordered after prior work on it and
+ * the call returns with its results final.
  */
 #ifndef CASCADE_B200_H
 #define CASCADE_B200_H

@@ -109,7 +109,10 @@ int Store::init() {
   if (device < 0 || device >= ndev) return fail(CB_ERR_ARG, "device %d out of range (%d)", device, ndev);
   CB_TRY(cudaSetDevice(device), "cudaSetDevice");
   CB_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device), "sm count");
-  CB_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamNonBlocking), "stream");
+  // A blocking stream: it is ordered with the legacy default stream, so a
+  // caller whose current stream is the default one (handle 0, which reaches
+  // the C ABI as NULL) sees its earlier writes before the store reads them.
+  CB_TRY(cudaStreamCreateWithFlags(&own_stream, cudaStreamDefault), "stream");
   pool_bytes = policy.hbm_capacity() / 256 * 256;
   if (pool_bytes) CB_TRY(cudaMalloc(&pool, pool_bytes), "HBM pool cudaMalloc");
   CB_TRY(cudaMalloc(&d_err, sizeof(unsigned)), "error word");

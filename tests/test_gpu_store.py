@@ -282,6 +282,28 @@ def test_index_growth_keeps_everything():
     assert all(found) and all(np.array_equal(o, b) for o, b in zip(outs, blocks))
 
 
+@pytest.mark.parametrize("use_side_stream", [False, True])
+def test_put_is_ordered_after_pending_torch_writes(use_side_stream):
+    """Blocks written by torch kernels still in flight on the caller's current
+    stream (the default stream, or a side stream) must be hashed and stored
+    after those writes land."""
+    store = make_store(hbm=4 << 30)
+    size, n = 5 << 20, 64
+    buf = torch.empty(n * size, dtype=torch.uint8, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(9)
+    s = torch.cuda.Stream() if use_side_stream else torch.cuda.current_stream()
+    with torch.cuda.stream(s):
+        for rnd in range(3):
+            buf.view(torch.bfloat16).copy_(torch.randn(n * size // 2, generator=g, device=DEV, dtype=torch.bfloat16))
+            views = [buf[i * size:(i + 1) * size] for i in range(n)]
+            ids = store.batch_put(views)  # no synchronize between the writes and the put
+            host = buf.cpu().numpy()
+            for i in (0, n // 2, n - 1):
+                assert ids[i] == O.block_id(host[i * size:(i + 1) * size]), (rnd, i)
+            out = torch.empty(size, dtype=torch.uint8, device=DEV)
+            assert store.get(ids[0], out)[0] and torch.equal(out, views[0])
+
+
 def test_config2_slice_device_roundtrip():
     """2048 Qwen2.5-7B blocks (config-2 shape, 25 % copies) in batches of
     1024: IDs equal the oracle's on a sample, every get is byte-exact."""
