@@ -700,15 +700,16 @@ def e2e_run(args, rank, world, device, store):
     from cascade_cpp import workloads as W
     src, is_prefix = W.dedup_mix(n, 64, 0.25, 99 + rank)
     uniq = np.unique(src)
-    host_u = torch.empty(len(uniq) * size, dtype=torch.uint8, pin_memory=True)
+    # The put stream as a caller holds it: one pinned [n, block] array of KV
+    # pages in stream order (copies of prefix blocks materialised).
     g = torch.Generator(device=device).manual_seed(5 + rank)
-    hv = host_u.view(torch.float16)
-    step = 256 * size // 2
-    for o in range(0, hv.numel(), step):
-        m = min(step, hv.numel() - o)
-        hv[o:o + m].copy_(torch.randn(m, generator=g, device=device, dtype=torch.float16))
-    pos = np.searchsorted(uniq, src)
-    ptrs = (np.uint64(host_u.data_ptr()) + pos.astype(np.uint64) * np.uint64(size)).astype(np.uint64)
+    dev_u = torch.randn(len(uniq) * size // 2, generator=g, device=device, dtype=torch.float16).view(torch.uint8)
+    pos = torch.from_numpy(np.searchsorted(uniq, src)).to(device)
+    host_u = torch.empty(n * size, dtype=torch.uint8, pin_memory=True)
+    host_u.view(n, size).copy_(dev_u.view(len(uniq), size).index_select(0, pos))
+    del dev_u
+    torch.cuda.empty_cache()
+    ptrs = (np.uint64(host_u.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
     sizes = np.full(n, size, np.uint64)
     prefix = is_prefix.astype(np.uint8)
     out = torch.empty(args.batch * size, dtype=torch.uint8, pin_memory=True)

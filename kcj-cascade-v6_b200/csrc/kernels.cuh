@@ -10,10 +10,19 @@ struct HashJob {
   uint64_t size;  // bytes
 };
 
+// Blocks that are still being copied in: segment k (seg_chunks 64-byte
+// chunks of every block) may be read once *counter > k. data_chunks =
+// ceil(block size / 64) (uniform block size).
+struct HashProgress {
+  const unsigned *counter;
+  uint32_t seg_chunks;
+  uint64_t data_chunks;
+};
+
 // sha256.cu — digests: n * 8 words holding the 32 digest bytes in order.
-// One CTA (producer + consumer warp) per 32 blocks.
+// One CTA (producer + consumer warp) per 32 blocks. progress may be null.
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
-                                unsigned *d_err, cudaStream_t stream);
+                                unsigned *d_err, cudaStream_t stream, const HashProgress *progress = nullptr);
 
 // copy.cu — batched copies. Descriptor i covers units
 // [unit_start[i], unit_start[i+1]) of kCopyUnit bytes each; a unit past the

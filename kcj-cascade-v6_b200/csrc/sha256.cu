@@ -118,9 +118,32 @@ struct Ring {
   uint64_t empty[kStages];
 };
 
+// Waits (bounded) until the copy stream has published segment `need - 1`.
+// Called by the whole producer warp with a warp-uniform `need`; lane 0
+// polls the counter with acquire loads, the result is broadcast.
+CB_D bool wait_progress(const HashProgress &pg, uint32_t need, uint32_t &seen, unsigned *err) {
+  if (!pg.counter || seen >= need) return true;
+  uint32_t v = 0;
+  if ((threadIdx.x & 31) == 0) {
+    for (uint64_t it = 0; it < kWaitLimit; ++it) {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(pg.counter) : "memory");
+      if (v >= need) break;
+      __nanosleep(128);
+    }
+  }
+  v = __shfl_sync(0xffffffffu, v, 0);
+  __syncwarp();
+  if (v < need) {
+    if ((threadIdx.x & 31) == 0) atomicOr(err, kErrTimeout);
+    return false;
+  }
+  seen = v;
+  return true;
+}
+
 __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict__ jobs, int n,
                                                        uint32_t *__restrict__ digests, unsigned *err,
-                                                       uint32_t one) {
+                                                       uint32_t one, HashProgress pg) {
   __shared__ __align__(16) Ring ring;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -151,6 +174,10 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
     const bool aligned = (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
     const uint4 *q = reinterpret_cast<const uint4 *>(p);
     uint4 v0 = make_uint4(0, 0, 0, 0), v1 = v0, v2 = v0, v3 = v0;
+    // When the blocks are still arriving (host put overlapped with the
+    // copy), chunk c may only be read once its segment has landed.
+    uint32_t seen = 0;
+    if (!wait_progress(pg, 1, seen, err)) return;
     if (aligned && nfull) {
       v0 = ld_stream16(q);
       v1 = ld_stream16(q + 1);
@@ -162,6 +189,12 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
       if (c >= kStages && !mbar_wait(&ring.empty[s], (uint32_t)((c / kStages) - 1) & 1u)) {
         atomicOr(err, kErrTimeout);
         return;
+      }
+      if (pg.counter) {
+        // this iteration reads chunk c (slow path) and prefetches chunk c+1
+        const uint64_t last = pg.data_chunks ? pg.data_chunks - 1 : 0;
+        const uint64_t need_chunk = c + 1 < last ? c + 1 : last;
+        if (!wait_progress(pg, (uint32_t)(need_chunk / pg.seg_chunks) + 1, seen, err)) return;
       }
       uint32_t w[16];
       if (c < nfull && aligned) {
@@ -267,10 +300,11 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
 }  // namespace
 
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
-                                unsigned *d_err, cudaStream_t stream) {
+                                unsigned *d_err, cudaStream_t stream, const HashProgress *progress) {
   (void)lanes;
   if (n <= 0) return cudaSuccess;
-  sha256_pc_kernel<<<(n + 31) / 32, 64, 0, stream>>>(d_jobs, n, d_digests, d_err, 1u);
+  const HashProgress pg = progress ? *progress : HashProgress{nullptr, 1, 0};
+  sha256_pc_kernel<<<(n + 31) / 32, 64, 0, stream>>>(d_jobs, n, d_digests, d_err, 1u, pg);
   return cudaGetLastError();
 }
 

@@ -124,6 +124,10 @@ int Store::init() {
   hash_lanes = (cfg.hash_lanes == 8 || cfg.hash_lanes == 16) ? cfg.hash_lanes : 32;
   CB_TRY(cudaEventCreate(&ev_a), "event");
   CB_TRY(cudaEventCreate(&ev_b), "event");
+  CB_TRY(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "copy stream");
+  CB_TRY(cudaEventCreateWithFlags(&ev_reset, cudaEventDisableTiming), "event");
+  CB_TRY(cudaEventCreateWithFlags(&ev_copies, cudaEventDisableTiming), "event");
+  CB_TRY(cudaMalloc(&d_progress, 256), "progress word");
   return CB_OK;
 }
 
@@ -142,6 +146,14 @@ Store::~Store() {
   d_staging.release();
   if (ev_a) cudaEventDestroy(ev_a);
   if (ev_b) cudaEventDestroy(ev_b);
+  if (copy_stream) {
+    cudaStreamSynchronize(copy_stream);
+    cudaStreamDestroy(copy_stream);
+  }
+  if (ev_reset) cudaEventDestroy(ev_reset);
+  if (ev_copies) cudaEventDestroy(ev_copies);
+  if (d_progress) cudaFree(d_progress);
+  h_progress.release();
   if (own_stream) cudaStreamDestroy(own_stream);
 }
 
@@ -315,7 +327,8 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
 }
 
 // SHA-256 of device-resident blocks; digests (n*32 B) land in h_out.
-int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st) {
+int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st,
+                       const HashProgress *pg, cudaEvent_t copies_done) {
   Layout L;
   const size_t o_jobs = L.add(sizeof(HashJob) * n);
   const size_t o_dig = L.add(32ull * n);
@@ -333,9 +346,11 @@ int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaS
   CB_TRY(timed(0, total, st,
                [&] {
                  return launch_sha256_batch(reinterpret_cast<const HashJob *>(d + o_jobs), n,
-                                            reinterpret_cast<uint32_t *>(d + o_dig), hash_lanes, d_err, st);
+                                            reinterpret_cast<uint32_t *>(d + o_dig), hash_lanes, d_err, st, pg);
                }),
          "sha256 launch");
+  // everything after the hash on st (scatter) also needs every copy done
+  if (copies_done) CB_TRY(cudaStreamWaitEvent(st, copies_done, 0), "wait copies");
   CB_TRY(cudaMemcpyAsync(h_out.ptr, d + o_dig, 32ull * n, cudaMemcpyDeviceToHost, st), "D2H digests");
   return check_device_error(st);  // syncs; a timed-out hash is an error
 }
@@ -344,12 +359,13 @@ int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaS
 
 int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
                       const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
-                      cudaStream_t st) {
+                      cudaStream_t st, const HashProgress *pg, cudaEvent_t copies_done) {
   std::vector<HKey> keys(n);
   if (keys_in) {
+    if (copies_done) CB_TRY(cudaStreamWaitEvent(st, copies_done, 0), "wait copies");
     for (int i = 0; i < n; ++i) keys[i] = to_hkey(keys_in + 16 * i);
   } else {
-    int rc = hash_device(ptrs, sizes, n, st);
+    int rc = hash_device(ptrs, sizes, n, st, pg, copies_done);
     if (rc) return rc;
     const uint8_t *dig = static_cast<const uint8_t *>(h_out.ptr);
     for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32 * i);
@@ -432,6 +448,17 @@ int Store::put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_
     while (j < n && (j == i || bytes + align_up(sizes[j], 256) <= cap)) bytes += align_up(sizes[j++], 256);
     CB_TRY(d_staging.ensure(bytes), "device staging");
     dptrs.resize(j - i);
+    HashProgress pg;
+    if (!keys_in && stage_overlapped(ptrs + i, sizes + i, j - i, dptrs.data(), pg, st) == CB_OK) {
+      // Copies run on copy_stream; the hash reads each segment as it lands.
+      int rc = put_device(dptrs.data(), sizes + i, is_prefix ? is_prefix + i : nullptr, nullptr, j - i,
+                          keys_out ? keys_out + 16 * i : nullptr, status_out ? status_out + i : nullptr, st, &pg,
+                          ev_copies);
+      CB_TRY(cudaStreamSynchronize(copy_stream), "copy stream");
+      if (rc) return rc;
+      i = j;
+      continue;
+    }
     uint64_t off = 0;
     for (int k = i; k < j; ++k) {
       dptrs[k - i] = (uint64_t)d_staging.ptr + off;
@@ -458,6 +485,53 @@ int Store::put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_
     if (rc) return rc;
     i = j;
   }
+  return CB_OK;
+}
+
+// Overlapped staging for host puts of equal-size blocks at a constant host
+// stride (KV pages in one pinned buffer): the batch is copied segment-major
+// (segment k = bytes [k*seg, (k+1)*seg) of every block) with one strided
+// copy per segment on copy_stream, each followed by a 4-byte copy that
+// publishes k+1 to d_progress. The SHA-256 kernel (which consumes every
+// chain front to back at the same pace) reads a segment once it is
+// published, so the host link and the hash overlap. Returns CB_ERR_ARG when
+// the batch does not have that shape (the caller then copies plainly).
+int Store::stage_overlapped(const void *const *ptrs, const uint64_t *sizes, int n, uint64_t *dptrs,
+                            HashProgress &pg, cudaStream_t st) {
+  constexpr uint64_t kSeg = 64 * 1024;
+  if (n < 32) return CB_ERR_ARG;
+  const uint64_t size = sizes[0];
+  if (size < 4 * kSeg) return CB_ERR_ARG;
+  const int64_t stride = static_cast<const uint8_t *>(ptrs[1]) - static_cast<const uint8_t *>(ptrs[0]);
+  if (stride < (int64_t)size) return CB_ERR_ARG;
+  for (int i = 1; i < n; ++i) {
+    if (sizes[i] != size) return CB_ERR_ARG;
+    if (static_cast<const uint8_t *>(ptrs[i]) - static_cast<const uint8_t *>(ptrs[i - 1]) != stride) return CB_ERR_ARG;
+  }
+  const uint64_t slot = align_up(size, 256);
+  for (int i = 0; i < n; ++i) dptrs[i] = (uint64_t)d_staging.ptr + slot * i;
+  const uint32_t nseg = (uint32_t)((size + kSeg - 1) / kSeg);
+  CB_TRY(h_progress.ensure(4ull * (nseg + 1)), "pinned progress");
+  unsigned *vals = static_cast<unsigned *>(h_progress.ptr);
+  for (uint32_t k = 0; k <= nseg; ++k) vals[k] = k;
+  // The staging area may still be read by earlier work on st.
+  CB_TRY(cudaEventRecord(ev_reset, st), "event");
+  CB_TRY(cudaStreamWaitEvent(copy_stream, ev_reset, 0), "wait");
+  CB_TRY(cudaMemcpyAsync(d_progress, &vals[0], 4, cudaMemcpyHostToDevice, copy_stream), "progress reset");
+  CB_TRY(cudaEventRecord(ev_reset, copy_stream), "event");
+  for (uint32_t k = 0; k < nseg; ++k) {
+    const uint64_t off = (uint64_t)k * kSeg;
+    const uint64_t w = std::min(kSeg, size - off);
+    CB_TRY(cudaMemcpy2DAsync(reinterpret_cast<void *>(dptrs[0] + off), slot,
+                             static_cast<const uint8_t *>(ptrs[0]) + off, (size_t)stride, w, n,
+                             cudaMemcpyHostToDevice, copy_stream),
+           "H2D segment");
+    CB_TRY(cudaMemcpyAsync(d_progress, &vals[k + 1], 4, cudaMemcpyHostToDevice, copy_stream), "progress");
+  }
+  CB_TRY(cudaEventRecord(ev_copies, copy_stream), "event");
+  // the hash must see the reset counter, not a stale one
+  CB_TRY(cudaStreamWaitEvent(st, ev_reset, 0), "wait reset");
+  pg = HashProgress{d_progress, (uint32_t)(kSeg / 64), (size + 63) / 64};
   return CB_OK;
 }
 

@@ -9,6 +9,7 @@
 
 #include "cascade_b200.h"
 #include "common.cuh"
+#include "kernels.cuh"
 #include "policy.hpp"
 
 // Returns from a Store member with CB_ERR_CUDA on a CUDA error.
@@ -113,10 +114,22 @@ struct Store {
   int check_device_error(cudaStream_t st);
   int run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped,
                 cudaStream_t st);
-  int hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st);
+  // pg/copies_done: the blocks are still arriving on copy_stream (see
+  // put_host); the hash kernel waits per segment and later work on st waits
+  // for copies_done.
+  int hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st,
+                  const HashProgress *pg = nullptr, cudaEvent_t copies_done = nullptr);
   int put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
                  const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
-                 cudaStream_t st);
+                 cudaStream_t st, const HashProgress *pg = nullptr, cudaEvent_t copies_done = nullptr);
+  int stage_overlapped(const void *const *ptrs, const uint64_t *sizes, int n, uint64_t *dptrs,
+                       HashProgress &pg, cudaStream_t st);
+
+  // Host puts: a second stream copies blocks in while the hash runs.
+  cudaStream_t copy_stream = nullptr;
+  unsigned *d_progress = nullptr;
+  PinnedBuf h_progress;
+  cudaEvent_t ev_reset = nullptr, ev_copies = nullptr;
   int put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
                const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
                cudaStream_t st);

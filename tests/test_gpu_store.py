@@ -304,6 +304,34 @@ def test_put_is_ordered_after_pending_torch_writes(use_side_stream):
             assert store.get(ids[0], out)[0] and torch.equal(out, views[0])
 
 
+@pytest.mark.parametrize("pinned", [True, False])
+@pytest.mark.parametrize("size,stride_pad", [(917504, 0), (300_000, 0), (262_144 + 17, 4096 + 3)])
+def test_host_put_overlapped_copy_and_hash(pinned, size, stride_pad):
+    """Equal-size host blocks at a constant stride take the overlapped path
+    (segment-major copies on a second stream, hash gated per segment)."""
+    n = 96
+    stride = size + stride_pad
+    rng = np.random.default_rng(size)
+    packed = torch.empty(n * stride, dtype=torch.uint8, pin_memory=pinned)
+    packed.copy_(torch.from_numpy(rng.integers(0, 256, n * stride, dtype=np.uint8)))
+    host = packed.numpy()
+    store = make_store(hbm=2 << 30)
+    ptrs = (np.uint64(host.ctypes.data) + np.arange(n, dtype=np.uint64) * np.uint64(stride)).astype(np.uint64)
+    sizes = np.full(n, size, np.uint64)
+    for rnd in range(2):
+        keys, status = store.put_ptrs(ptrs, sizes, device_memory=False)
+        want = [O.block_id(host[i * stride:i * stride + size]) for i in range(n)]
+        assert [k.tobytes().hex() for k in keys] == want
+        assert (status == rnd).all()  # second round: all dedup hits
+    outs = torch.empty(n * size, dtype=torch.uint8, device=DEV)
+    optrs = (np.uint64(outs.data_ptr()) + np.arange(n, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+    s, f = store.get_ptrs(keys, optrs, sizes, device_memory=True)
+    assert (f == 1).all()
+    got = outs.cpu().numpy()
+    for i in range(n):
+        assert np.array_equal(got[i * size:(i + 1) * size], host[i * stride:i * stride + size])
+
+
 def test_config2_slice_device_roundtrip():
     """2048 Qwen2.5-7B blocks (config-2 shape, 25 % copies) in batches of
     1024: IDs equal the oracle's on a sample, every get is byte-exact."""
