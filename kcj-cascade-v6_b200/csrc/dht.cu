@@ -505,10 +505,34 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
                    uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
   const int me = dht->me;
-  std::vector<uint64_t> reps;
-  std::vector<int> owner;
-  int rc = dht_lookup(keys, n, reps, owner, st);
+  // A key repeated inside the batch (hot keys under a skewed access
+  // pattern) is looked up and fetched over NVLink once; the other
+  // occurrences are filled from the first copy with a local device copy.
+  std::vector<int> uidx(n);
+  std::vector<uint8_t> ukeys;
+  ukeys.reserve(16ull * n);
+  {
+    std::unordered_map<HKey, int, HKeyHash> first;
+    first.reserve(2ull * n);
+    for (int i = 0; i < n; ++i) {
+      auto ins = first.emplace(to_hkey(keys + 16 * i), (int)(ukeys.size() / 16));
+      if (ins.second) ukeys.insert(ukeys.end(), keys + 16 * i, keys + 16 * i + 16);
+      uidx[i] = ins.first->second;
+    }
+  }
+  const int m = (int)(ukeys.size() / 16);
+  std::vector<uint64_t> ureps;
+  std::vector<int> uowner;
+  int rc = dht_lookup(ukeys.data(), m, ureps, uowner, st);
   if (rc) return rc;
+  std::vector<uint64_t> reps(2ull * n);
+  std::vector<int> owner(n);
+  for (int i = 0; i < n; ++i) {
+    reps[2ull * i] = ureps[2ull * uidx[i]];
+    reps[2ull * i + 1] = ureps[2ull * uidx[i] + 1];
+    owner[i] = uowner[uidx[i]];
+  }
+  std::vector<int> leader(m, -1);  // occurrence that fetches the block
   // host outputs: gather into staging, then DMA out
   std::vector<uint64_t> dst(n);
   if (mem_kind == CB_MEM_HOST) {
@@ -554,6 +578,8 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
       continue;
     }
     if (!sz) continue;
+    if (leader[uidx[i]] >= 0) continue;  // a repeat: filled from the leader below
+    leader[uidx[i]] = i;
     const uint64_t off = loc & kLocOffMask;
     const uint64_t src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
     us.push_back(total);
@@ -561,6 +587,19 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
     desc.push_back(CopyDesc{src, dst[i], sz, (dram || !local) ? 1u : 0u});
     total += (uint32_t)((sz + kCopyUnit - 1) / kCopyUnit);
     bytes += sz;
+  }
+  // repeats: device-local copies from the leader's output, after the gather
+  std::vector<CopyDesc> rdesc;
+  std::vector<uint32_t> rus;
+  uint32_t rtotal = 0;
+  for (int i = 0; i < n; ++i) {
+    const int l = leader[uidx[i]];
+    if (l < 0 || l == i || (found_out[i] & CB_FOUND_NOT_COPIED) || (found_out[i] & 0x0f) == CB_FOUND_MISS ||
+        !sizes_out[i])
+      continue;
+    rus.push_back(rtotal);
+    rdesc.push_back(CopyDesc{dst[l], dst[i], sizes_out[i], 0u});
+    rtotal += (uint32_t)((sizes_out[i] + kCopyUnit - 1) / kCopyUnit);
   }
   if (!desc.empty()) {
     us.push_back(total);
@@ -582,6 +621,25 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
                                                  num_sms, st);
                       }),
                 "gather");
+  }
+  if (!rdesc.empty()) {
+    rus.push_back(rtotal);
+    const size_t o_us = align_up(sizeof(CopyDesc) * rdesc.size(), 256);
+    const size_t need = o_us + 4 * rus.size();
+    // the gather above may still read its descriptors from d_scratch
+    CB_TRY_CUDA(cudaStreamSynchronize(st), "gather");
+    CB_TRY_CUDA(h_scratch.ensure(need), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(need), "device");
+    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    memcpy(h, rdesc.data(), sizeof(CopyDesc) * rdesc.size());
+    memcpy(h + o_us, rus.data(), 4 * rus.size());
+    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, need, cudaMemcpyHostToDevice, st), "H2D repeats");
+    const int nr = (int)rdesc.size();
+    CB_TRY_CUDA(launch_batch_copy(reinterpret_cast<const CopyDesc *>(d), reinterpret_cast<const uint32_t *>(d + o_us),
+                                  nr, rtotal, copy_engine, d_err, num_sms, st),
+                "repeat copies");
+    launches++;
   }
   // owners must not reuse pool extents before every reader is done
   CB_TRY_CUDA(dht->d_misc.ensure(256), "device");

@@ -65,6 +65,11 @@ def main():
     assert all(found), "found"
     for b, o, s in zip(req, outs, sizes):
         assert s == len(by_id[b]) and np.array_equal(o.cpu().numpy(), by_id[b]), ("bytes", b)
+    # repeated keys in one batch (fetched once, fanned out locally)
+    rep = req[:7] * 3 + [req[0]]
+    routs = [torch.empty(len(by_id[b]), dtype=torch.uint8, device=dev) for b in rep]
+    found, sizes = store.batch_get(rep, routs)
+    assert all(found) and all(np.array_equal(o.cpu().numpy(), by_id[b]) for o, b in zip(routs, rep)), "repeats"
     # host-memory outputs too
     houts = [np.empty(len(by_id[b]), np.uint8) for b in req[:20]]
     found, sizes = store.batch_get(req[:20], houts)
