@@ -356,8 +356,8 @@ def main():
         t_ev1.record()
         sync_all()
     elapsed = t_ev0.elapsed_time(t_ev1) / 1e3
-    remote_b = run_pass.remote_bytes
     st1 = store._n.stats()
+    remote_b = st1.peer_bytes_read - st0.peer_bytes_read  # crossed NVLink
     elapsed_max = reduce_max(elapsed, world)
     total_bytes = reduce_sum(put_b + get_b, world)
     value = total_bytes / elapsed_max / GB
@@ -514,8 +514,8 @@ def zipf_main(args, rank, world, local, device):
     st1 = store._n.stats()
     tot = reduce_sum(got, world)
     d = {f: getattr(st1, f) - getattr(st0, f) for f in ("remote_gpu_hits", "local_gpu_hits", "gather_ns",
-                                                        "gather_bytes", "kernel_launches")}
-    remote_b = d["remote_gpu_hits"] * size
+                                                        "gather_bytes", "kernel_launches", "peer_bytes_read")}
+    remote_b = d["peer_bytes_read"]  # fetched over NVLink (a key repeated in a batch crosses once)
     gather_s = d["gather_ns"] / 1e9
     nv = remote_b / gather_s / GB if gather_s else 0.0
     nv_min = -reduce_max(-nv, world)
@@ -531,6 +531,8 @@ def zipf_main(args, rank, world, local, device):
                    "l2": "every step reads 2.7 GB per GPU >> L2"},
         "populate_s": round(populate_s, 2),
         "remote_fraction": round(d["remote_gpu_hits"] / max(1, d["remote_gpu_hits"] + d["local_gpu_hits"]), 4),
+        "nvlink_bytes_per_step": int(remote_b / max(args.steps, 1)),
+        "logical_bytes_per_step": int(got / max(args.steps, 1)),
         "roofline": {"kernel": "copy_lsu (peer-load gather)", "bound": "nvlink" if world > 1 else "hbm",
                      "achieved": round(nv_min if world > 1 else 2 * d["gather_bytes"] / gather_s / GB, 2),
                      "peak": NVLINK_PEER_GBS if world > 1 else None, "unit": "GB/s",

@@ -88,6 +88,8 @@ typedef struct cb_stats {
   uint64_t scatter_ns, scatter_bytes, scatter_launches;
   uint64_t gather_ns, gather_bytes, gather_launches;
   uint64_t tier_ns, tier_bytes, tier_launches;
+  /* DHT payload bytes this rank read from / wrote to peers' pools (NVLink) */
+  uint64_t peer_bytes_read, peer_bytes_written;
 } cb_stats;
 
 /* Mirrors BlockLocation (include/cascade_distributed.hpp:62-80). */

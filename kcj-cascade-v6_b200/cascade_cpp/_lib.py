@@ -65,6 +65,7 @@ STATS_FIELDS = [
     "evicted_bytes", "promoted_bytes", "dropped_blocks", "kernel_launches",
     "sha_ns", "sha_bytes", "sha_launches", "scatter_ns", "scatter_bytes", "scatter_launches",
     "gather_ns", "gather_bytes", "gather_launches", "tier_ns", "tier_bytes", "tier_launches",
+    "peer_bytes_read", "peer_bytes_written",
 ]
 
 

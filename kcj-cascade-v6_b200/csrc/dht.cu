@@ -402,6 +402,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
       continue;
     }
     const uint64_t dst = dht->pool[owner] + (mine[j].loc & kLocOffMask);
+    if (owner != me) peer_bytes_written += sizes[i];
     us.push_back(total);
     desc.push_back(CopyDesc{dptr[i], dst, sizes[i], owner == me ? 0u : 1u});
     total += (uint32_t)((sizes[i] + kCopyUnit - 1) / kCopyUnit);
@@ -580,6 +581,7 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
     if (!sz) continue;
     if (leader[uidx[i]] >= 0) continue;  // a repeat: filled from the leader below
     leader[uidx[i]] = i;
+    if (!local) peer_bytes_read += sz;
     const uint64_t off = loc & kLocOffMask;
     const uint64_t src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
     us.push_back(total);

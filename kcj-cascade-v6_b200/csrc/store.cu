@@ -747,6 +747,8 @@ void Store::fill_stats(cb_stats *o) const {
   o->promoted_bytes = c.promoted_bytes;
   o->dropped_blocks = c.dropped_blocks;
   o->kernel_launches = launches;
+  o->peer_bytes_read = peer_bytes_read;
+  o->peer_bytes_written = peer_bytes_written;
   uint64_t *p = &o->sha_ns;  // sha, scatter, gather, tier: (ns, bytes, launches) each
   for (int k = 0; k < 4; ++k) {
     p[3 * k] = prof_ns[k];

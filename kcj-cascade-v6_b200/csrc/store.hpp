@@ -69,6 +69,7 @@ struct Store {
 
   uint64_t local_gpu_hits = 0, local_dram_hits = 0, remote_gpu_hits = 0, remote_dram_hits = 0,
            misses = 0, remote_dedup_hits = 0, remote_dedup_bytes = 0;
+  uint64_t peer_bytes_read = 0, peer_bytes_written = 0;  // not reset by clear (traffic counters)
 
   int rank = 0, world = 1;
   DhtState *dht = nullptr;
