@@ -60,7 +60,9 @@ def parse():
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
-    p.add_argument("--workload", default="config2", choices=["config2", "zipf", "spill"])
+    p.add_argument("--workload", default="config2", choices=["config2", "zipf", "spill", "sweep"])
+    p.add_argument("--sweep-sizes", default="4096,65536,1048576,4194304,16777216")
+    p.add_argument("--sweep-gib", type=float, default=16.0)
     p.add_argument("--spill-blocks", type=int, default=40000)
     p.add_argument("--spill-hbm-gb", type=float, default=120.0)
     p.add_argument("--spill-dram-gb", type=float, default=100.0)
@@ -320,6 +322,8 @@ def main():
         return zipf_main(args, rank, world, local, device)
     if args.workload == "spill":
         return spill_main(args, rank, world, local, device)
+    if args.workload == "sweep":
+        return sweep_main(args, rank, world, local, device)
     pool, ptrs, prefix = gpu_blocks(args, rank, device)
     sizes = np.full(len(ptrs), size, np.uint64)
     n_unique = pool.numel() // size
@@ -544,6 +548,88 @@ def zipf_main(args, rank, world, local, device):
     store.close()
     if world > 1:
         dist.destroy_process_group()
+
+
+def sweep_main(args, rank, world, local, device):
+    """Config 5: block sizes 4 KiB, 64 KiB, 1 MiB, 4 MiB, 16 MiB of bf16
+    N(0,1); each step is 512 ops, 30 % batch_put (half of them byte-identical
+    copies of a block this rank put earlier) and 70 % batch_get of uniformly
+    drawn keys this rank stored; 16 GiB of logical traffic per GPU per size
+    (--sweep-gib). Reports GB/s and p50/p99 step latency per size. On N GPUs
+    every call is a DHT collective."""
+    import torch
+    import cascade_cpp
+    out = {}
+    ops = 512
+    n_put = int(round(ops * 0.3))
+    n_get = ops - n_put
+    for size in [int(s) for s in args.sweep_sizes.split(",")]:
+        steps = max(2, int(args.sweep_gib * (1 << 30) // (ops * size)))
+        uniq_needed = steps * n_put // 2 + n_put + 1
+        cfg = cascade_cpp.DistributedConfig()
+        cfg.gpu_capacity_per_device = int(uniq_needed * size * 1.3) + (1 << 30)
+        cfg.dram_capacity = 0
+        cfg.device = local
+        cfg.index_log2 = max(16, int(np.ceil(np.log2(max(uniq_needed * 2.6, 2)))))
+        cfg.dht = world > 1
+        cfg.profile = False
+        store = cascade_cpp.DistributedStore(cfg)
+        g = torch.Generator(device=device).manual_seed(500 + rank)
+        src = torch.randn(uniq_needed * size // 2, generator=g, device=device, dtype=torch.bfloat16).view(torch.uint8)
+        base = np.uint64(src.data_ptr())
+        rng = np.random.default_rng(600 + rank)
+        outb = torch.empty(n_get * size, dtype=torch.uint8, device=device)
+        optrs = (np.uint64(outb.data_ptr()) + np.arange(n_get, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+        caps = np.full(n_get, size, np.uint64)
+        sizes = np.full(n_put, size, np.uint64)
+        # seed the store with one batch of unique blocks so gets have targets;
+        # source block j is stored under keys[j] (unique blocks are consecutive)
+        keys = np.empty((uniq_needed, 16), np.uint8)
+        p0 = (base + np.arange(n_put, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+        k, _ = store.put_ptrs(p0, sizes, True)
+        keys[:n_put] = k
+        nxt = n_put
+        lat = []
+        logical = 0
+        new = n_put - n_put // 2
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        t_all = time.perf_counter()
+        for s in range(steps):
+            # half new blocks, half copies of blocks put earlier (50 % dedup)
+            sel = np.concatenate([np.arange(nxt, nxt + new), rng.integers(0, nxt, n_put // 2)])
+            ptrs = (base + sel.astype(np.uint64) * np.uint64(size)).astype(np.uint64)
+            gk = keys[rng.integers(0, nxt, n_get)]
+            t0 = time.perf_counter()
+            k, st = store.put_ptrs(ptrs, sizes, True)
+            sz, f = store.get_ptrs(gk, optrs, caps, True)
+            lat.append(time.perf_counter() - t0)
+            logical += n_put * size + int(sz[(f & 0x0F) != 0].sum())
+            keys[nxt:nxt + new] = k[:new]
+            nxt += new
+        el = time.perf_counter() - t_all
+        el = reduce_max(el, world)
+        tot = reduce_sum(logical, world)
+        lat_ms = np.array(lat) * 1e3
+        out[str(size)] = {"gbs": round(tot / el / GB, 3), "steps": steps,
+                          "p50_ms": round(float(np.percentile(lat_ms, 50)), 3),
+                          "p99_ms": round(float(np.percentile(lat_ms, 99)), 3),
+                          "dedup_hits": int(store.get_stats().dedup_hits)}
+        store.close()
+        del src, outb
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "config 5 variable-block sweep: aggregate GB/s and p50/p99 step latency per size",
+            "n_gpus": world, "unit": "GB/s", "higher_is_better": True, "scaling": "weak", "dtype": "u8",
+            "data": "synthetic (seeded bf16 N(0,1) blocks generated on the GPU)",
+            "config": {"workload": f"config5: 512 ops/step (30% put, half of them copies; 70% get, uniform keys), "
+                                   f"{args.sweep_gib} GiB logical per GPU per size",
+                       "parallelism": f"hash-sharded DHT over {world} GPUs" if world > 1 else "single store"},
+            "per_size": out}), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
 
 
 def host_link_peaks(device, nbytes=4 << 30, reps=3):
