@@ -65,7 +65,10 @@ typedef struct cb_config {
   uint64_t staging_bytes;       /* device staging for host-memory callers   */
   int32_t profile;              /* 1: time each kernel with CUDA events     */
   int32_t hash_lanes;           /* SHA-256 chains per warp: 8, 16 or 32     */
-  uint64_t reserved[6];
+  uint64_t replica_bytes;       /* DHT: HBM for replicas of hot remote blocks */
+  int32_t locality_aware;       /* DHT: replicate hot remote blocks locally */
+  uint32_t promotion_threshold; /* accesses before a block may be replicated */
+  uint64_t reserved[4];
 } cb_config;
 
 /* Mirrors DistributedStore::Stats (include/cascade_distributed.hpp:386-409). */

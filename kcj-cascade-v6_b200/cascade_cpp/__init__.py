@@ -287,6 +287,7 @@ class DistributedConfig:
         self.index_log2 = 16
         self.staging_bytes = 1 << 30  # device staging for host-memory callers
         self.dht = None               # None: shard over all ranks when WORLD_SIZE > 1
+        self.replica_bytes = 0        # DHT: HBM for replicas of hot remote blocks (0 = auto)
         self.profile = False          # time every kernel with CUDA events (stats *_ns)
         self.hash_lanes = 32          # SHA-256 chains per warp (8, 16, 32)
 
@@ -533,6 +534,9 @@ class DistributedStore(_StoreBase):
         c.staging_bytes = int(cfg.staging_bytes)
         c.profile = 1 if cfg.profile else 0
         c.hash_lanes = int(cfg.hash_lanes)
+        c.locality_aware = 1 if cfg.locality_aware else 0
+        c.promotion_threshold = int(cfg.promotion_threshold)
+        c.replica_bytes = int(cfg.replica_bytes)
         self._init_native(c)
         self._rank, self._world = 0, 1
         world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -52,7 +52,10 @@ class cb_config(C.Structure):
         ("staging_bytes", C.c_uint64),
         ("profile", C.c_int32),
         ("hash_lanes", C.c_int32),
-        ("reserved", C.c_uint64 * 6),
+        ("replica_bytes", C.c_uint64),
+        ("locality_aware", C.c_int32),
+        ("promotion_threshold", C.c_uint32),
+        ("reserved", C.c_uint64 * 4),
     ]
 
 

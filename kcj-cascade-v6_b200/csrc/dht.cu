@@ -65,6 +65,57 @@ struct DhtState {
   DevBuf d_send, d_recv, d_misc;
   PinnedBuf h_send, h_recv, h_misc;
   double timeout_s = 600.0;
+
+  // Locality-aware placement (DistributedStore::record_access /
+  // should_promote_local / promote_to_local_gpu, src/distributed_backend.cpp:
+  // 1224-1275; AccessRecord, include/cascade_distributed.hpp:162-180): a
+  // block this rank keeps fetching from a peer is copied into a local replica
+  // region and served from local HBM afterwards. Blocks are content-addressed
+  // and immutable, so a replica never goes stale; evicting one only drops it.
+  bool locality = false;
+  uint32_t threshold = 3;
+  uint8_t *rbase = nullptr;  // replica region (local HBM)
+  uint64_t rbytes = 0;
+  ExtentAllocator ralloc;
+  struct Rep {
+    uint64_t off, size;
+    std::list<HKey>::iterator lru;
+  };
+  std::unordered_map<HKey, Rep, HKeyHash> rmap;
+  std::list<HKey> rlru;  // front = most recent
+  struct Access {
+    uint32_t total = 0, local = 0, remote = 0, wtotal = 0, wremote = 0;
+    float ema = 0.f;
+  };
+  std::unordered_map<HKey, Access, HKeyHash> access;
+
+  void record_access(const HKey &k, bool remote) {
+    Access &a = access[k];
+    a.total++;
+    a.wtotal++;
+    if (remote) {
+      a.remote++;
+      a.wremote++;
+    } else {
+      a.local++;
+    }
+    if (a.wtotal >= 8) {  // AccessRecord::WINDOW_SIZE, EMA_ALPHA = 0.3
+      const float cur = static_cast<float>(a.wremote) / a.wtotal;
+      a.ema = 0.3f * cur + (1.0f - 0.3f) * a.ema;
+      a.wremote = 0;
+      a.wtotal = 0;
+    }
+  }
+  bool should_promote(const HKey &k) const {
+    auto it = access.find(k);
+    return it != access.end() && it->second.total >= threshold && it->second.ema > 0.5f;
+  }
+  void clear_replicas() {
+    rmap.clear();
+    rlru.clear();
+    access.clear();
+    ralloc.reset(rbytes, 256);
+  }
 };
 
 // ------------------------------------------------------------ plumbing
@@ -244,6 +295,17 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   rank = r;
   world = W;
   policy.set_direct_dram_placement(false);
+  if (cfg.locality_aware) {
+    uint64_t rb = cfg.replica_bytes ? cfg.replica_bytes : std::min<uint64_t>(pool_bytes / 32, 4ull << 30);
+    rb = rb / 256 * 256;
+    if (rb) {
+      CB_TRY_CUDA(cudaMalloc(&dht->rbase, rb), "replica region");
+      dht->rbytes = rb;
+      dht->ralloc.reset(rb, 256);
+      dht->locality = true;
+      dht->threshold = cfg.promotion_threshold ? cfg.promotion_threshold : 3;
+    }
+  }
   return CB_OK;
 }
 
@@ -254,6 +316,7 @@ void Store::dht_detach() {
     dht->comm = nullptr;
   }
   for (void *p : dht->opened) cudaIpcCloseMemHandle(p);
+  if (dht->rbase) cudaFree(dht->rbase);
   dht->d_send.release();
   dht->d_recv.release();
   dht->d_misc.release();
@@ -506,17 +569,27 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
                    uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
   const int me = dht->me;
-  // A key repeated inside the batch (hot keys under a skewed access
-  // pattern) is looked up and fetched over NVLink once; the other
-  // occurrences are filled from the first copy with a local device copy.
-  std::vector<int> uidx(n);
+  // Replica hits are served from local HBM. Other keys repeated inside the
+  // batch (hot keys under a skewed access pattern) are looked up and fetched
+  // over NVLink once; the other occurrences are filled from the first copy.
+  std::vector<int> uidx(n, -1);
+  std::vector<int64_t> rep_off(n, -1);
   std::vector<uint8_t> ukeys;
   ukeys.reserve(16ull * n);
   {
     std::unordered_map<HKey, int, HKeyHash> first;
     first.reserve(2ull * n);
     for (int i = 0; i < n; ++i) {
-      auto ins = first.emplace(to_hkey(keys + 16 * i), (int)(ukeys.size() / 16));
+      const HKey k = to_hkey(keys + 16 * i);
+      if (dht->locality) {
+        auto r = dht->rmap.find(k);
+        if (r != dht->rmap.end()) {
+          rep_off[i] = (int64_t)r->second.off;
+          dht->rlru.splice(dht->rlru.begin(), dht->rlru, r->second.lru);
+          continue;
+        }
+      }
+      auto ins = first.emplace(k, (int)(ukeys.size() / 16));
       if (ins.second) ukeys.insert(ukeys.end(), keys + 16 * i, keys + 16 * i + 16);
       uidx[i] = ins.first->second;
     }
@@ -524,11 +597,17 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
   const int m = (int)(ukeys.size() / 16);
   std::vector<uint64_t> ureps;
   std::vector<int> uowner;
-  int rc = dht_lookup(ukeys.data(), m, ureps, uowner, st);
+  int rc = dht_lookup(ukeys.data(), m, ureps, uowner, st);  // collective, also when m == 0
   if (rc) return rc;
-  std::vector<uint64_t> reps(2ull * n);
-  std::vector<int> owner(n);
+  std::vector<uint64_t> reps(2ull * n, 0);
+  std::vector<int> owner(n, me);
   for (int i = 0; i < n; ++i) {
+    if (rep_off[i] >= 0) {
+      const HKey k = to_hkey(keys + 16 * i);
+      reps[2ull * i] = (uint64_t)rep_off[i];
+      reps[2ull * i + 1] = kMetaOccupied | (dht->rmap.at(k).size & kSizeMask);
+      continue;
+    }
     reps[2ull * i] = ureps[2ull * uidx[i]];
     reps[2ull * i + 1] = ureps[2ull * uidx[i] + 1];
     owner[i] = uowner[uidx[i]];
@@ -559,7 +638,8 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
   for (int i = 0; i < n; ++i) {
     const uint64_t meta = reps[2ull * i + 1], loc = reps[2ull * i];
     const uint64_t sz = meta & kSizeMask;
-    const bool dram = (loc & kLocDram) != 0;
+    const bool replica = rep_off[i] >= 0;
+    const bool dram = !replica && (loc & kLocDram) != 0;
     const bool local = owner[i] == me;
     sizes_out[i] = 0;
     if (!(meta & kMetaOccupied)) {
@@ -574,34 +654,69 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
     if (local && dram) local_dram_hits++;
     if (!local && !dram) remote_gpu_hits++;
     if (!local && dram) remote_dram_hits++;
+    if (dht->locality) dht->record_access(to_hkey(keys + 16 * i), !local);
     if (sz > caps[i] || (dram && !local)) {  // too small, or a peer's pinned DRAM (not mapped here)
       found_out[i] |= CB_FOUND_NOT_COPIED;
       continue;
     }
     if (!sz) continue;
-    if (leader[uidx[i]] >= 0) continue;  // a repeat: filled from the leader below
-    leader[uidx[i]] = i;
-    if (!local) peer_bytes_read += sz;
-    const uint64_t off = loc & kLocOffMask;
-    const uint64_t src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
+    uint64_t src;
+    uint64_t flags = 0;
+    if (replica) {
+      src = (uint64_t)dht->rbase + loc;
+    } else {
+      if (leader[uidx[i]] >= 0) continue;  // a repeat: filled from the leader below
+      leader[uidx[i]] = i;
+      if (!local) peer_bytes_read += sz;
+      const uint64_t off = loc & kLocOffMask;
+      src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
+      flags = (dram || !local) ? 1u : 0u;  // peer and pinned-host sources: plain loads
+    }
     us.push_back(total);
-    // peer and pinned-host sources are read with plain (coherent) loads
-    desc.push_back(CopyDesc{src, dst[i], sz, (dram || !local) ? 1u : 0u});
+    desc.push_back(CopyDesc{src, dst[i], sz, flags});
     total += (uint32_t)((sz + kCopyUnit - 1) / kCopyUnit);
     bytes += sz;
   }
-  // repeats: device-local copies from the leader's output, after the gather
+  // second pass (after the gather): repeats copied from their leader's
+  // output, and promotions of hot remote blocks into the replica region
   std::vector<CopyDesc> rdesc;
   std::vector<uint32_t> rus;
   uint32_t rtotal = 0;
+  auto add2 = [&](uint64_t s, uint64_t d, uint64_t sz) {
+    rus.push_back(rtotal);
+    rdesc.push_back(CopyDesc{s, d, sz, 0u});
+    rtotal += (uint32_t)((sz + kCopyUnit - 1) / kCopyUnit);
+  };
   for (int i = 0; i < n; ++i) {
+    if (uidx[i] < 0) continue;
     const int l = leader[uidx[i]];
     if (l < 0 || l == i || (found_out[i] & CB_FOUND_NOT_COPIED) || (found_out[i] & 0x0f) == CB_FOUND_MISS ||
         !sizes_out[i])
       continue;
-    rus.push_back(rtotal);
-    rdesc.push_back(CopyDesc{dst[l], dst[i], sizes_out[i], 0u});
-    rtotal += (uint32_t)((sizes_out[i] + kCopyUnit - 1) / kCopyUnit);
+    add2(dst[l], dst[i], sizes_out[i]);
+  }
+  if (dht->locality) {
+    for (int u = 0; u < m; ++u) {
+      const int l = leader[u];
+      if (l < 0 || (found_out[l] & 0x0f) != CB_FOUND_REMOTE_HBM) continue;
+      const HKey k = to_hkey(ukeys.data() + 16 * u);
+      if (dht->rmap.count(k) || !dht->should_promote(k)) continue;
+      const uint64_t sz = sizes_out[l];
+      uint64_t off = dht->ralloc.alloc(sz);
+      while (off == UINT64_MAX && !dht->rlru.empty()) {  // drop least recently used replicas
+        const HKey v = dht->rlru.back();
+        auto it = dht->rmap.find(v);
+        dht->ralloc.free(it->second.off, it->second.size);
+        dht->rlru.pop_back();
+        dht->rmap.erase(it);
+        off = dht->ralloc.alloc(sz);
+      }
+      if (off == UINT64_MAX) continue;
+      dht->rlru.push_front(k);
+      dht->rmap.emplace(k, DhtState::Rep{off, sz, dht->rlru.begin()});
+      add2(dst[l], (uint64_t)dht->rbase + off, sz);
+      replica_promotions++;
+    }
   }
   if (!desc.empty()) {
     us.push_back(total);
@@ -735,3 +850,9 @@ int cb_dht_unique_id(uint8_t *uid_out) {
 }
 
 }  // extern "C"
+
+namespace cb {
+void Store::dht_clear_replicas() {
+  if (dht) dht->clear_replicas();
+}
+}  // namespace cb

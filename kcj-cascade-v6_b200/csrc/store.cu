@@ -718,7 +718,11 @@ int Store::clear(cudaStream_t st) {
   table_used = table_tombs = 0;
   local_gpu_hits = local_dram_hits = remote_gpu_hits = remote_dram_hits = misses = 0;
   remote_dedup_hits = remote_dedup_bytes = 0;
-  if (dht) return dht_barrier();
+  replica_promotions = 0;
+  if (dht) {
+    dht_clear_replicas();
+    return dht_barrier();
+  }
   return CB_OK;
 }
 
@@ -740,7 +744,7 @@ void Store::fill_stats(cb_stats *o) const {
   o->dedup_bytes_saved = dht ? remote_dedup_bytes : c.dedup_bytes_saved;
   o->gpu_evictions = c.gpu_evictions;
   o->dram_evictions = c.dram_evictions;
-  o->promotions_to_local = c.promotions;
+  o->promotions_to_local = c.promotions + replica_promotions;
   o->total_blocks = policy.size();
   o->prefix_blocks = c.prefix_blocks;
   o->evicted_bytes = c.evicted_bytes;

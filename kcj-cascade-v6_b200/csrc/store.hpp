@@ -70,6 +70,7 @@ struct Store {
   uint64_t local_gpu_hits = 0, local_dram_hits = 0, remote_gpu_hits = 0, remote_dram_hits = 0,
            misses = 0, remote_dedup_hits = 0, remote_dedup_bytes = 0;
   uint64_t peer_bytes_read = 0, peer_bytes_written = 0;  // not reset by clear (traffic counters)
+  uint64_t replica_promotions = 0;  // DHT: hot remote blocks copied to local HBM
 
   int rank = 0, world = 1;
   DhtState *dht = nullptr;
@@ -155,6 +156,7 @@ struct Store {
   int dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, std::vector<int> &owner,
                  cudaStream_t st);
   int dht_locate(const uint8_t *key, cb_location *out, int32_t *found);
+  void dht_clear_replicas();
   int dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
               const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out,
               uint8_t *status_out, cudaStream_t st);

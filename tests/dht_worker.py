@@ -70,6 +70,26 @@ def main():
     routs = [torch.empty(len(by_id[b]), dtype=torch.uint8, device=dev) for b in rep]
     found, sizes = store.batch_get(rep, routs)
     assert all(found) and all(np.array_equal(o.cpu().numpy(), by_id[b]) for o, b in zip(routs, rep)), "repeats"
+    # locality promotion: a remote block fetched 16 times (EMA of the remote
+    # rate passes 0.5 after two windows of 8) is replicated into local HBM
+    # and served locally from then on
+    hot = next(b for b in uniq if owner(b, world) != rank and len(by_id[b]) > 0)
+    p0 = store.get_stats().promotions_to_local
+    hk = np.frombuffer(bytes.fromhex(hot), np.uint8).reshape(1, 16)
+    hout = torch.empty(len(by_id[hot]), dtype=torch.uint8, device=dev)
+    optr = np.array([hout.data_ptr()], np.uint64)
+    cap = np.array([hout.numel()], np.uint64)
+    codes = []
+    for _ in range(20):  # same number of collective calls on every rank
+        s, f = store.get_ptrs(hk, optr, cap, True)
+        codes.append(int(f[0]))
+    # CB_FOUND_REMOTE_HBM (3) until promoted, CB_FOUND_LOCAL_HBM (1) after
+    assert codes[0] == 3 and codes[-1] == 1, codes
+    first_local = codes.index(1)
+    assert all(c == 3 for c in codes[:first_local]) and all(c == 1 for c in codes[first_local:]), codes
+    assert first_local >= 8, codes  # the EMA needs two full windows of remote accesses
+    assert np.array_equal(hout.cpu().numpy(), by_id[hot]), "replica bytes"
+    assert store.get_stats().promotions_to_local == p0 + 1
     # host-memory outputs too
     houts = [np.empty(len(by_id[b]), np.uint8) for b in req[:20]]
     found, sizes = store.batch_get(req[:20], houts)
