@@ -7,7 +7,12 @@
 //     in an OpenMP loop — the reference drivers' CPU hashing pass;
 //   * CascadeStore.put_batch / get_batch (cascade_core.cpp:1358-1390), the
 //     reference's parallel OpenMP batch API, which bindings.cpp:68-85 leaves
-//     unbound.
+//     unbound;
+//   * kv_compress / kv_decompress: KVCompressor::compress / decompress
+//     (cascade_core.cpp:908-967), the INT8 format of the DRAM tier when
+//     kv_compression is on. The header's 3 padding bytes are indeterminate in
+//     the reference; the shim zeroes the CompressionMeta it passes so they
+//     come out as zero.
 // The store is configured for the CPU path only: use_gpu = false, SHM tier
 // (ShmBackend on /dev/shm, cascade_core.cpp:269-497), no Lustre, no prefetch.
 #include <pybind11/numpy.h>
@@ -16,6 +21,7 @@
 
 #include <omp.h>
 
+#include <cstring>
 #include <memory>
 #include <string>
 #include <vector>
@@ -76,6 +82,26 @@ PYBIND11_MODULE(cascade_ref, m) {
       py::arg("packed"), py::arg("offsets"), py::arg("sizes"), py::arg("threads") = 0);
 
   m.def("max_threads", []() { return omp_get_max_threads(); });
+
+  m.def("kv_compress", [](u8arr a) {
+    auto b = a.request();
+    cascade::CompressionMeta meta;
+    std::memset(&meta, 0, sizeof(meta));
+    std::vector<uint8_t> c = cascade::KVCompressor::compress(static_cast<const uint8_t *>(b.ptr), b.size, meta);
+    return py::bytes(reinterpret_cast<const char *>(c.data()), c.size());
+  });
+
+  m.def("kv_decompress", [](u8arr comp, size_t orig_size) {
+    auto b = comp.request();
+    const uint8_t *p = static_cast<const uint8_t *>(b.ptr);
+    cascade::CompressionMeta meta;
+    std::memset(&meta, 0, sizeof(meta));
+    std::memcpy(&meta, p, sizeof(meta));
+    std::string out((orig_size / 2) * 2, '\0');
+    const bool ok = cascade::KVCompressor::decompress(p, b.size, meta, reinterpret_cast<uint8_t *>(&out[0]),
+                                                      orig_size);
+    return py::make_tuple(ok, py::bytes(out));
+  });
 
   py::class_<CascadeStore, std::unique_ptr<CascadeStore>>(m, "CascadeStore")
       .def(py::init(&make_store), py::arg("shm_capacity"), py::arg("shm_path"),

@@ -22,6 +22,18 @@ def gen(kind, seed, size):
         return W.kv_block_fp16(seed, size)
     if kind == "kv_bf16":
         return W.kv_block_bf16(seed, size)
+    if kind == "kv_fp16_pos":  # one sign only: the zero point stays inside int8
+        return np.abs(W.kv_block_fp16(seed, size).view(np.float16)).view(np.uint8)
+    if kind == "kv_fp16_small":
+        rng = np.random.default_rng(seed)
+        return (rng.standard_normal(size // 2) * 1e-3).astype(np.float16).view(np.uint8)
+    if kind == "int16_full":  # both int16 extremes present
+        rng = np.random.default_rng(seed)
+        v = rng.integers(-32768, 32768, size // 2, dtype=np.int64).astype(np.int16)
+        v[: min(2, v.size)] = [-32768, 32767][: min(2, v.size)]
+        return v.view(np.uint8)
+    if kind == "const_i16":  # max == min: scale 1
+        return np.full(size // 2, seed - 32768, np.int16).view(np.uint8)
     if kind == "fips_abc":
         return np.frombuffer(b"abc", np.uint8)
     if kind == "fips_448":
