@@ -68,7 +68,12 @@ typedef struct cb_config {
   uint64_t replica_bytes;       /* DHT: HBM for replicas of hot remote blocks */
   int32_t locality_aware;       /* DHT: replicate hot remote blocks locally */
   uint32_t promotion_threshold; /* accesses before a block may be replicated */
-  uint64_t reserved[4];
+  int32_t kv_compression;       /* kv_compression: DRAM-tier copies of blocks
+                                   >= 64 B in the INT8 KVCompressor format
+                                   (src/cascade_core.cpp:908-967); a read of
+                                   such a block returns (size/2)*2 bytes    */
+  int32_t reserved32;
+  uint64_t reserved[3];
 } cb_config;
 
 /* Mirrors DistributedStore::Stats (include/cascade_distributed.hpp:386-409). */
@@ -118,6 +123,24 @@ int cb_destroy(cb_store *s);
 /* Message of the last failed call on this store (or of cb_create when s is
  * NULL). Replaces the CUDA_CHECK fprintf of src/gpu_backend.cu:43-51. */
 const char *cb_last_error(const cb_store *s);
+
+/* Batched INT8 KV compression of n device blocks (srcs[i], sizes[i] >= 2
+ * bytes) into dsts[i] (device memory, 8 + sizes[i]/2 bytes each) in the
+ * format [f32 scale][i8 zero_point][3 zero bytes][sizes[i]/2 x i8] — the
+ * format of DRAM-tier blocks under kv_compression. Replaces
+ * KVCompressor::compress (src/cascade_core.cpp:908-944,
+ * include/cascade.hpp:400-403). */
+int cb_kv_compress_batch(cb_store *s, const void *const *srcs, const uint64_t *sizes, void *const *dsts,
+                         int32_t n, void *stream);
+
+/* Inverse of cb_kv_compress_batch: packed block i (srcs[i], comp_sizes[i]
+ * bytes, device memory) -> (orig_sizes[i]/2)*2 bytes at dsts[i]. ok_out[i]
+ * (may be NULL) = 0 and nothing written when comp_sizes[i] < 8 +
+ * orig_sizes[i]/2. Replaces KVCompressor::decompress
+ * (src/cascade_core.cpp:946-967, include/cascade.hpp:405-407). */
+int cb_kv_decompress_batch(cb_store *s, const void *const *srcs, const uint64_t *comp_sizes,
+                           const uint64_t *orig_sizes, void *const *dsts, int32_t n, uint8_t *ok_out,
+                           void *stream);
 
 /* Batched SHA-256 of n blocks on the GPU; digests_out = n*32 host bytes.
  * Replaces n calls of compute_block_id (src/cascade_core.cpp:47-58) /

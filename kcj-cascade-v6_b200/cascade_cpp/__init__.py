@@ -40,7 +40,7 @@ except Exception:  # pragma: no cover - torch is present in this image
 __all__ = [
     "DistributedConfig", "DistributedStore", "DistributedStats", "BlockLocation",
     "CascadeConfig", "CascadeStore", "CascadeStats", "compute_block_id",
-    "compute_block_ids", "block_id_to_key", "key_to_block_id", "CascadeError",
+    "compute_block_ids", "block_id_to_key", "key_to_block_id", "CascadeError", "KVCompressor",
 ]
 
 _lib_handle = None
@@ -165,6 +165,17 @@ class _Native:
                                           _ptr(sizes), _ptr(found), self.stream_ptr(kind)))
         return sizes, found
 
+    def kv_compress(self, srcs, sizes, dsts):
+        self._check(self.lib.cb_kv_compress_batch(self.h, _ptr(srcs), _ptr(sizes), _ptr(dsts), len(srcs),
+                                                  self.stream_ptr(L.CB_MEM_DEVICE)))
+
+    def kv_decompress(self, srcs, comp_sizes, orig_sizes, dsts) -> np.ndarray:
+        ok = np.zeros(len(srcs), np.uint8)
+        self._check(self.lib.cb_kv_decompress_batch(self.h, _ptr(srcs), _ptr(comp_sizes), _ptr(orig_sizes),
+                                                    _ptr(dsts), len(srcs), _ptr(ok),
+                                                    self.stream_ptr(L.CB_MEM_DEVICE)))
+        return ok
+
     def contains(self, keys) -> np.ndarray:
         n = len(keys)
         found = np.zeros(n, np.uint8)
@@ -255,6 +266,88 @@ def compute_block_ids(blocks: Sequence) -> list[str]:
     sizes = np.array([v[1] for v in views], np.uint64)
     dig = h.hash(ptrs, sizes, kind)
     return [row[:16].tobytes().hex() for row in dig]
+
+
+# ----------------------------------------------------------- KV compressor
+
+class KVCompressor:
+    """KVCompressor (include/cascade.hpp:397-418, src/cascade_core.cpp:
+    908-967) on the GPU: INT8 compression of fp16 KV blocks into
+    [f32 scale][i8 zero_point][3 zero bytes][size/2 x i8], the format of
+    DRAM-tier blocks under ``kv_compression``. Blocks are contiguous CUDA
+    uint8 tensors of one device; the batched forms take one launch pair per
+    batch."""
+
+    _stores: dict = {}
+
+    @staticmethod
+    def compressed_size(original_size: int) -> int:
+        return 8 + int(original_size) // 2
+
+    @staticmethod
+    def original_size(compressed_size: int) -> int:
+        return (int(compressed_size) - 8) * 2
+
+    @classmethod
+    def _native(cls, device: int) -> "_Native":
+        n = cls._stores.get(device)
+        if n is None:
+            c = L.cb_config()
+            _native_lib().cb_config_init(C.byref(c))
+            c.gpu_capacity_bytes = 0  # no pool: the store only lends its scratch buffers and stream
+            c.dram_capacity_bytes = 0
+            c.index_log2 = 4
+            c.device = device
+            n = cls._stores[device] = _Native(c)
+        return n
+
+    @staticmethod
+    def _check_blocks(blocks) -> int:
+        dev = None
+        for b in blocks:
+            if not (torch is not None and isinstance(b, torch.Tensor) and b.is_cuda and b.dtype == torch.uint8
+                    and b.is_contiguous()):
+                raise TypeError("KVCompressor works on contiguous CUDA uint8 tensors")
+            if dev is not None and b.device.index != dev:
+                raise ValueError("all blocks of a batch must be on one device")
+            dev = b.device.index
+        return 0 if dev is None else dev
+
+    @classmethod
+    def compress_batch(cls, blocks):
+        dev = cls._check_blocks(blocks)
+        for b in blocks:
+            if b.numel() < 2:
+                raise ValueError("compression needs at least one 16-bit value")
+        outs = [torch.empty(cls.compressed_size(b.numel()), dtype=torch.uint8, device=b.device) for b in blocks]
+        if blocks:
+            cls._native(dev).kv_compress(np.array([b.data_ptr() for b in blocks], np.uint64),
+                                         np.array([b.numel() for b in blocks], np.uint64),
+                                         np.array([o.data_ptr() for o in outs], np.uint64))
+        return outs
+
+    @classmethod
+    def compress(cls, block):
+        return cls.compress_batch([block])[0]
+
+    @classmethod
+    def decompress_batch(cls, packed, original_sizes):
+        """Returns one tensor of (original_size/2)*2 bytes per block, or None
+        where the packed block is too short (the reference's false)."""
+        dev = cls._check_blocks(packed)
+        outs = [torch.empty(int(s) // 2 * 2, dtype=torch.uint8, device=p.device)
+                for p, s in zip(packed, original_sizes)]
+        if not packed:
+            return []
+        ok = cls._native(dev).kv_decompress(np.array([p.data_ptr() for p in packed], np.uint64),
+                                            np.array([p.numel() for p in packed], np.uint64),
+                                            np.array([int(s) for s in original_sizes], np.uint64),
+                                            np.array([o.data_ptr() for o in outs], np.uint64))
+        return [o if k else None for o, k in zip(outs, ok)]
+
+    @classmethod
+    def decompress(cls, packed, original_size: int):
+        return cls.decompress_batch([packed], [original_size])[0]
 
 
 # ------------------------------------------------------------------- config
@@ -517,8 +610,6 @@ class DistributedStore(_StoreBase):
 
     def __init__(self, cfg: DistributedConfig | None = None):
         cfg = cfg or DistributedConfig()
-        if cfg.kv_compression:
-            _warn_once("kv_compression is lossy and not part of the bit-exact path; ignored")
         if cfg.lustre_path:
             _warn_once("the Lustre tier is out of scope; lustre_path ignored")
         c = L.cb_config()
@@ -537,6 +628,7 @@ class DistributedStore(_StoreBase):
         c.locality_aware = 1 if cfg.locality_aware else 0
         c.promotion_threshold = int(cfg.promotion_threshold)
         c.replica_bytes = int(cfg.replica_bytes)
+        c.kv_compression = 1 if cfg.kv_compression else 0
         self._init_native(c)
         self._rank, self._world = 0, 1
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -601,8 +693,6 @@ class CascadeStore(_StoreBase):
 
     def __init__(self, cfg: CascadeConfig | None = None):
         cfg = cfg or CascadeConfig()
-        if cfg.kv_compression:
-            _warn_once("kv_compression is lossy and not part of the bit-exact path; ignored")
         c = L.cb_config()
         _native_lib().cb_config_init(C.byref(c))
         c.gpu_capacity_bytes = int(cfg.gpu_capacity_bytes) if cfg.use_gpu else 0
@@ -614,6 +704,7 @@ class CascadeStore(_StoreBase):
         c.index_log2 = int(cfg.index_log2)
         c.copy_engine = int(cfg.copy_engine)
         c.staging_bytes = int(cfg.staging_bytes)
+        c.kv_compression = 1 if cfg.kv_compression else 0
         self._init_native(c)
 
     def get_stats(self) -> CascadeStats:
@@ -623,4 +714,5 @@ class CascadeStore(_StoreBase):
                             lustre_hits=0, misses=st.misses, dedup_hits=st.dedup_hits,
                             gpu_evictions=st.gpu_evictions, shm_evictions=st.dram_evictions,
                             promotions_to_gpu=st.promotions_to_local, promotions_to_shm=0,
-                            prefetch_completed=0, compression_savings_bytes=0, shm_puts=0, lustre_puts=0)
+                            prefetch_completed=0, compression_savings_bytes=st.compression_savings, shm_puts=0,
+                            lustre_puts=0)

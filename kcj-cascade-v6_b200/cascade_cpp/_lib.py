@@ -55,7 +55,9 @@ class cb_config(C.Structure):
         ("replica_bytes", C.c_uint64),
         ("locality_aware", C.c_int32),
         ("promotion_threshold", C.c_uint32),
-        ("reserved", C.c_uint64 * 4),
+        ("kv_compression", C.c_int32),
+        ("reserved32", C.c_int32),
+        ("reserved", C.c_uint64 * 3),
     ]
 
 
@@ -96,6 +98,8 @@ SIGNATURES = [
     ("cb_create", C.c_int, [C.POINTER(cb_config), C.POINTER(_P)]),
     ("cb_destroy", C.c_int, [_P]),
     ("cb_last_error", C.c_char_p, [_P]),
+    ("cb_kv_compress_batch", C.c_int, [_P, _P, _P, _P, C.c_int32, _P]),
+    ("cb_kv_decompress_batch", C.c_int, [_P, _P, _P, _P, _P, C.c_int32, _P, _P]),
     ("cb_hash_batch", C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, _P, _P]),
     ("cb_put_batch", C.c_int, [_P, _P, _P, _P, _P, C.c_int32, C.c_int32, _P, _P, _P]),
     ("cb_get_batch", C.c_int, [_P, _P, C.c_int32, _P, _P, C.c_int32, _P, _P, _P]),

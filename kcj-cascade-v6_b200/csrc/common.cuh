@@ -41,7 +41,9 @@ CB_HD uint64_t slot_hash(const Key &k) { return k.hi ^ (k.lo >> 29) ^ (k.lo << 3
 // ---------------------------------------------------------------------------
 // Device index slot (32 B, one sector). Open addressing, linear probing.
 //   meta: bit 63 occupied, bit 62 tombstone, bit 61 claim-in-progress,
-//         bit 48 prefix flag, bits 0..47 logical block size.
+//         bit 49 packed (the DRAM copy is INT8-packed, kv_compression),
+//         bit 48 prefix flag, bits 0..47 logical block size (for a packed
+//         block: its unpacked size).
 //   loc : bit 63 tier (0 = HBM pool, 1 = pinned DRAM arena), bits 0..62 byte
 //         offset inside that arena.
 // ---------------------------------------------------------------------------
@@ -54,6 +56,7 @@ struct __align__(16) Slot {
 constexpr uint64_t kMetaOccupied = 1ull << 63;
 constexpr uint64_t kMetaTomb = 1ull << 62;
 constexpr uint64_t kMetaClaim = 1ull << 61;
+constexpr uint64_t kMetaPacked = 1ull << 49;
 constexpr uint64_t kMetaPrefix = 1ull << 48;
 constexpr uint64_t kSizeMask = (1ull << 48) - 1;
 constexpr uint64_t kLocDram = 1ull << 63;
@@ -72,8 +75,10 @@ struct CopyDesc {
   uint64_t src;
   uint64_t dst;
   uint64_t size;
-  uint64_t flags;  // bit 0: either side is host memory (no TMA)
+  uint64_t flags;  // kCopyHost | kCopyUnpack
 };
+constexpr uint64_t kCopyHost = 1;    // either side is host or peer memory (no TMA)
+constexpr uint64_t kCopyUnpack = 2;  // src is an INT8-packed block; size = unpacked bytes
 
 // Result of a device lookup for one get request.
 struct GetResult {

@@ -17,7 +17,11 @@
 //    thread, with streaming cache hints.
 // Units touching host memory (tier moves), units whose addresses are not
 // 16-byte aligned, and the sub-16-byte tail of a unit always use the LSU path.
+// Descriptors flagged kCopyUnpack (reads of INT8-packed DRAM-tier blocks)
+// are unpacked by the same LSU threads (kvquant.cuh).
 #include "kernels.cuh"
+#include "kvquant.cuh"
+#include "units.cuh"
 
 namespace cb {
 
@@ -28,19 +32,6 @@ constexpr int kLsuCtasPerSm = 8;
 constexpr int kTmaStages = 6;
 constexpr uint32_t kTmaStageBytes = 32 * 1024;
 constexpr uint64_t kWaitLimit = 1ull << 24;  // try_wait rounds before giving up
-
-// Largest i with unit_start[i] <= u (requests with no units are skipped).
-CB_D int find_req(const uint32_t *unit_start, int n, uint32_t u) {
-  int lo = 0, hi = n - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (unit_start[mid] <= u)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  return lo;
-}
 
 CB_D uint4 ld_dev16(const uint4 *p) {
   uint4 r;
@@ -101,10 +92,15 @@ CB_D void copy_range_lsu(const uint8_t *s, uint8_t *d, uint64_t len, int tid, in
   }
 }
 
-CB_D void cta_unit_range(uint32_t total_units, uint32_t &u0, uint32_t &u1) {
-  const uint32_t per = (total_units + gridDim.x - 1) / gridDim.x;
-  u0 = blockIdx.x * per;
-  u1 = min(total_units, u0 + per);
+// One unit of a descriptor through the LSU: a plain copy or an unpack.
+CB_D void lsu_unit(const CopyDesc &d, uint64_t off, uint64_t len, int tid, int nt) {
+  if (d.flags & kCopyUnpack) {
+    unpack_range(reinterpret_cast<const uint8_t *>(d.src), reinterpret_cast<uint8_t *>(d.dst), off, len, tid,
+                 nt);
+  } else {
+    copy_range_lsu(reinterpret_cast<const uint8_t *>(d.src) + off, reinterpret_cast<uint8_t *>(d.dst) + off,
+                   len, tid, nt, (d.flags & kCopyHost) != 0);
+  }
 }
 
 __global__ void __launch_bounds__(kLsuThreads) copy_lsu_kernel(const CopyDesc *__restrict__ desc,
@@ -120,9 +116,7 @@ __global__ void __launch_bounds__(kLsuThreads) copy_lsu_kernel(const CopyDesc *_
     const uint64_t off = (uint64_t)(u - unit_start[i]) * kCopyUnit;
     if (off >= d.size) continue;
     const uint64_t len = min(kCopyUnit, d.size - off);
-    copy_range_lsu(reinterpret_cast<const uint8_t *>(d.src) + off,
-                   reinterpret_cast<uint8_t *>(d.dst) + off, len, threadIdx.x, blockDim.x,
-                   (d.flags & 1) != 0);
+    lsu_unit(d, off, len, threadIdx.x, blockDim.x);
   }
 }
 
@@ -181,7 +175,7 @@ struct PieceIter {
 };
 
 CB_D bool tma_unit(const CopyDesc &d, uint64_t off) {
-  return !(d.flags & 1) && (((d.src + off) | (d.dst + off)) & 15) == 0;
+  return !(d.flags & (kCopyHost | kCopyUnpack)) && (((d.src + off) | (d.dst + off)) & 15) == 0;
 }
 
 // Next TMA piece (<= kTmaStageBytes, 16-byte multiple) of the CTA's range.
@@ -226,11 +220,11 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const CopyDesc *__restrict
       const uint64_t off = (uint64_t)(u - unit_start[i]) * kCopyUnit;
       if (off >= d.size) continue;
       const uint64_t len = min(kCopyUnit, d.size - off);
-      const uint8_t *s = reinterpret_cast<const uint8_t *>(d.src) + off;
-      uint8_t *t = reinterpret_cast<uint8_t *>(d.dst) + off;
       if (!tma_unit(d, off)) {
-        copy_range_lsu(s, t, len, lane, 32, (d.flags & 1) != 0);
+        lsu_unit(d, off, len, lane, 32);
       } else if (len & 15) {
+        const uint8_t *s = reinterpret_cast<const uint8_t *>(d.src) + off;
+        uint8_t *t = reinterpret_cast<uint8_t *>(d.dst) + off;
         const uint64_t body = len & ~15ull;
         for (uint64_t b = body + lane; b < len; b += 32) t[b] = s[b];
       }

@@ -670,7 +670,8 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
       if (!local) peer_bytes_read += sz;
       const uint64_t off = loc & kLocOffMask;
       src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
-      flags = (dram || !local) ? 1u : 0u;  // peer and pinned-host sources: plain loads
+      flags = (dram || !local) ? kCopyHost : 0;  // peer and pinned-host sources: plain loads
+      if (dram && (meta & kMetaPacked)) flags |= kCopyUnpack;
     }
     us.push_back(total);
     desc.push_back(CopyDesc{src, dst[i], sz, flags});

@@ -9,6 +9,7 @@
 // is absent and that an updated or erased key is present; mutation kernels
 // are stream-ordered with lookups, so a slot is never read while written.
 #include "kernels.cuh"
+#include "kvquant.cuh"
 
 namespace cb {
 
@@ -100,9 +101,11 @@ __global__ void index_lookup_kernel(LookupArgs a) {
     const uint64_t size = m & kSizeMask;
     const bool dram = (loc & kLocDram) != 0;
     const uint64_t off = loc & kLocOffMask;
+    const bool packed = dram && (m & kMetaPacked);
+    const uint64_t foot = packed ? packed_size(size) : size;  // bytes held in the arena
     const uint64_t base = dram ? a.dram_base : a.pool_base;
     const uint64_t bytes = dram ? a.dram_bytes : a.pool_bytes;
-    if (off > bytes || size > bytes - off) {
+    if (off > bytes || foot > bytes - off) {
       atomicOr(a.err, kErrBounds);
       break;
     }
@@ -116,7 +119,7 @@ __global__ void index_lookup_kernel(LookupArgs a) {
     } else if (size <= a.caps[i]) {
       d.src = base + off;
       d.size = size;
-      d.flags = dram ? 1u : 0u;
+      d.flags = dram ? (kCopyHost | (packed ? kCopyUnpack : 0)) : 0;
     } else {
       res.code |= CB_FOUND_NOT_COPIED;
     }

@@ -33,6 +33,16 @@ cudaError_t launch_batch_copy(const CopyDesc *d_desc, const uint32_t *d_unit_sta
                               uint32_t total_units, int engine, unsigned *d_err, int num_sms,
                               cudaStream_t stream);
 
+// kvquant.cu — INT8 packing (KVCompressor::compress format) of blocks:
+// descriptor i packs the d.size-byte block at d.src (device memory, d.size
+// >= 2) into packed_size(d.size) bytes at d.dst (device or mapped pinned host
+// memory); units as for launch_batch_copy over the source bytes. d_mm holds
+// n (min, max) int pairs the caller initialised to (INT_MAX, INT_MIN). Two
+// kernels (min/max, then pack). Unpacking is launch_batch_copy with
+// kCopyUnpack descriptors.
+cudaError_t launch_kv_pack(const CopyDesc *d_desc, const uint32_t *d_unit_start, int n, uint32_t total_units,
+                           int *d_mm, int num_sms, cudaStream_t stream);
+
 // index.cu — device index mutations and lookups.
 cudaError_t launch_index_insert(Slot *table, uint64_t mask, const IndexRec *recs, int n,
                                 unsigned *d_err, cudaStream_t stream);

@@ -139,8 +139,8 @@ void Policy::drop(const HKey &k, std::vector<HKey> &dropped) {
     hbm_.free(m.off, m.size);
     hbm_used_ -= m.size;
   } else {
-    dram_.free(m.off, m.size);
-    dram_used_ -= m.size;
+    dram_.free(m.off, footprint(m));
+    dram_used_ -= footprint(m);
     ctr_.dram_evictions++;
   }
   lru_[m.tier][m.prefix].erase(m.lru);
@@ -168,19 +168,28 @@ bool Policy::demote_one(std::vector<TierMove> &moves, std::vector<HKey> &dropped
   if (!pick_victim(kTierHbm, true, v)) return false;
   BlockMeta &m = map_.at(v);
   ctr_.gpu_evictions++;
-  if (!make_dram_room(m.size, dropped)) {
+  // evict_gpu_to_dram compresses blocks >= 64 B on their way to DRAM
+  // (distributed_backend.cpp:898-903).
+  const bool pack = compress_ && m.size >= kPackMinBytes;
+  const uint64_t dbytes = pack ? packed_bytes(m.size) : m.size;
+  if (!make_dram_room(dbytes, dropped)) {
     // No DRAM room: the reference sends the victim to Lustre
     // (distributed_backend.cpp:915-918); without that tier it is dropped.
     drop(v, dropped);
     return true;
   }
   BlockMeta &mm = map_.at(v);  // make_dram_room never drops pending/HBM blocks
-  const uint64_t doff = dram_.alloc(mm.size);
-  moves.push_back(TierMove{v, kTierHbm, kTierDram, mm.off, doff, mm.size});
+  const uint64_t doff = dram_.alloc(dbytes);
+  moves.push_back(TierMove{v, kTierHbm, kTierDram, mm.off, doff, mm.size, pack ? kMovePack : kMoveCopy});
   hbm_.free(mm.off, mm.size);
   hbm_used_ -= mm.size;
-  dram_used_ += mm.size;
+  dram_used_ += dbytes;
   ctr_.evicted_bytes += mm.size;
+  if (pack) {
+    ctr_.compression_savings += mm.size - dbytes;
+    mm.size &= ~1ull;  // what a read of the packed block returns
+    mm.packed = 1;
+  }
   auto &src = lru_[kTierHbm][mm.prefix];
   auto &dst = lru_[kTierDram][mm.prefix];
   dst.splice(dst.begin(), src, mm.lru);
@@ -226,12 +235,16 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
     if (make_hbm_room(size, plan.moves, plan.dropped)) {
       off = hbm_.alloc(size);
     }
+    bool pack = false;
     if (off == UINT64_MAX && direct_dram_) {
       // Larger than the whole HBM pool (or every HBM block pending): the
       // reference's put still succeeds through its DRAM copy
-      // (distributed_backend.cpp:643-652).
-      if (make_dram_room(size, plan.dropped)) {
-        off = dram_.alloc(size);
+      // (distributed_backend.cpp:643-652), compressed when kv_compression is
+      // on (:615-620).
+      pack = compress_ && size >= kPackMinBytes;
+      const uint64_t dbytes = pack ? packed_bytes(size) : size;
+      if (make_dram_room(dbytes, plan.dropped)) {
+        off = dram_.alloc(dbytes);
         tier = kTierDram;
       }
     }
@@ -239,24 +252,28 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
       plan.status[i] = 2;
       continue;
     }
+    if (tier != kTierDram) pack = false;
     BlockMeta m;
     m.off = off;
-    m.size = size;
+    m.size = pack ? (size & ~1ull) : size;
     m.tier = tier;
     m.prefix = pf;
     m.pending = 1;
+    m.packed = pack ? 1 : 0;
     m.stamp = ++clock_;
     auto &lst = lru_[tier][pf];
     lst.push_front(k);
     m.lru = lst.begin();
     map_.emplace(k, m);
     pending_.push_back(k);
-    if (tier == kTierHbm)
+    if (tier == kTierHbm) {
       hbm_used_ += size;
-    else
-      dram_used_ += size;
+    } else {
+      dram_used_ += pack ? packed_bytes(size) : size;
+      if (pack) ctr_.compression_savings += size - packed_bytes(size);
+    }
     if (pf) ctr_.prefix_blocks++;
-    plan.places.push_back(Placement{i, k, off, size, pf, tier});
+    plan.places.push_back(Placement{i, k, off, size, pf, tier, (uint8_t)(pack ? 1 : 0)});
   }
 }
 
@@ -281,14 +298,15 @@ bool Policy::plan_promote(const HKey &k, std::vector<TierMove> &moves,
   const uint64_t hoff = hbm_.alloc(size);
   if (hoff == UINT64_MAX) return false;
   BlockMeta &m = map_.at(k);
-  moves.push_back(TierMove{k, kTierDram, kTierHbm, m.off, hoff, size});
+  moves.push_back(TierMove{k, kTierDram, kTierHbm, m.off, hoff, size, m.packed ? kMoveUnpack : kMoveCopy});
   // The DRAM extent is released now; no later move of this plan writes DRAM
   // after promotions read it because the store runs every HBM->DRAM move of a
   // plan before any DRAM->HBM move, and DRAM destinations of those demotions
   // were allocated while this extent was still held.
-  deferred_free_.push_back({m.off, size});
-  dram_used_ -= size;
+  deferred_free_.push_back({m.off, footprint(m)});
+  dram_used_ -= footprint(m);
   hbm_used_ += size;
+  m.packed = 0;
   auto &src = lru_[kTierDram][m.prefix];
   auto &dst = lru_[kTierHbm][m.prefix];
   dst.splice(dst.begin(), src, m.lru);

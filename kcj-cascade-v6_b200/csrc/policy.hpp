@@ -22,6 +22,12 @@
 //   * DRAM eviction: DistributedDRAMBackend::evict_for_space
 //     (src/distributed_backend.cpp:240-284) - LRU, prefix blocks skipped, no
 //     fallback; with no Lustre tier an evicted DRAM block is dropped.
+//   * INT8 KV compression (kv_compression): DistributedStore keeps HBM blocks
+//     as they are and stores DRAM-tier copies of blocks >= 64 B in the
+//     KVCompressor format (src/distributed_backend.cpp:611-620, :898-903;
+//     src/cascade_core.cpp:908-967): 8 + size/2 bytes in DRAM, and a read
+//     returns (size/2)*2 bytes. Such a block is "packed": its DRAM footprint
+//     is 8 + size/2 and its size from then on is the even unpacked size.
 // Victim order is exact LRU (the reference approximates it per shard,
 // src/cascade_core.cpp:160-221); order is not a parity target, the
 // protection rule is.
@@ -71,22 +77,34 @@ class ExtentAllocator {
 
 enum : uint8_t { kTierHbm = 0, kTierDram = 1 };
 
+// INT8 packing of DRAM-tier blocks (KVCompressor, include/cascade.hpp:386-418).
+constexpr uint64_t kPackHeaderBytes = 8;  // [f32 scale][i8 zero point][3 pad]
+constexpr uint64_t kPackMinBytes = 64;    // smaller blocks are stored as they are
+inline uint64_t packed_bytes(uint64_t size) { return kPackHeaderBytes + size / 2; }
+
+// How a tier move transforms the bytes it moves.
+enum : uint8_t { kMoveCopy = 0, kMovePack = 1, kMoveUnpack = 2 };
+
 struct BlockMeta {
   uint64_t off = 0;
   uint64_t size = 0;
   uint8_t tier = kTierHbm;
   uint8_t prefix = 0;
   uint8_t pending = 0;  // placed by the batch being planned; not evictable yet
+  uint8_t packed = 0;   // DRAM copy in the INT8 format (size is then even)
   uint64_t stamp = 0;   // recency (larger = more recent)
   std::list<HKey>::iterator lru;
 };
 
-// A tier move the store executes: copy `size` bytes from (src_tier, src_off)
-// to (dst_tier, dst_off). Moves of one plan run in vector order.
+// A tier move the store executes from (src_tier, src_off) to (dst_tier,
+// dst_off). Moves of one plan run in vector order. size = bytes on the plain
+// side: kMoveCopy copies size bytes, kMovePack packs a size-byte block into
+// packed_bytes(size) bytes, kMoveUnpack unpacks into size (even) bytes.
 struct TierMove {
   HKey key;
   uint8_t src_tier, dst_tier;
   uint64_t src_off, dst_off, size;
+  uint8_t op = kMoveCopy;
 };
 
 struct Placement {
@@ -96,6 +114,7 @@ struct Placement {
   uint64_t size;
   uint8_t prefix;
   uint8_t tier;  // kTierHbm normally; kTierDram when larger than the HBM pool
+  uint8_t packed = 0;  // DRAM placement in the INT8 format (size = source bytes)
 };
 
 struct PutPlan {
@@ -116,6 +135,7 @@ struct PolicyCounters {
   uint64_t gpu_evictions = 0, dram_evictions = 0;
   uint64_t evicted_bytes = 0, promoted_bytes = 0, promotions = 0;
   uint64_t dropped_blocks = 0, prefix_blocks = 0;
+  uint64_t compression_savings = 0;  // bytes saved by packing into DRAM
 };
 
 class Policy {
@@ -152,6 +172,11 @@ class Policy {
   // When false, a new block that cannot get HBM fails instead of landing in
   // the DRAM tier (DHT mode: remote writers can only reach HBM pools).
   void set_direct_dram_placement(bool on) { direct_dram_ = on; }
+  // INT8 packing of DRAM-tier blocks >= kPackMinBytes (kv_compression).
+  void set_compression(bool on) { compress_ = on; }
+  bool compression() const { return compress_; }
+  // Bytes a block occupies in its tier's arena (logical, before rounding).
+  static uint64_t footprint(const BlockMeta &m) { return m.packed ? packed_bytes(m.size) : m.size; }
   template <class F>
   void for_each(F f) const {
     for (const auto &kv : map_) f(kv.first, kv.second);
@@ -167,6 +192,7 @@ class Policy {
   uint64_t hbm_cap_, dram_cap_;
   bool semantic_;
   bool direct_dram_ = true;
+  bool compress_ = false;
   ExtentAllocator hbm_, dram_;
   uint64_t hbm_used_ = 0, dram_used_ = 0;  // logical bytes (reference used_)
   std::unordered_map<HKey, BlockMeta, HKeyHash> map_;

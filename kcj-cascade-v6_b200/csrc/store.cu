@@ -16,6 +16,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <climits>
 #include <mutex>
 #include <new>
 #include <string>
@@ -121,6 +122,7 @@ int Store::init() {
   CB_TRY(alloc_table((uint64_t)1 << log2), "index");
   CB_TRY(h_err.ensure(64), "pinned");
   profile = cfg.profile != 0;
+  policy.set_compression(cfg.kv_compression != 0);
   hash_lanes = (cfg.hash_lanes == 8 || cfg.hash_lanes == 16) ? cfg.hash_lanes : 32;
   CB_TRY(cudaEventCreate(&ev_a), "event");
   CB_TRY(cudaEventCreate(&ev_b), "event");
@@ -200,7 +202,7 @@ int Store::reserve_index(uint64_t incoming, cudaStream_t st) {
   recs.reserve(live);
   policy.for_each([&](const HKey &k, const BlockMeta &m) {
     recs.push_back(IndexRec{k.lo, k.hi, m.off | (m.tier == kTierDram ? kLocDram : 0),
-                            meta_word(m.size, m.prefix)});
+                            meta_word(m.size, m.prefix) | (m.packed ? kMetaPacked : 0)});
   });
   const size_t bytes = recs.size() * sizeof(IndexRec);
   CB_TRY(h_scratch.ensure(bytes), "pinned scratch");
@@ -258,53 +260,76 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     cudaError_t e = ensure_dram();
     if (e != cudaSuccess) return cuda_fail(e, "pinned DRAM arena cudaHostAlloc");
   }
-  std::vector<const TierMove *> wave[2];
-  for (const auto &m : moves) wave[m.dst_tier == kTierDram ? 0 : 1].push_back(&m);
-  const int nm = (int)moves.size(), nd = (int)dropped.size();
+  // Launch groups, in this order: demotions copied as they are, demotions
+  // packed to INT8 (kv_compression), then promotions (copies and unpacks).
+  // Every promotion runs after every demotion: its HBM destination may be an
+  // extent a demotion of the same plan vacated.
+  std::vector<const TierMove *> grp[3];
+  for (const auto &m : moves) grp[m.dst_tier == kTierDram ? (m.op == kMovePack ? 1 : 0) : 2].push_back(&m);
+  const int nm = (int)moves.size(), nd = (int)dropped.size(), npk = (int)grp[1].size();
   Layout L;
   const size_t o_desc = L.add(sizeof(CopyDesc) * nm);
-  const size_t o_us0 = L.add(sizeof(uint32_t) * (wave[0].size() + 1));
-  const size_t o_us1 = L.add(sizeof(uint32_t) * (wave[1].size() + 1));
+  size_t o_us[3];
+  for (int g = 0; g < 3; ++g) o_us[g] = L.add(sizeof(uint32_t) * (grp[g].size() + 1));
+  const size_t o_mm = L.add(sizeof(int) * 2 * npk);
   const size_t o_upd = L.add(sizeof(IndexRec) * nm);
   const size_t o_era = L.add(sizeof(IndexRec) * nd);
   CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
   CB_TRY(d_scratch.ensure(L.off), "device scratch");
   uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
   CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
-  uint32_t *us[2] = {reinterpret_cast<uint32_t *>(h + o_us0), reinterpret_cast<uint32_t *>(h + o_us1)};
+  int *mm = reinterpret_cast<int *>(h + o_mm);
   IndexRec *upd = reinterpret_cast<IndexRec *>(h + o_upd);
   IndexRec *era = reinterpret_cast<IndexRec *>(h + o_era);
-  uint32_t total[2] = {0, 0};
-  uint64_t wave_bytes[2] = {0, 0};
+  uint32_t total[3] = {0, 0, 0};
+  uint64_t grp_bytes[3] = {0, 0, 0};
+  int base[3] = {0, 0, 0};
   int di = 0;
-  for (int w = 0; w < 2; ++w) {
-    for (size_t j = 0; j < wave[w].size(); ++j) {
-      const TierMove &m = *wave[w][j];
+  for (int g = 0; g < 3; ++g) {
+    uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us[g]);
+    base[g] = di;
+    for (size_t j = 0; j < grp[g].size(); ++j) {
+      const TierMove &m = *grp[g][j];
       const uint64_t src = m.src_tier == kTierDram ? (uint64_t)dram_dev + m.src_off : (uint64_t)pool + m.src_off;
       const uint64_t dst = m.dst_tier == kTierDram ? (uint64_t)dram_dev + m.dst_off : (uint64_t)pool + m.dst_off;
-      desc[di + j] = CopyDesc{src, dst, m.size, 1};
-      us[w][j] = total[w];
-      total[w] += units_of(m.size);
-      wave_bytes[w] += m.size;
+      desc[di + j] = CopyDesc{src, dst, m.size, kCopyHost | (m.op == kMoveUnpack ? kCopyUnpack : 0)};
+      us[j] = total[g];
+      total[g] += units_of(m.size);
+      grp_bytes[g] += m.size;
       const BlockMeta *bm = policy.find(m.key);
+      const bool packed = m.op == kMovePack;
       upd[di + j] = IndexRec{m.key.lo, m.key.hi, m.dst_off | (m.dst_tier == kTierDram ? kLocDram : 0),
-                             meta_word(m.size, bm ? bm->prefix : 0)};
+                             meta_word(packed ? (m.size & ~1ull) : m.size, bm ? bm->prefix : 0) |
+                                 (packed ? kMetaPacked : 0)};
     }
-    us[w][wave[w].size()] = total[w];
-    di += (int)wave[w].size();
+    us[grp[g].size()] = total[g];
+    di += (int)grp[g].size();
+  }
+  for (int j = 0; j < npk; ++j) {
+    mm[2 * j] = INT_MAX;
+    mm[2 * j + 1] = INT_MIN;
   }
   for (int j = 0; j < nd; ++j) era[j] = IndexRec{dropped[j].lo, dropped[j].hi, 0, 0};
   uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
   CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D moves");
   const CopyDesc *ddesc = reinterpret_cast<const CopyDesc *>(d + o_desc);
-  for (int w = 0; w < 2; ++w) {
-    if (wave[w].empty()) continue;
-    const CopyDesc *wd = ddesc + (w ? wave[0].size() : 0);
-    const uint32_t *wu = reinterpret_cast<const uint32_t *>(d + (w ? o_us1 : o_us0));
-    const int wn = (int)wave[w].size();
-    CB_TRY(timed(3, wave_bytes[w], st,
-                 [&] { return launch_batch_copy(wd, wu, wn, total[w], 2, d_err, num_sms, st); }),
-           w ? "promote copy" : "demote copy");
+  for (int g = 0; g < 3; ++g) {
+    if (grp[g].empty()) continue;
+    const CopyDesc *gd = ddesc + base[g];
+    const uint32_t *gu = reinterpret_cast<const uint32_t *>(d + o_us[g]);
+    const int gn = (int)grp[g].size();
+    if (g == 1) {
+      CB_TRY(timed(3, grp_bytes[g], st,
+                   [&] {
+                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + o_mm), num_sms, st);
+                   }),
+             "demote pack");
+      launches++;  // two kernels
+    } else {
+      CB_TRY(timed(3, grp_bytes[g], st,
+                   [&] { return launch_batch_copy(gd, gu, gn, total[g], 2, d_err, num_sms, st); }),
+             g ? "promote copy" : "demote copy");
+    }
   }
   if (nm) {
     CB_TRY(launch_index_update(table, table_slots - 1, reinterpret_cast<const IndexRec *>(d + o_upd), nm,
@@ -385,38 +410,73 @@ int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t
       cudaError_t e = ensure_dram();
       if (e != cudaSuccess) return cuda_fail(e, "pinned DRAM arena cudaHostAlloc");
     }
+    // Two groups: blocks copied as they are (HBM, or DRAM without packing),
+    // then blocks packed to INT8 straight into the DRAM tier.
+    int npk = 0;
+    for (const auto &p : plan.places) npk += p.packed ? 1 : 0;
+    const int ncp = np - npk;
     Layout L;
     const size_t o_desc = L.add(sizeof(CopyDesc) * np);
-    const size_t o_us = L.add(sizeof(uint32_t) * (np + 1));
+    const size_t o_us = L.add(sizeof(uint32_t) * (ncp + 1));
+    const size_t o_pus = L.add(sizeof(uint32_t) * (npk + 1));
+    const size_t o_mm = L.add(sizeof(int) * 2 * npk);
     const size_t o_ins = L.add(sizeof(IndexRec) * np);
     CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
     CB_TRY(d_scratch.ensure(L.off), "device scratch");
     uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
     CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
     uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
+    uint32_t *pus = reinterpret_cast<uint32_t *>(h + o_pus);
+    int *mm = reinterpret_cast<int *>(h + o_mm);
     IndexRec *ins = reinterpret_cast<IndexRec *>(h + o_ins);
-    uint32_t total = 0;
-    uint64_t bytes = 0;
+    uint32_t total = 0, ptotal = 0;
+    uint64_t bytes = 0, pbytes = 0;
+    int jc = 0, jp = 0;
     for (int j = 0; j < np; ++j) {
       const Placement &p = plan.places[j];
-      bytes += p.size;
       const bool dram = p.tier == kTierDram;
       const uint64_t dst = dram ? (uint64_t)dram_dev + p.off : (uint64_t)pool + p.off;
-      desc[j] = CopyDesc{ptrs[p.idx], dst, p.size, dram ? 1u : 0u};
-      us[j] = total;
-      total += units_of(p.size);
-      ins[j] = IndexRec{p.key.lo, p.key.hi, p.off | (dram ? kLocDram : 0), meta_word(p.size, p.prefix)};
+      const int slot = p.packed ? ncp + jp : jc;
+      desc[slot] = CopyDesc{ptrs[p.idx], dst, p.size, dram ? kCopyHost : 0};
+      if (p.packed) {
+        pus[jp] = ptotal;
+        ptotal += units_of(p.size);
+        pbytes += p.size;
+        mm[2 * jp] = INT_MAX;
+        mm[2 * jp + 1] = INT_MIN;
+        ++jp;
+      } else {
+        us[jc] = total;
+        total += units_of(p.size);
+        bytes += p.size;
+        ++jc;
+      }
+      ins[j] = IndexRec{p.key.lo, p.key.hi, p.off | (dram ? kLocDram : 0),
+                        meta_word(p.packed ? (p.size & ~1ull) : p.size, p.prefix) | (p.packed ? kMetaPacked : 0)};
     }
-    us[np] = total;
+    us[ncp] = total;
+    pus[npk] = ptotal;
     uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
     CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D scatter");
-    CB_TRY(timed(1, bytes, st,
-                 [&] {
-                   return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_desc),
-                                            reinterpret_cast<const uint32_t *>(d + o_us), np, total,
-                                            copy_engine, d_err, num_sms, st);
-                 }),
-           "scatter");
+    if (ncp) {
+      CB_TRY(timed(1, bytes, st,
+                   [&] {
+                     return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_desc),
+                                              reinterpret_cast<const uint32_t *>(d + o_us), ncp, total,
+                                              copy_engine, d_err, num_sms, st);
+                   }),
+             "scatter");
+    }
+    if (npk) {
+      CB_TRY(timed(1, pbytes, st,
+                   [&] {
+                     return launch_kv_pack(reinterpret_cast<const CopyDesc *>(d + o_desc) + ncp,
+                                           reinterpret_cast<const uint32_t *>(d + o_pus), npk, ptotal,
+                                           reinterpret_cast<int *>(d + o_mm), num_sms, st);
+                   }),
+             "scatter pack");
+      launches++;  // two kernels
+    }
     CB_TRY(launch_index_insert(table, table_slots - 1, reinterpret_cast<const IndexRec *>(d + o_ins), np,
                                d_err, st),
            "index insert");
@@ -694,6 +754,82 @@ int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_
 
 // ---------------------------------------------------------------- misc
 
+// KVCompressor::compress (src/cascade_core.cpp:908-944) of n device blocks:
+// the pack kernels of the DRAM tier on caller buffers.
+int Store::kv_compress(const uint64_t *srcs, const uint64_t *sizes, const uint64_t *dsts, int n, cudaStream_t st) {
+  Layout L;
+  const size_t o_desc = L.add(sizeof(CopyDesc) * n);
+  const size_t o_us = L.add(sizeof(uint32_t) * (n + 1));
+  const size_t o_mm = L.add(sizeof(int) * 2 * n);
+  CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
+  CB_TRY(d_scratch.ensure(L.off), "device scratch");
+  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
+  uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
+  int *mm = reinterpret_cast<int *>(h + o_mm);
+  uint32_t total = 0;
+  uint64_t bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    if (sizes[i] < 2) return fail(CB_ERR_ARG, "block %d: compression needs at least one 16-bit value", i);
+    desc[i] = CopyDesc{srcs[i], dsts[i], sizes[i], 0};
+    us[i] = total;
+    total += units_of(sizes[i]);
+    bytes += sizes[i];
+    mm[2 * i] = INT_MAX;
+    mm[2 * i + 1] = INT_MIN;
+  }
+  us[n] = total;
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D pack");
+  CB_TRY(timed(3, bytes, st,
+               [&] {
+                 return launch_kv_pack(reinterpret_cast<const CopyDesc *>(d + o_desc),
+                                       reinterpret_cast<const uint32_t *>(d + o_us), n, total,
+                                       reinterpret_cast<int *>(d + o_mm), num_sms, st);
+               }),
+         "pack");
+  launches++;  // two kernels
+  return check_device_error(st);
+}
+
+// KVCompressor::decompress (src/cascade_core.cpp:946-967) of n device
+// blocks; ok_out[i] = 0 (nothing written) when block i is shorter than
+// 8 + orig_sizes[i]/2 bytes, the reference's `return false`.
+int Store::kv_decompress(const uint64_t *srcs, const uint64_t *comp_sizes, const uint64_t *orig_sizes,
+                         const uint64_t *dsts, int n, uint8_t *ok_out, cudaStream_t st) {
+  Layout L;
+  const size_t o_desc = L.add(sizeof(CopyDesc) * n);
+  const size_t o_us = L.add(sizeof(uint32_t) * (n + 1));
+  CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
+  CB_TRY(d_scratch.ensure(L.off), "device scratch");
+  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
+  uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
+  uint32_t total = 0;
+  uint64_t bytes = 0;
+  for (int i = 0; i < n; ++i) {
+    const bool ok = comp_sizes[i] >= packed_bytes(orig_sizes[i]);
+    if (ok_out) ok_out[i] = ok ? 1 : 0;
+    const uint64_t out = ok ? orig_sizes[i] / 2 * 2 : 0;
+    desc[i] = CopyDesc{srcs[i], dsts[i], out, kCopyHost | kCopyUnpack};
+    us[i] = total;
+    total += units_of(out);
+    bytes += out;
+  }
+  us[n] = total;
+  if (total == 0) return CB_OK;
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D unpack");
+  CB_TRY(timed(3, bytes, st,
+               [&] {
+                 return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_desc),
+                                          reinterpret_cast<const uint32_t *>(d + o_us), n, total, 2, d_err,
+                                          num_sms, st);
+               }),
+         "unpack");
+  return check_device_error(st);
+}
+
 int Store::evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st) {
   std::vector<TierMove> moves;
   std::vector<HKey> dropped;
@@ -745,6 +881,7 @@ void Store::fill_stats(cb_stats *o) const {
   o->gpu_evictions = c.gpu_evictions;
   o->dram_evictions = c.dram_evictions;
   o->promotions_to_local = c.promotions + replica_promotions;
+  o->compression_savings = c.compression_savings;
   o->total_blocks = policy.size();
   o->prefix_blocks = c.prefix_blocks;
   o->evicted_bytes = c.evicted_bytes;
@@ -846,6 +983,35 @@ int cb_destroy(cb_store *h) {
 const char *cb_last_error(const cb_store *h) {
   if (!h || !h->s) return cb::g_create_error.c_str();
   return h->s->last_error.c_str();
+}
+
+int cb_kv_compress_batch(cb_store *h, const void *const *srcs, const uint64_t *sizes, void *const *dsts,
+                         int32_t n, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!srcs || !sizes || !dsts))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (n == 0) return CB_OK;
+    std::vector<uint64_t> src(n), dst(n);
+    for (int i = 0; i < n; ++i) {
+      src[i] = (uint64_t)srcs[i];
+      dst[i] = (uint64_t)dsts[i];
+    }
+    return s->kv_compress(src.data(), sizes, dst.data(), n, pick_stream(s, stream));
+  });
+}
+
+int cb_kv_decompress_batch(cb_store *h, const void *const *srcs, const uint64_t *comp_sizes,
+                           const uint64_t *orig_sizes, void *const *dsts, int32_t n, uint8_t *ok_out,
+                           void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!srcs || !comp_sizes || !orig_sizes || !dsts))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (n == 0) return CB_OK;
+    std::vector<uint64_t> src(n), dst(n);
+    for (int i = 0; i < n; ++i) {
+      src[i] = (uint64_t)srcs[i];
+      dst[i] = (uint64_t)dsts[i];
+    }
+    return s->kv_decompress(src.data(), comp_sizes, orig_sizes, dst.data(), n, ok_out, pick_stream(s, stream));
+  });
 }
 
 int cb_hash_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, int32_t n,

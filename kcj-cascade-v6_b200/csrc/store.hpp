@@ -140,6 +140,10 @@ struct Store {
   int get_host(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps,
                uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
   int evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st);
+  // INT8 KV packing of device blocks outside the store (KVCompressor).
+  int kv_compress(const uint64_t *srcs, const uint64_t *sizes, const uint64_t *dsts, int n, cudaStream_t st);
+  int kv_decompress(const uint64_t *srcs, const uint64_t *comp_sizes, const uint64_t *orig_sizes,
+                    const uint64_t *dsts, int n, uint8_t *ok_out, cudaStream_t st);
   int clear(cudaStream_t st);
   void fill_stats(cb_stats *o) const;
   uint64_t staging_capacity() const;

@@ -118,15 +118,31 @@ class TierModel:
     Logical-capacity model (the reference checks ``used + size > capacity``,
     src/gpu_backend.cu:307); allocation fragmentation is not modelled, so use
     equal block sizes when comparing placements exactly.
+
+    With ``compress`` (kv_compression) a block >= 64 B that enters DRAM is
+    held as KVCompressor output, 8 + size/2 bytes
+    (src/distributed_backend.cpp:611-620, :898-903), and its size becomes
+    (size/2)*2, what a read returns (:712-719).
     """
 
-    def __init__(self, hbm_cap: int, dram_cap: int, semantic: bool = True):
+    def __init__(self, hbm_cap: int, dram_cap: int, semantic: bool = True, compress: bool = False):
         self.hbm_cap, self.dram_cap, self.semantic = hbm_cap, dram_cap, semantic
+        self.compress = compress
         self.hbm: OrderedDict[str, int] = OrderedDict()   # id -> size, last = MRU
-        self.dram: OrderedDict[str, int] = OrderedDict()
+        self.dram: OrderedDict[str, int] = OrderedDict()  # id -> bytes held in DRAM
+        self.size: dict[str, int] = {}                    # id -> size a read returns
         self.prefix: set[str] = set()
         self.dropped: list[str] = []
         self.evictions = 0
+        self.compression_savings = 0
+
+    def _to_dram(self, k: str, size: int) -> int:
+        """Bytes block k of `size` bytes occupies in DRAM (and its new size)."""
+        if self.compress and size >= 64:
+            self.size[k] = size // 2 * 2
+            return 8 + size // 2
+        self.size[k] = size
+        return size
 
     def _victim_hbm(self):
         order = list(self.hbm.keys())
@@ -154,8 +170,10 @@ class TierModel:
             return False
         size = self.hbm.pop(v)
         self.evictions += 1
-        if self._room_dram(size):
-            self.dram[v] = size
+        dsize = 8 + size // 2 if self.compress and size >= 64 else size
+        if self._room_dram(dsize):
+            self.dram[v] = self._to_dram(v, size)
+            self.compression_savings += size - dsize
         else:
             self.dropped.append(v)
         return True
@@ -170,9 +188,12 @@ class TierModel:
                 break
         if sum(self.hbm.values()) + size <= self.hbm_cap:
             self.hbm[k] = size
+            self.size[k] = size
             return "hbm"
-        if self._room_dram(size):
-            self.dram[k] = size
+        dsize = 8 + size // 2 if self.compress and size >= 64 else size
+        if self._room_dram(dsize):
+            self.dram[k] = self._to_dram(k, size)
+            self.compression_savings += size - dsize
             return "dram"
         return "failed"
 
@@ -185,7 +206,7 @@ class TierModel:
     def promote(self, k: str) -> bool:
         if k not in self.dram:
             return False
-        size = self.dram[k]
+        size = self.size[k]
         # the promoted block itself is never a DRAM victim while room is made
         while sum(self.hbm.values()) + size > self.hbm_cap:
             v = self._victim_hbm()
@@ -193,8 +214,9 @@ class TierModel:
                 return False
             vs = self.hbm.pop(v)
             self.evictions += 1
-            cands_ok = self.dram_cap > 0 and vs <= self.dram_cap
-            while cands_ok and sum(self.dram.values()) + vs > self.dram_cap:
+            vd = 8 + vs // 2 if self.compress and vs >= 64 else vs
+            cands_ok = self.dram_cap > 0 and vd <= self.dram_cap
+            while cands_ok and sum(self.dram.values()) + vd > self.dram_cap:
                 cands = [x for x in self.dram if x != k and not (self.semantic and x in self.prefix)]
                 if not cands:
                     cands_ok = False
@@ -202,7 +224,8 @@ class TierModel:
                 del self.dram[cands[0]]
                 self.dropped.append(cands[0])
             if cands_ok:
-                self.dram[v] = vs
+                self.dram[v] = self._to_dram(v, vs)
+                self.compression_savings += vs - vd
             else:
                 self.dropped.append(v)
         del self.dram[k]

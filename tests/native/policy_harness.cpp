@@ -13,9 +13,10 @@ extern "C" {
 
 void *ph_create(uint64_t hbm, uint64_t dram, int semantic) { return new Policy(hbm, dram, semantic != 0); }
 void ph_destroy(void *p) { delete static_cast<Policy *>(p); }
+void ph_set_compression(void *p, int on) { static_cast<Policy *>(p)->set_compression(on != 0); }
 
-// keys: n*2 u64; out_status: n; out_moves: up to cap records of 6 u64
-// (key.lo, key.hi, src_tier, dst_tier, src_off, dst_off); returns #moves,
+// keys: n*2 u64; out_status: n; out_moves: up to cap records of 7 u64
+// (key.lo, key.hi, src_tier, dst_tier, src_off, dst_off, op); returns #moves,
 // *n_dropped receives the dropped count (keys into out_dropped, 2 u64 each).
 int ph_put(void *p, const uint64_t *keys, const uint64_t *sizes, const uint8_t *prefix, int n, int dedup,
            uint8_t *out_status, uint64_t *out_moves, int cap, uint64_t *out_dropped, int *n_dropped,
@@ -30,13 +31,14 @@ int ph_put(void *p, const uint64_t *keys, const uint64_t *sizes, const uint8_t *
   int m = 0;
   for (const auto &mv : plan.moves) {
     if (m >= cap) break;
-    uint64_t *r = out_moves + 6 * m++;
+    uint64_t *r = out_moves + 7 * m++;
     r[0] = mv.key.lo;
     r[1] = mv.key.hi;
     r[2] = mv.src_tier;
     r[3] = mv.dst_tier;
     r[4] = mv.src_off;
     r[5] = mv.dst_off;
+    r[6] = mv.op;
   }
   *n_dropped = (int)plan.dropped.size();
   for (size_t i = 0; i < plan.dropped.size() && (int)i < cap; ++i) {
@@ -82,7 +84,7 @@ uint64_t ph_evict(void *p, uint64_t bytes) {
 }
 
 // counters: hbm_used, dram_used, size, dedup_hits, dedup_bytes, gpu_evictions,
-// dram_evictions, dropped, prefix_blocks, promotions
+// dram_evictions, dropped, prefix_blocks, promotions, compression_savings
 void ph_counters(void *p, uint64_t *out) {
   Policy *pol = static_cast<Policy *>(p);
   const PolicyCounters &c = pol->counters();
@@ -96,6 +98,15 @@ void ph_counters(void *p, uint64_t *out) {
   out[7] = c.dropped_blocks;
   out[8] = c.prefix_blocks;
   out[9] = c.promotions;
+  out[10] = c.compression_savings;
+}
+
+// Returns the block's size (its unpacked size once packed) and packed flag.
+int ph_size(void *p, uint64_t lo, uint64_t hi, uint64_t *size) {
+  const BlockMeta *m = static_cast<Policy *>(p)->find(HKey{lo, hi});
+  if (!m) return -1;
+  *size = m->size;
+  return m->packed;
 }
 
 // Extent allocator checks.

@@ -27,6 +27,9 @@ def ph(tmp_path_factory):
     lib.ph_create.restype = V
     lib.ph_create.argtypes = [U64, U64, I]
     lib.ph_destroy.argtypes = [V]
+    lib.ph_set_compression.argtypes = [V, I]
+    lib.ph_size.restype = I
+    lib.ph_size.argtypes = [V, U64, U64, C.POINTER(U64)]
     lib.ph_put.restype = I
     lib.ph_put.argtypes = [V, V, V, V, I, I, V, V, I, V, C.POINTER(I), V, C.POINTER(I)]
     lib.ph_find.restype = I
@@ -50,9 +53,11 @@ def ph(tmp_path_factory):
 
 
 class Pol:
-    def __init__(self, lib, hbm, dram, semantic=True):
+    def __init__(self, lib, hbm, dram, semantic=True, compress=False):
         self.lib, self.p = lib, lib.ph_create(hbm, dram, 1 if semantic else 0)
         self.names = {}
+        if compress:
+            lib.ph_set_compression(self.p, 1)
 
     def key(self, name):
         k = self.names.setdefault(name, (len(self.names) + 1, 0xABC))
@@ -64,7 +69,7 @@ class Pol:
         sz = np.array(sizes, np.uint64)
         pf = np.array(prefix if prefix is not None else [0] * n, np.uint8)
         st = np.zeros(n, np.uint8)
-        moves = np.zeros((4096, 6), np.uint64)
+        moves = np.zeros((4096, 7), np.uint64)
         dropped = np.zeros((4096, 2), np.uint64)
         places = np.zeros((max(n, 1), 4), np.uint64)
         nd, npl = C.c_int(0), C.c_int(0)
@@ -85,11 +90,17 @@ class Pol:
     def promote(self, name):
         return self.lib.ph_promote(self.p, *self.key(name))
 
+    def size(self, name):
+        sz = C.c_uint64(0)
+        packed = self.lib.ph_size(self.p, *self.key(name), C.byref(sz))
+        return int(sz.value), packed
+
     def counters(self):
-        out = np.zeros(10, np.uint64)
+        out = np.zeros(11, np.uint64)
         self.lib.ph_counters(self.p, out.ctypes.data)
         return dict(zip(["hbm_used", "dram_used", "size", "dedup_hits", "dedup_bytes", "gpu_evictions",
-                         "dram_evictions", "dropped", "prefix_blocks", "promotions"], map(int, out)))
+                         "dram_evictions", "dropped", "prefix_blocks", "promotions", "compression_savings"],
+                        map(int, out)))
 
 
 def test_allocator_best_fit_and_coalesce(ph):
@@ -154,12 +165,12 @@ def test_dedup_disabled_counts_nothing(ph):
     assert st == [0, 1, 0] and pol.counters()["dedup_hits"] == 0
 
 
-@pytest.mark.parametrize("semantic", [True, False])
-def test_demotion_matches_tier_model(ph, semantic):
+@pytest.mark.parametrize("semantic,compress", [(True, False), (False, False), (True, True), (False, True)])
+def test_demotion_matches_tier_model(ph, semantic, compress):
     S = 64 * 1024
-    rng = np.random.default_rng(4 if semantic else 5)
-    pol = Pol(ph, 10 * S, 25 * S, semantic=semantic)
-    model = TierModel(10 * S, 25 * S, semantic=semantic)
+    rng = np.random.default_rng((4 if semantic else 5) + (10 if compress else 0))
+    pol = Pol(ph, 10 * S, 25 * S, semantic=semantic, compress=compress)
+    model = TierModel(10 * S, 25 * S, semantic=semantic, compress=compress)
     for step in range(200):
         op = rng.random()
         name = f"k{int(rng.integers(0, 60))}"
@@ -180,6 +191,7 @@ def test_demotion_matches_tier_model(ph, semantic):
     c = pol.counters()
     assert c["gpu_evictions"] == model.evictions
     assert c["hbm_used"] == sum(model.hbm.values()) and c["dram_used"] == sum(model.dram.values())
+    assert c["compression_savings"] == model.compression_savings
 
 
 def test_prefix_never_evicted_while_nonprefix_evictable(ph):
@@ -219,3 +231,44 @@ def test_explicit_evict(ph):
     pol.put([f"b{i}" for i in range(8)], [S] * 8)
     assert ph.ph_evict(pol.p, 3 * S) == 3 * S
     assert [pol.tier(f"b{i}") for i in range(3)] == ["dram"] * 3
+
+
+def test_compression_packs_demotions_and_unpacks_promotions(ph):
+    # kv_compression: DRAM copies of blocks >= 64 B hold 8 + size/2 bytes
+    # (src/distributed_backend.cpp:898-903); a packed block reads back as
+    # (size/2)*2 bytes; smaller blocks move as they are.
+    S = 4097  # odd: the last byte is not kept once packed
+    pol = Pol(ph, 3 * 4352, 1 << 20, compress=True)
+    pol.put(["a", "b", "c"], [S, S, 40])
+    _, moves, _, _ = pol.put(["d", "e"], [S, S])
+    ops = {next(k for k, v in pol.names.items() if v == (int(m[0]), int(m[1]))): int(m[6]) for m in moves}
+    assert ops == {"a": 1, "b": 1}  # kMovePack, oldest first
+    assert pol.tier("a") == "dram" and pol.size("a") == (4096, 1)
+    assert pol.tier("c") == "hbm" and pol.size("c") == (40, 0)
+    c = pol.counters()
+    assert c["dram_used"] == 2 * (8 + S // 2)
+    assert c["compression_savings"] == 2 * (S - (8 + S // 2))
+    nm = pol.promote("a")
+    assert nm >= 1
+    assert pol.tier("a") == "hbm" and pol.size("a") == (4096, 0)
+    # the promotion move unpacks; "a" is now an even 4096-byte HBM block
+    assert pol.counters()["hbm_used"] == sum(
+        sz for n, sz in [("a", 4096), ("c", 40), ("d", S), ("e", S)] if pol.tier(n) == "hbm")
+
+
+def test_compression_small_blocks_stay_raw(ph):
+    pol = Pol(ph, 256, 1 << 20, compress=True)
+    pol.put(["s0"], [63])
+    _, moves, _, _ = pol.put(["s1"], [63])
+    assert len(moves) == 1 and int(moves[0][6]) == 0  # kMoveCopy
+    assert pol.size("s0") == (63, 0) and pol.counters()["compression_savings"] == 0
+
+
+def test_compression_direct_dram_placement_is_packed(ph):
+    # a block larger than the whole HBM pool goes to DRAM at put time,
+    # compressed (distributed_backend.cpp:615-620, :643-652)
+    pol = Pol(ph, 1024, 1 << 20, compress=True)
+    st, _, _, places = pol.put(["big"], [100_001])
+    assert st == [0] and int(places[0][2]) == 1  # DRAM tier
+    assert pol.size("big") == (100_000, 1)
+    assert pol.counters()["dram_used"] == 8 + 50_000
