@@ -66,6 +66,8 @@ def parse():
     p.add_argument("--spill-blocks", type=int, default=40000)
     p.add_argument("--spill-hbm-gb", type=float, default=120.0)
     p.add_argument("--spill-dram-gb", type=float, default=100.0)
+    p.add_argument("--kv-compression", action="store_true",
+                   help="spill: DRAM-tier blocks in the INT8 KVCompressor format (lossy)")
     p.add_argument("--zipf-blocks-per-gpu", type=int, default=20000)
     p.add_argument("--zipf-block-bytes", type=int, default=5242880)
     p.add_argument("--zipf-batch", type=int, default=512)
@@ -657,8 +659,13 @@ def spill_main(args, rank, world, local, device):
     120 GB HBM pool with a pinned DRAM tier; 10 % of the blocks (seeded) are
     prefix-protected. Put everything (LRU demotions to DRAM run as mapped-host
     copy kernels), then batch_get Zipf(1.1) keys; DRAM hits are promoted back
-    to HBM (each promotion demotes an LRU block). Every get batch is checked:
-    the bytes returned must hash (GPU SHA-256) to the requested ID."""
+    to HBM (each promotion demotes an LRU block). Every warm-up get batch is
+    checked: the bytes returned must hash (GPU SHA-256) to the requested ID.
+    With --kv-compression the DRAM tier holds INT8-packed blocks (8 + size/2
+    bytes) and a block that went through it reads back lossy, so the check
+    keeps the originals of the first 128 distinct blocks the warm-up steps
+    draw: a read of one must equal the original or its KVCompressor round
+    trip."""
     import torch
     import cascade_cpp
     from cascade_cpp import workloads as W
@@ -671,11 +678,23 @@ def spill_main(args, rank, world, local, device):
     cfg.profile = True
     cfg.dht = False
     cfg.index_log2 = 17
+    cfg.kv_compression = bool(args.kv_compression)
     store = cascade_cpp.DistributedStore(cfg)
     rng = np.random.default_rng(33)
     prefix = (rng.random(nb) < 0.10).astype(np.uint8)
     pb = 256
     buf = torch.empty(pb * size, dtype=torch.uint8, device=device)
+    gb = args.zipf_batch
+    total_steps = args.warmup + args.steps
+    draws = W.zipf_keys(nb, total_steps * gb, args.zipf_alpha, seed=34)
+    slot = {}
+    if args.kv_compression:
+        for b in draws[:args.warmup * gb]:
+            if len(slot) == 128:
+                break
+            slot.setdefault(int(b), len(slot))
+    n_keep = len(slot)
+    kept = torch.empty(max(n_keep, 1) * size, dtype=torch.uint8, device=device)
     g = torch.Generator(device=device).manual_seed(33)
     keys = np.empty((nb, 16), np.uint8)
     s0 = store._n.stats()
@@ -685,6 +704,9 @@ def spill_main(args, rank, world, local, device):
         m = min(pb, nb - i)
         buf[:m * size].view(torch.bfloat16).copy_(
             torch.randn(m * size // 2, generator=g, device=device, dtype=torch.bfloat16))
+        for j in range(i, i + m):
+            if j in slot:
+                kept[slot[j] * size:(slot[j] + 1) * size].copy_(buf[(j - i) * size:(j - i + 1) * size])
         ptrs = (np.uint64(buf.data_ptr()) + np.arange(m, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
         k, st = store.put_ptrs(ptrs, np.full(m, size, np.uint64), True, prefix=prefix[i:i + m])
         assert (st == 0).all(), "put failed"
@@ -699,19 +721,29 @@ def spill_main(args, rank, world, local, device):
     in_dram = [store.locate(k.tobytes().hex()) for k in keys]
     pf_dram = sum(1 for j, l in enumerate(in_dram) if prefix[j] and not l.is_gpu)
     np_hbm = sum(1 for j, l in enumerate(in_dram) if not prefix[j] and l.is_gpu)
-    gb = args.zipf_batch
-    total_steps = args.warmup + args.steps
-    draws = W.zipf_keys(nb, total_steps * gb, args.zipf_alpha, seed=34)
     out = torch.empty(gb * size, dtype=torch.uint8, device=device)
     outs = (np.uint64(out.data_ptr()) + np.arange(gb, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
     caps = np.full(gb, size, np.uint64)
     hasher = cascade_cpp._hasher(local)
+    if n_keep:
+        blocks = [kept[j * size:(j + 1) * size] for j in range(n_keep)]
+        rt = cascade_cpp.KVCompressor.decompress_batch(cascade_cpp.KVCompressor.compress_batch(blocks),
+                                                       [size] * n_keep)
+    checked = 0
     for s in range(args.warmup):
-        kk = keys[draws[s * gb:(s + 1) * gb]]
+        dk = draws[s * gb:(s + 1) * gb]
+        kk = keys[dk]
         sz, f = store.get_ptrs(kk, outs, caps, True)
         assert ((f & 0x0F) != 0).all()
-        dig = hasher.hash(outs, caps, 0)  # bytes returned hash to the requested IDs
-        assert np.array_equal(dig[:, :16], kk), "get returned wrong bytes"
+        if not n_keep:
+            dig = hasher.hash(outs, caps, 0)  # bytes returned hash to the requested IDs
+            assert np.array_equal(dig[:, :16], kk), "get returned wrong bytes"
+            continue
+        for j, b in enumerate(dk):
+            if int(b) in slot:
+                o, t = out[j * size:(j + 1) * size], slot[int(b)]
+                assert torch.equal(o, blocks[t]) or torch.equal(o, rt[t]), "get returned wrong bytes"
+                checked += 1
     s2 = store._n.stats()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     got = 0
@@ -730,6 +762,9 @@ def spill_main(args, rank, world, local, device):
 
     ev_b, ev_ns = dd(s0, s1, "tier_bytes"), dd(s0, s1, "tier_ns")
     pr_b, pr_ns = dd(s2, s3, "tier_bytes"), dd(s2, s3, "tier_ns")
+    # bytes that crossed the host link on demotion: packed (8 + size/2 per
+    # block) with kv_compression, the whole block without
+    link_b = ev_b // size * (8 + size // 2) if args.kv_compression else ev_b
     line = {
         "metric": "tier moves (config 3: HBM <-> pinned DRAM spill)", "value": round(got / get_s / GB, 3),
         "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -737,22 +772,29 @@ def spill_main(args, rank, world, local, device):
         "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded bf16 N(0,1) blocks generated on the GPU)",
         "config": {"workload": f"config3: {nb} x {size} B Qwen2.5-72B blocks ({nb * size / 1e9:.1f} GB), HBM pool "
                                f"{args.spill_hbm_gb} GB, pinned DRAM {args.spill_dram_gb} GB, 10% prefix, "
-                               f"batch_get {gb} Zipf({args.zipf_alpha}) keys per step, promotion on DRAM hit"},
+                               f"batch_get {gb} Zipf({args.zipf_alpha}) keys per step, promotion on DRAM hit"
+                               + (", kv_compression (INT8 DRAM tier)" if args.kv_compression else "")},
         "value_is": "batch_get GB/s in the timed steps (DRAM hits promoted inline)",
         "put_phase": {"seconds": round(put_s, 2), "gb_put": round(nb * size / 1e9, 1),
                       "gpu_evictions": dd(s0, s1, "gpu_evictions"), "evicted_gb": round(ev_b / 1e9, 2),
                       "evict_kernel_gbs": round(ev_b / ev_ns, 2) if ev_ns else None,
+                      "evict_link_gb": round(link_b / 1e9, 2),
+                      "compression_savings_gb": round(dd(s0, s1, "compression_savings") / 1e9, 2),
                       "prefix_blocks_in_dram": pf_dram, "nonprefix_blocks_in_hbm": np_hbm},
         "get_phase": {"local_gpu_hits": dd(s2, s3, "local_gpu_hits"), "local_dram_hits": dd(s2, s3, "local_dram_hits"),
                       "promotions": dd(s2, s3, "promotions_to_local"), "tier_moved_gb": round(pr_b / 1e9, 2),
                       "tier_kernel_gbs": round(pr_b / pr_ns, 2) if pr_ns else None},
-        "roofline": {"kernel": "copy_lsu (mapped pinned host)", "bound": "host link",
-                     "achieved": round(ev_b / ev_ns, 2) if ev_ns else None,
+        "roofline": {"kernel": ("kv_minmax + kv_pack (INT8 into mapped pinned host)" if args.kv_compression
+                                else "copy_lsu (mapped pinned host)"), "bound": "host link",
+                     "achieved": round(link_b / ev_ns, 2) if ev_ns else None,
                      "peak": round(peaks["d2h"], 2), "unit": "GB/s",
-                     "frac": round((ev_b / ev_ns) / peaks["d2h"], 4) if ev_ns else None,
+                     "frac": round((link_b / ev_ns) / peaks["d2h"], 4) if ev_ns else None,
+                     "achieved_is": "host-link bytes of the demotions / their kernel time",
                      "peak_source": "measured pinned D2H copy in this run", "h2d_peak": round(peaks["h2d"], 2)},
         "gpu_launches": dd(s2, s3, "kernel_launches"), "clocks": clk.summary(),
     }
+    if n_keep:
+        line["check"] = f"{checked} warm-up reads of kept blocks equal the original or its INT8 round trip"
     print(json.dumps(line), flush=True)
     store.close()
 

@@ -103,7 +103,7 @@ CB_D void lsu_unit(const CopyDesc &d, uint64_t off, uint64_t len, int tid, int n
   }
 }
 
-__global__ void __launch_bounds__(kLsuThreads) copy_lsu_kernel(const CopyDesc *__restrict__ desc,
+__global__ void __launch_bounds__(kLsuThreads, kLsuCtasPerSm) copy_lsu_kernel(const CopyDesc *__restrict__ desc,
                                                                const uint32_t *__restrict__ unit_start,
                                                                int n, uint32_t total_units) {
   uint32_t u0, u1;

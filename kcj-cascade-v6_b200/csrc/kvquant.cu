@@ -8,7 +8,8 @@
 //   1. kv_minmax_kernel: the int16 min/max of every block (warp reductions,
 //      one atomicMin/atomicMax pair per warp and unit);
 //   2. kv_pack_kernel: header + one int8 code per value (16-byte loads from
-//      HBM, 8-byte stores to the arena).
+//      HBM, 16-byte stores to the arena: the store starts every packed block
+//      8 bytes into its extent so that the int8 payload is 16-byte aligned).
 // Both walk the same kCopyUnit units as the copy kernels (units.cuh). The
 // inverse (unpack) runs inside the copy kernels on kCopyUnpack descriptors.
 #include <climits>
@@ -28,6 +29,10 @@ CB_D int ld_i16(const uint8_t *p) { return (int)(short)((uint32_t)p[0] | ((uint3
 
 CB_D void st_plain8(void *p, uint2 v) {
   asm volatile("st.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y) : "memory");
+}
+CB_D void st_plain16(void *p, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
 
 // Values [e0, e1) of the unit that starts at source byte 2*e0.
@@ -121,17 +126,32 @@ __global__ void __launch_bounds__(kThreads) kv_pack_kernel(const CopyDesc *__res
     const uint8_t *s = reinterpret_cast<const uint8_t *>(d.src) + 2 * e0;
     uint8_t *q = blk + kPackHeaderBytes + e0;
     uint64_t done = 0;
-    if (((reinterpret_cast<uintptr_t>(s) & 15) | (reinterpret_cast<uintptr_t>(q) & 7)) == 0) {
-      const uint64_t ng = (e1 - e0) / 8;
-      const uint4 *s16 = reinterpret_cast<const uint4 *>(s);
-      uint2 *q8 = reinterpret_cast<uint2 *>(q);
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(s), qa = reinterpret_cast<uintptr_t>(q);
+    const uint4 *s16 = reinterpret_cast<const uint4 *>(s);
+    if (((sa | qa) & 15) == 0) {
+      // 16 values (two 16-byte loads) -> 16 codes (one 16-byte store). The
+      // store places packed blocks so that q is 16-byte aligned.
+      const uint64_t ng = (e1 - e0) / 16;
+      uint4 *q16 = reinterpret_cast<uint4 *>(q);
       uint64_t g = threadIdx.x;
       for (; g + blockDim.x < ng; g += 2 * (uint64_t)blockDim.x) {
-        const uint4 a = __ldg(s16 + g), b = __ldg(s16 + g + blockDim.x);
-        st_plain8(q8 + g, pack8(a, p));
-        st_plain8(q8 + g + blockDim.x, pack8(b, p));
+        const uint64_t h = g + blockDim.x;
+        const uint4 a0 = __ldg(s16 + 2 * g), a1 = __ldg(s16 + 2 * g + 1);
+        const uint4 b0 = __ldg(s16 + 2 * h), b1 = __ldg(s16 + 2 * h + 1);
+        const uint2 wa0 = pack8(a0, p), wa1 = pack8(a1, p), wb0 = pack8(b0, p), wb1 = pack8(b1, p);
+        st_plain16(q16 + g, make_uint4(wa0.x, wa0.y, wa1.x, wa1.y));
+        st_plain16(q16 + h, make_uint4(wb0.x, wb0.y, wb1.x, wb1.y));
       }
-      for (; g < ng; g += blockDim.x) st_plain8(q8 + g, pack8(__ldg(s16 + g), p));
+      for (; g < ng; g += blockDim.x) {
+        const uint2 w0 = pack8(__ldg(s16 + 2 * g), p), w1 = pack8(__ldg(s16 + 2 * g + 1), p);
+        st_plain16(q16 + g, make_uint4(w0.x, w0.y, w1.x, w1.y));
+      }
+      done = ng * 16;
+    } else if ((sa & 15) == 0 && (qa & 7) == 0) {
+      // 8 values (one 16-byte load) -> 8 codes (one 8-byte store)
+      const uint64_t ng = (e1 - e0) / 8;
+      uint2 *q8 = reinterpret_cast<uint2 *>(q);
+      for (uint64_t g = threadIdx.x; g < ng; g += blockDim.x) st_plain8(q8 + g, pack8(__ldg(s16 + g), p));
       done = ng * 8;
     }
     for (uint64_t k = done + threadIdx.x; k < e1 - e0; k += blockDim.x)

@@ -59,9 +59,15 @@ CB_D int lo16s(uint32_t w) { return (int)(short)(w & 0xffffu); }
 CB_D int hi16s(uint32_t w) { return (int)(short)(w >> 16); }
 CB_D int byte_s(uint32_t w, int k) { return (int)(signed char)((w >> (8 * k)) & 0xffu); }
 
-CB_D uint2 ld_plain8(const void *p) {
+// Plain (coherent) loads: the packed side may be mapped pinned host memory.
+CB_D uint2 ld_host8(const void *p) {
   uint2 r;
   asm volatile("ld.global.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+CB_D uint4 ld_host16(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
   return r;
 }
 
@@ -76,12 +82,14 @@ CB_D uint2 unpack4(uint32_t w, float scale, float zmin) {
 // Writes bytes [off, off + len) of the unpacked form of the packed block at
 // blk into out + off, with threads tid = 0..nt-1 of the caller's group. off
 // is a multiple of 16 (a copy unit boundary) and len is even. blk may be
-// mapped pinned host memory (plain loads throughout).
+// mapped pinned host memory (plain loads throughout). The store places packed
+// blocks so that the payload (blk + 8) is 16-byte aligned; other alignments
+// (caller buffers) take 8-byte or byte-wise paths.
 CB_D void unpack_range(const uint8_t *blk, uint8_t *out, uint64_t off, uint64_t len, int tid, int nt) {
   float scale;
   int zp;
   if ((reinterpret_cast<uintptr_t>(blk) & 7) == 0) {
-    const uint2 h = ld_plain8(blk);
+    const uint2 h = ld_host8(blk);
     scale = __uint_as_float(h.x);
     zp = byte_s(h.y, 0);
   } else {
@@ -94,26 +102,42 @@ CB_D void unpack_range(const uint8_t *blk, uint8_t *out, uint64_t off, uint64_t 
   const uint8_t *q = blk + kPackHeaderBytes + off / 2;
   uint8_t *o = out + off;
   const uint64_t ne = len / 2;
+  const uintptr_t qa = reinterpret_cast<uintptr_t>(q), oa = reinterpret_cast<uintptr_t>(o);
   uint64_t done = 0;
-  if (((reinterpret_cast<uintptr_t>(q) & 7) | (reinterpret_cast<uintptr_t>(o) & 15)) == 0) {
-    // 8 codes (one 8-byte load) -> 8 values (one 16-byte store); 4 loads in
-    // flight per thread to cover the host-link latency.
-    const uint64_t ng = ne / 8;
-    const uint2 *q8 = reinterpret_cast<const uint2 *>(q);
+  if (((qa | oa) & 15) == 0) {
+    // 16 codes (one 16-byte load) -> 16 values (two 16-byte stores); 4 loads
+    // in flight per thread to cover the host-link latency.
+    const uint64_t ng = ne / 16;
+    const uint4 *q16 = reinterpret_cast<const uint4 *>(q);
     uint4 *o16 = reinterpret_cast<uint4 *>(o);
     uint64_t g = tid;
     for (; g + 3 * (uint64_t)nt < ng; g += 4 * (uint64_t)nt) {
-      uint2 w[4];
+      uint4 w[4];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) w[k] = ld_plain8(q8 + g + k * nt);
+      for (int k = 0; k < 4; ++k) w[k] = ld_host16(q16 + g + k * nt);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         const uint2 a = unpack4(w[k].x, scale, zmin), b = unpack4(w[k].y, scale, zmin);
-        o16[g + k * nt] = make_uint4(a.x, a.y, b.x, b.y);
+        const uint2 c = unpack4(w[k].z, scale, zmin), d = unpack4(w[k].w, scale, zmin);
+        o16[2 * (g + k * nt)] = make_uint4(a.x, a.y, b.x, b.y);
+        o16[2 * (g + k * nt) + 1] = make_uint4(c.x, c.y, d.x, d.y);
       }
     }
     for (; g < ng; g += nt) {
-      const uint2 w = ld_plain8(q8 + g);
+      const uint4 w = ld_host16(q16 + g);
+      const uint2 a = unpack4(w.x, scale, zmin), b = unpack4(w.y, scale, zmin);
+      const uint2 c = unpack4(w.z, scale, zmin), d = unpack4(w.w, scale, zmin);
+      o16[2 * g] = make_uint4(a.x, a.y, b.x, b.y);
+      o16[2 * g + 1] = make_uint4(c.x, c.y, d.x, d.y);
+    }
+    done = ng * 16;
+  } else if ((qa & 7) == 0 && (oa & 15) == 0) {
+    // 8 codes (one 8-byte load) -> 8 values (one 16-byte store)
+    const uint64_t ng = ne / 8;
+    const uint2 *q8 = reinterpret_cast<const uint2 *>(q);
+    uint4 *o16 = reinterpret_cast<uint4 *>(o);
+    for (uint64_t g = tid; g < ng; g += nt) {
+      const uint2 w = ld_host8(q8 + g);
       const uint2 a = unpack4(w.x, scale, zmin), b = unpack4(w.y, scale, zmin);
       o16[g] = make_uint4(a.x, a.y, b.x, b.y);
     }

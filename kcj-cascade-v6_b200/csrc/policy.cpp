@@ -87,6 +87,13 @@ void Policy::touch(const HKey &k) {
   m.stamp = ++clock_;
 }
 
+void Policy::protect(const HKey &k) {
+  auto it = map_.find(k);
+  if (it == map_.end() || it->second.pending) return;
+  it->second.pending = 1;
+  pending_.push_back(k);
+}
+
 void Policy::clear() {
   map_.clear();
   for (auto &t : lru_)
@@ -139,7 +146,7 @@ void Policy::drop(const HKey &k, std::vector<HKey> &dropped) {
     hbm_.free(m.off, m.size);
     hbm_used_ -= m.size;
   } else {
-    dram_.free(m.off, footprint(m));
+    dram_.free(m.off, extent_bytes(m));
     dram_used_ -= footprint(m);
     ctr_.dram_evictions++;
   }
@@ -150,9 +157,9 @@ void Policy::drop(const HKey &k, std::vector<HKey> &dropped) {
   map_.erase(it);
 }
 
-bool Policy::make_dram_room(uint64_t size, std::vector<HKey> &dropped) {
-  if (dram_cap_ == 0 || size > dram_cap_) return false;
-  const uint64_t need = std::max(dram_.rounded(size), (uint64_t)256);
+bool Policy::make_dram_room(uint64_t size, uint64_t extent, std::vector<HKey> &dropped) {
+  if (dram_cap_ == 0 || size > dram_cap_ || extent > dram_.capacity()) return false;
+  const uint64_t need = std::max(dram_.rounded(extent), (uint64_t)256);
   while (dram_used_ + size > dram_cap_ || dram_.largest_free() < need) {
     // DistributedDRAMBackend::evict_for_space: LRU tail, prefix blocks
     // protected with no fallback (distributed_backend.cpp:240-284).
@@ -172,15 +179,17 @@ bool Policy::demote_one(std::vector<TierMove> &moves, std::vector<HKey> &dropped
   // (distributed_backend.cpp:898-903).
   const bool pack = compress_ && m.size >= kPackMinBytes;
   const uint64_t dbytes = pack ? packed_bytes(m.size) : m.size;
-  if (!make_dram_room(dbytes, dropped)) {
+  const uint64_t dext = pack ? kPackLead + dbytes : dbytes;
+  if (!make_dram_room(dbytes, dext, dropped)) {
     // No DRAM room: the reference sends the victim to Lustre
     // (distributed_backend.cpp:915-918); without that tier it is dropped.
     drop(v, dropped);
     return true;
   }
   BlockMeta &mm = map_.at(v);  // make_dram_room never drops pending/HBM blocks
-  const uint64_t doff = dram_.alloc(dbytes);
-  moves.push_back(TierMove{v, kTierHbm, kTierDram, mm.off, doff, mm.size, pack ? kMovePack : kMoveCopy});
+  const uint64_t doff = dram_.alloc(dext);
+  moves.push_back(
+      TierMove{v, kTierHbm, kTierDram, mm.off, doff + (pack ? kPackLead : 0), mm.size, pack ? kMovePack : kMoveCopy});
   hbm_.free(mm.off, mm.size);
   hbm_used_ -= mm.size;
   dram_used_ += dbytes;
@@ -243,8 +252,9 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
       // on (:615-620).
       pack = compress_ && size >= kPackMinBytes;
       const uint64_t dbytes = pack ? packed_bytes(size) : size;
-      if (make_dram_room(dbytes, plan.dropped)) {
-        off = dram_.alloc(dbytes);
+      const uint64_t dext = pack ? kPackLead + dbytes : dbytes;
+      if (make_dram_room(dbytes, dext, plan.dropped)) {
+        off = dram_.alloc(dext);
         tier = kTierDram;
       }
     }
@@ -273,7 +283,7 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
       if (pack) ctr_.compression_savings += size - packed_bytes(size);
     }
     if (pf) ctr_.prefix_blocks++;
-    plan.places.push_back(Placement{i, k, off, size, pf, tier, (uint8_t)(pack ? 1 : 0)});
+    plan.places.push_back(Placement{i, k, off + (pack ? kPackLead : 0), size, pf, tier, (uint8_t)(pack ? 1 : 0)});
   }
 }
 
@@ -298,12 +308,12 @@ bool Policy::plan_promote(const HKey &k, std::vector<TierMove> &moves,
   const uint64_t hoff = hbm_.alloc(size);
   if (hoff == UINT64_MAX) return false;
   BlockMeta &m = map_.at(k);
-  moves.push_back(TierMove{k, kTierDram, kTierHbm, m.off, hoff, size, m.packed ? kMoveUnpack : kMoveCopy});
+  moves.push_back(TierMove{k, kTierDram, kTierHbm, data_offset(m), hoff, size, m.packed ? kMoveUnpack : kMoveCopy});
   // The DRAM extent is released now; no later move of this plan writes DRAM
   // after promotions read it because the store runs every HBM->DRAM move of a
   // plan before any DRAM->HBM move, and DRAM destinations of those demotions
   // were allocated while this extent was still held.
-  deferred_free_.push_back({m.off, footprint(m)});
+  deferred_free_.push_back({m.off, extent_bytes(m)});
   dram_used_ -= footprint(m);
   hbm_used_ += size;
   m.packed = 0;

@@ -80,6 +80,9 @@ enum : uint8_t { kTierHbm = 0, kTierDram = 1 };
 // INT8 packing of DRAM-tier blocks (KVCompressor, include/cascade.hpp:386-418).
 constexpr uint64_t kPackHeaderBytes = 8;  // [f32 scale][i8 zero point][3 pad]
 constexpr uint64_t kPackMinBytes = 64;    // smaller blocks are stored as they are
+// A packed block starts kPackLead bytes into its (256-byte aligned) extent so
+// that its int8 payload, after the 8-byte header, is 16-byte aligned.
+constexpr uint64_t kPackLead = 8;
 inline uint64_t packed_bytes(uint64_t size) { return kPackHeaderBytes + size / 2; }
 
 // How a tier move transforms the bytes it moves.
@@ -97,20 +100,25 @@ struct BlockMeta {
 };
 
 // A tier move the store executes from (src_tier, src_off) to (dst_tier,
-// dst_off). Moves of one plan run in vector order. size = bytes on the plain
-// side: kMoveCopy copies size bytes, kMovePack packs a size-byte block into
-// packed_bytes(size) bytes, kMoveUnpack unpacks into size (even) bytes.
+// dst_off); the offsets are those of the block's first byte. Moves of one
+// plan run in vector order. size = bytes on the plain side: kMoveCopy copies
+// size bytes, kMovePack packs a size-byte block into packed_bytes(size)
+// bytes, kMoveUnpack unpacks into size (even) bytes.
 struct TierMove {
   HKey key;
   uint8_t src_tier, dst_tier;
   uint64_t src_off, dst_off, size;
   uint8_t op = kMoveCopy;
+  // Set by the store: a device address holding the block's (unpacked) bytes
+  // to read instead of the source tier (a promotion after a get that has
+  // just copied the block into a device buffer). 0 = read the source tier.
+  uint64_t src_dev = 0;
 };
 
 struct Placement {
   int32_t idx;  // batch index
   HKey key;
-  uint64_t off;  // offset in the tier's arena
+  uint64_t off;  // offset of the block's first byte in the tier's arena
   uint64_t size;
   uint8_t prefix;
   uint8_t tier;  // kTierHbm normally; kTierDram when larger than the HBM pool
@@ -159,6 +167,9 @@ class Policy {
 
   const BlockMeta *find(const HKey &k) const;
   void touch(const HKey &k);  // mark most recently used
+  // Keep a block out of every victim choice until commit() (a get is still
+  // reading it while this plan's moves run).
+  void protect(const HKey &k);
   void clear();
 
   uint64_t hbm_used() const { return hbm_used_; }
@@ -175,8 +186,12 @@ class Policy {
   // INT8 packing of DRAM-tier blocks >= kPackMinBytes (kv_compression).
   void set_compression(bool on) { compress_ = on; }
   bool compression() const { return compress_; }
-  // Bytes a block occupies in its tier's arena (logical, before rounding).
+  // Bytes a block holds in its tier (logical, the reference's used bytes).
   static uint64_t footprint(const BlockMeta &m) { return m.packed ? packed_bytes(m.size) : m.size; }
+  // Bytes of its extent in the arena (a packed block starts kPackLead in).
+  static uint64_t extent_bytes(const BlockMeta &m) { return m.packed ? kPackLead + packed_bytes(m.size) : m.size; }
+  // Byte offset of the block's first byte in its tier's arena.
+  static uint64_t data_offset(const BlockMeta &m) { return m.off + (m.packed ? kPackLead : 0); }
   template <class F>
   void for_each(F f) const {
     for (const auto &kv : map_) f(kv.first, kv.second);
@@ -184,7 +199,8 @@ class Policy {
 
  private:
   bool make_hbm_room(uint64_t size, std::vector<TierMove> &moves, std::vector<HKey> &dropped);
-  bool make_dram_room(uint64_t size, std::vector<HKey> &dropped);
+  // Room for a block holding `size` bytes in an extent of `extent` bytes.
+  bool make_dram_room(uint64_t size, uint64_t extent, std::vector<HKey> &dropped);
   bool demote_one(std::vector<TierMove> &moves, std::vector<HKey> &dropped);
   bool pick_victim(uint8_t tier, bool prefix_fallback, HKey &out) const;
   void drop(const HKey &k, std::vector<HKey> &dropped);

@@ -124,8 +124,9 @@ int Store::init() {
   profile = cfg.profile != 0;
   policy.set_compression(cfg.kv_compression != 0);
   hash_lanes = (cfg.hash_lanes == 8 || cfg.hash_lanes == 16) ? cfg.hash_lanes : 32;
-  CB_TRY(cudaEventCreate(&ev_a), "event");
-  CB_TRY(cudaEventCreate(&ev_b), "event");
+  CB_TRY(cudaStreamCreateWithFlags(&move_stream, cudaStreamNonBlocking), "move stream");
+  CB_TRY(cudaEventCreateWithFlags(&ev_move_in, cudaEventDisableTiming), "event");
+  CB_TRY(cudaEventCreateWithFlags(&ev_move_done, cudaEventDisableTiming), "event");
   CB_TRY(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "copy stream");
   CB_TRY(cudaEventCreateWithFlags(&ev_reset, cudaEventDisableTiming), "event");
   CB_TRY(cudaEventCreateWithFlags(&ev_copies, cudaEventDisableTiming), "event");
@@ -146,8 +147,15 @@ Store::~Store() {
   h_out.release();
   h_err.release();
   d_staging.release();
-  if (ev_a) cudaEventDestroy(ev_a);
-  if (ev_b) cudaEventDestroy(ev_b);
+  if (move_stream) {
+    cudaStreamSynchronize(move_stream);
+    cudaStreamDestroy(move_stream);
+  }
+  if (ev_move_in) cudaEventDestroy(ev_move_in);
+  if (ev_move_done) cudaEventDestroy(ev_move_done);
+  for (cudaEvent_t e : prof_events) cudaEventDestroy(e);
+  h_mscratch.release();
+  d_mscratch.release();
   if (copy_stream) {
     cudaStreamSynchronize(copy_stream);
     cudaStreamDestroy(copy_stream);
@@ -201,7 +209,7 @@ int Store::reserve_index(uint64_t incoming, cudaStream_t st) {
   std::vector<IndexRec> recs;
   recs.reserve(live);
   policy.for_each([&](const HKey &k, const BlockMeta &m) {
-    recs.push_back(IndexRec{k.lo, k.hi, m.off | (m.tier == kTierDram ? kLocDram : 0),
+    recs.push_back(IndexRec{k.lo, k.hi, Policy::data_offset(m) | (m.tier == kTierDram ? kLocDram : 0),
                             meta_word(m.size, m.prefix) | (m.packed ? kMetaPacked : 0)});
   });
   const size_t bytes = recs.size() * sizeof(IndexRec);
@@ -218,10 +226,34 @@ int Store::reserve_index(uint64_t incoming, cudaStream_t st) {
   return CB_OK;
 }
 
+cudaError_t Store::prof_event(cudaEvent_t &e) {
+  if (prof_events_used == prof_events.size()) {
+    cudaEvent_t ne;
+    cudaError_t r = cudaEventCreate(&ne);
+    if (r != cudaSuccess) return r;
+    prof_events.push_back(ne);
+  }
+  e = prof_events[prof_events_used++];
+  return cudaSuccess;
+}
+
+void Store::resolve_prof() {
+  for (const ProfRec &r : prof_pending) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(r.b) != cudaSuccess || cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) continue;
+    prof_ns[r.kind] += (uint64_t)(ms * 1.0e6);
+    prof_bytes[r.kind] += r.bytes;
+    prof_launches[r.kind]++;
+  }
+  prof_pending.clear();
+  prof_events_used = 0;
+}
+
 // Reads and clears the device error word (after a stream sync).
 int Store::check_device_error(cudaStream_t st) {
   CB_TRY(cudaMemcpyAsync(h_err.ptr, d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "D2H err");
   CB_TRY(cudaStreamSynchronize(st), "stream sync");
+  resolve_prof();
   const unsigned e = *static_cast<unsigned *>(h_err.ptr);
   if (!e) return CB_OK;
   CB_TRY(cudaMemsetAsync(d_err, 0, sizeof(unsigned), st), "clear err");
@@ -251,9 +283,9 @@ static uint32_t units_of(uint64_t size) {
 
 // Executes tier moves (HBM->DRAM first, then DRAM->HBM), index updates for
 // moved blocks and index erases for dropped blocks, stream-ordered on st.
-int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped,
-                     cudaStream_t st) {
-  if (moves.empty() && dropped.empty()) return CB_OK;
+int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped, cudaStream_t st,
+                     const std::function<int()> &concurrent) {
+  if (moves.empty() && dropped.empty()) return concurrent ? concurrent() : CB_OK;
   bool need_dram = false;
   for (const auto &m : moves) need_dram |= (m.src_tier == kTierDram || m.dst_tier == kTierDram);
   if (need_dram) {
@@ -274,9 +306,9 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
   const size_t o_mm = L.add(sizeof(int) * 2 * npk);
   const size_t o_upd = L.add(sizeof(IndexRec) * nm);
   const size_t o_era = L.add(sizeof(IndexRec) * nd);
-  CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
-  CB_TRY(d_scratch.ensure(L.off), "device scratch");
-  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  CB_TRY(h_mscratch.ensure(L.off), "pinned scratch");
+  CB_TRY(d_mscratch.ensure(L.off), "device scratch");
+  uint8_t *h = static_cast<uint8_t *>(h_mscratch.ptr);
   CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
   int *mm = reinterpret_cast<int *>(h + o_mm);
   IndexRec *upd = reinterpret_cast<IndexRec *>(h + o_upd);
@@ -284,6 +316,7 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
   uint32_t total[3] = {0, 0, 0};
   uint64_t grp_bytes[3] = {0, 0, 0};
   int base[3] = {0, 0, 0};
+  bool dev_only[3] = {true, true, true};  // no host-memory side in the group
   int di = 0;
   for (int g = 0; g < 3; ++g) {
     uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us[g]);
@@ -292,7 +325,12 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
       const TierMove &m = *grp[g][j];
       const uint64_t src = m.src_tier == kTierDram ? (uint64_t)dram_dev + m.src_off : (uint64_t)pool + m.src_off;
       const uint64_t dst = m.dst_tier == kTierDram ? (uint64_t)dram_dev + m.dst_off : (uint64_t)pool + m.dst_off;
-      desc[di + j] = CopyDesc{src, dst, m.size, kCopyHost | (m.op == kMoveUnpack ? kCopyUnpack : 0)};
+      if (m.src_dev) {
+        desc[di + j] = CopyDesc{m.src_dev, dst, m.size, 0};  // device -> HBM, already unpacked
+      } else {
+        desc[di + j] = CopyDesc{src, dst, m.size, kCopyHost | (m.op == kMoveUnpack ? kCopyUnpack : 0)};
+        dev_only[g] = false;
+      }
       us[j] = total[g];
       total[g] += units_of(m.size);
       grp_bytes[g] += m.size;
@@ -310,26 +348,58 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     mm[2 * j + 1] = INT_MIN;
   }
   for (int j = 0; j < nd; ++j) era[j] = IndexRec{dropped[j].lo, dropped[j].hi, 0, 0};
-  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  uint8_t *d = static_cast<uint8_t *>(d_mscratch.ptr);
   CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D moves");
   const CopyDesc *ddesc = reinterpret_cast<const CopyDesc *>(d + o_desc);
-  for (int g = 0; g < 3; ++g) {
-    if (grp[g].empty()) continue;
+  // Demotions: on st, or on move_stream beside the caller's concurrent work.
+  cudaStream_t ds = st;
+  if (concurrent) {
+    CB_TRY(cudaEventRecord(ev_move_in, st), "event");
+    CB_TRY(cudaStreamWaitEvent(move_stream, ev_move_in, 0), "wait");
+    ds = move_stream;
+  }
+  auto launch_group = [&](int g, cudaStream_t gs) -> int {
+    if (grp[g].empty()) return CB_OK;
     const CopyDesc *gd = ddesc + base[g];
     const uint32_t *gu = reinterpret_cast<const uint32_t *>(d + o_us[g]);
     const int gn = (int)grp[g].size();
     if (g == 1) {
-      CB_TRY(timed(3, grp_bytes[g], st,
+      CB_TRY(timed(3, grp_bytes[g], gs,
                    [&] {
-                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + o_mm), num_sms, st);
+                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + o_mm), num_sms, gs);
                    }),
              "demote pack");
       launches++;  // two kernels
     } else {
-      CB_TRY(timed(3, grp_bytes[g], st,
-                   [&] { return launch_batch_copy(gd, gu, gn, total[g], 2, d_err, num_sms, st); }),
+      // host-link moves on the LSU engine; device-only groups on the store's
+      const int engine = dev_only[g] ? copy_engine : 2;
+      CB_TRY(timed(3, grp_bytes[g], gs,
+                   [&] { return launch_batch_copy(gd, gu, gn, total[g], engine, d_err, num_sms, gs); }),
              g ? "promote copy" : "demote copy");
     }
+    return CB_OK;
+  };
+  int rc = launch_group(0, ds);
+  if (rc == CB_OK) rc = launch_group(1, ds);
+  if (concurrent) {
+    // join: whatever happens, st waits for the demotions before going on
+    const cudaError_t e = cudaEventRecord(ev_move_done, move_stream);
+    if (rc == CB_OK && e == cudaSuccess) rc = concurrent();
+    if (e == cudaSuccess) cudaStreamWaitEvent(st, ev_move_done, 0);
+    if (e != cudaSuccess) {
+      cudaStreamSynchronize(move_stream);
+      return cuda_fail(e, "event");
+    }
+  }
+  if (rc) {
+    cudaStreamSynchronize(move_stream);
+    cudaStreamSynchronize(st);
+    return rc;
+  }
+  rc = launch_group(2, st);
+  if (rc) {
+    cudaStreamSynchronize(st);
+    return rc;
   }
   if (nm) {
     CB_TRY(launch_index_update(table, table_slots - 1, reinterpret_cast<const IndexRec *>(d + o_upd), nm,
@@ -345,9 +415,10 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
   }
   table_tombs += nd;
   table_used -= std::min<uint64_t>(table_used, nd);
-  // The scratch buffers are reused by the next phase: wait for the copies
-  // of this phase's descriptors to be consumed.
+  // The scratch buffers are reused by the next plan: wait for the copies
+  // of this plan's descriptors to be consumed.
   CB_TRY(cudaStreamSynchronize(st), "moves");
+  resolve_prof();
   return CB_OK;
 }
 
@@ -625,41 +696,80 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
     }
   }
   us[n] = total;
-  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
-  CB_TRY(cudaMemcpyAsync(d, h, o_desc, cudaMemcpyHostToDevice, st), "H2D get");
-  LookupArgs a;
-  a.table = table;
-  a.mask = table_slots - 1;
-  a.keys = reinterpret_cast<const Key *>(d + o_keys);
-  a.outs = reinterpret_cast<const uint64_t *>(d + o_outs);
-  a.caps = reinterpret_cast<const uint64_t *>(d + o_caps);
-  a.unit_start = reinterpret_cast<const uint32_t *>(d + o_us);
-  a.n = n;
-  a.pool_base = (uint64_t)pool;
-  a.pool_bytes = pool_bytes;
-  a.dram_base = (uint64_t)dram_dev;
-  a.dram_bytes = dram_host ? dram_bytes : 0;
-  a.code_hbm = CB_FOUND_LOCAL_HBM;
-  a.code_dram = CB_FOUND_LOCAL_DRAM;
-  a.desc = reinterpret_cast<CopyDesc *>(d + o_desc);
-  a.res = reinterpret_cast<GetResult *>(d + o_res);
-  a.err = d_err;
-  CB_TRY(launch_index_lookup(a, st), "index lookup");
-  launches++;
-  if (total) {
-    CB_TRY(timed(2, bytes, st,
-                 [&] { return launch_batch_copy(a.desc, a.unit_start, n, total, copy_engine, d_err, num_sms, st); }),
-           "gather");
-  }
-  CB_TRY(cudaMemcpyAsync(h_out.ptr, d + o_res, sizeof(GetResult) * n, cudaMemcpyDeviceToHost, st),
-         "D2H results");
-  // LRU touches overlap the device work (CascadeStore::get touches on hit,
-  // src/cascade_core.cpp:1281).
+  // LRU touches first (CascadeStore::get touches on hit,
+  // src/cascade_core.cpp:1281), so that blocks of this batch are the last
+  // victims of the promotions below.
   for (int i = 0; i < n; ++i) policy.touch(to_hkey(keys + 16 * i));
-  int rc = check_device_error(st);
+  // Promotion on a DRAM hit (CascadeStore::get -> promote_to_gpu,
+  // src/cascade_core.cpp:1303-1307, :1166-1185; DistributedStore::get ->
+  // promote_to_local_gpu(id, out, size), src/distributed_backend.cpp:721-723).
+  // The host metadata already knows which requests are DRAM hits that will
+  // be copied, so the promotions are planned before the lookup: the
+  // demotions that make room for them (HBM -> DRAM, the device-to-host
+  // direction of the host link) run on move_stream while the gather reads
+  // the DRAM hits (host-to-device); the promotions then read the copy the
+  // gather made in the caller's buffer (or the staging slot of a host get),
+  // already unpacked, like the reference, instead of reading DRAM again.
+  std::vector<TierMove> moves;
+  std::vector<HKey> dropped;
+  bool planned = false;
+  if (cfg.promote_on_hit && policy.dram_used() > 0) {
+    std::unordered_map<HKey, uint64_t, HKeyHash> copy_of;
+    std::vector<HKey> order;
+    for (int i = 0; i < n; ++i) {
+      const HKey k = to_hkey(keys + 16 * i);
+      const BlockMeta *m = policy.find(k);
+      if (m && m->tier == kTierDram && m->size && m->size <= caps[i] && copy_of.emplace(k, outs[i]).second)
+        order.push_back(k);
+    }
+    // every DRAM block this get reads stays put (and its extent unused)
+    // until the batch ends, whatever the plans for the others evict
+    for (const HKey &k : order) policy.protect(k);
+    for (const HKey &k : order) policy.plan_promote(k, moves, dropped);
+    for (TierMove &mv : moves) {
+      if (mv.src_tier != kTierDram || mv.dst_tier != kTierHbm) continue;
+      auto it = copy_of.find(mv.key);
+      if (it != copy_of.end()) mv.src_dev = it->second;
+    }
+    planned = !order.empty();
+  }
+  uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+  auto lookup_and_gather = [&]() -> int {
+    CB_TRY(cudaMemcpyAsync(d, h, o_desc, cudaMemcpyHostToDevice, st), "H2D get");
+    LookupArgs a;
+    a.table = table;
+    a.mask = table_slots - 1;
+    a.keys = reinterpret_cast<const Key *>(d + o_keys);
+    a.outs = reinterpret_cast<const uint64_t *>(d + o_outs);
+    a.caps = reinterpret_cast<const uint64_t *>(d + o_caps);
+    a.unit_start = reinterpret_cast<const uint32_t *>(d + o_us);
+    a.n = n;
+    a.pool_base = (uint64_t)pool;
+    a.pool_bytes = pool_bytes;
+    a.dram_base = (uint64_t)dram_dev;
+    a.dram_bytes = dram_host ? dram_bytes : 0;
+    a.code_hbm = CB_FOUND_LOCAL_HBM;
+    a.code_dram = CB_FOUND_LOCAL_DRAM;
+    a.desc = reinterpret_cast<CopyDesc *>(d + o_desc);
+    a.res = reinterpret_cast<GetResult *>(d + o_res);
+    a.err = d_err;
+    CB_TRY(launch_index_lookup(a, st), "index lookup");
+    launches++;
+    if (total) {
+      CB_TRY(timed(2, bytes, st,
+                   [&] { return launch_batch_copy(a.desc, a.unit_start, n, total, copy_engine, d_err, num_sms, st); }),
+             "gather");
+    }
+    CB_TRY(cudaMemcpyAsync(h_out.ptr, d + o_res, sizeof(GetResult) * n, cudaMemcpyDeviceToHost, st),
+           "D2H results");
+    return CB_OK;
+  };
+  int rc = run_moves(moves, dropped, st, lookup_and_gather);
+  if (planned) policy.commit();
+  if (rc) return rc;
+  rc = check_device_error(st);
   if (rc) return rc;
   const GetResult *res = static_cast<const GetResult *>(h_out.ptr);
-  std::vector<HKey> promote;
   for (int i = 0; i < n; ++i) {
     sizes_out[i] = res[i].size;
     found_out[i] = (uint8_t)res[i].code;
@@ -670,23 +780,7 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
       local_gpu_hits++;
     } else if (tier == CB_FOUND_LOCAL_DRAM) {
       local_dram_hits++;
-      if (cfg.promote_on_hit) promote.push_back(to_hkey(keys + 16 * i));
     }
-  }
-  if (!promote.empty()) {
-    // Promotion on a DRAM hit (CascadeStore::get -> promote_to_gpu,
-    // src/cascade_core.cpp:1303-1307, :1166-1185).
-    std::vector<TierMove> moves;
-    std::vector<HKey> dropped;
-    for (const HKey &k : promote) {
-      const BlockMeta *m = policy.find(k);
-      if (m && m->tier == kTierDram) policy.plan_promote(k, moves, dropped);
-    }
-    rc = run_moves(moves, dropped, st);
-    policy.commit();
-    if (rc) return rc;
-    rc = check_device_error(st);
-    if (rc) return rc;
   }
   return CB_OK;
 }
@@ -1109,7 +1203,7 @@ int cb_locate(cb_store *h, const uint8_t *key, cb_location *out, int32_t *found)
     if (!m) return CB_OK;
     out->node_id = s->rank;
     out->gpu_id = m->tier == cb::kTierHbm ? s->device : -1;
-    out->offset = m->off;
+    out->offset = cb::Policy::data_offset(*m);
     out->size = m->size;
     out->is_gpu = m->tier == cb::kTierHbm;
     out->is_prefix = m->prefix;
@@ -1124,6 +1218,7 @@ int cb_evict(cb_store *h, uint64_t bytes, uint64_t *evicted_bytes) {
 int cb_get_stats(cb_store *h, cb_stats *out) {
   return guarded(h, [&](Store *s) -> int {
     if (!out) return s->fail(CB_ERR_ARG, "bad arguments");
+    s->resolve_prof();  // records of batches that ended without a store-side sync
     s->fill_stats(out);
     if (s->world > 1) return s->dht_cluster_usage(out);
     return CB_OK;

@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <functional>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -76,34 +77,38 @@ struct Store {
   DhtState *dht = nullptr;
 
   // Kernel accounting. kinds: 0 SHA-256, 1 scatter, 2 gather, 3 tier move.
+  // With profiling on, every launch is bracketed by two CUDA events on its
+  // stream; the pairs are read after the batch's final synchronisation
+  // (resolve_prof), so profiling does not serialise streams.
   bool profile = false;
-  cudaEvent_t ev_a = nullptr, ev_b = nullptr;
   uint64_t launches = 0;
   uint64_t prof_ns[4] = {0, 0, 0, 0}, prof_bytes[4] = {0, 0, 0, 0}, prof_launches[4] = {0, 0, 0, 0};
+  struct ProfRec {
+    int kind;
+    uint64_t bytes;
+    cudaEvent_t a, b;
+  };
+  std::vector<cudaEvent_t> prof_events;
+  size_t prof_events_used = 0;
+  std::vector<ProfRec> prof_pending;
+  cudaError_t prof_event(cudaEvent_t &e);
+  void resolve_prof();  // after every stream with pending records is idle
 
-  // Runs `launch` (one kernel) and, when profiling, times it with CUDA events
-  // recorded on the launching stream. `bytes` = payload bytes it processes.
+  // Runs `launch` (one or two kernels on stream st) and, when profiling,
+  // brackets it with events. `bytes` = payload bytes it processes.
   template <class F>
   cudaError_t timed(int kind, uint64_t bytes, cudaStream_t st, F launch) {
-    if (!profile) {
-      cudaError_t e = launch();
-      launches++;
-      return e;
-    }
-    cudaError_t e = cudaEventRecord(ev_a, st);
+    launches++;
+    if (!profile) return launch();
+    cudaEvent_t a, b;
+    cudaError_t e = prof_event(a);
+    if (e == cudaSuccess) e = prof_event(b);
+    if (e == cudaSuccess) e = cudaEventRecord(a, st);
     if (e != cudaSuccess) return e;
     e = launch();
     if (e != cudaSuccess) return e;
-    e = cudaEventRecord(ev_b, st);
-    if (e != cudaSuccess) return e;
-    e = cudaEventSynchronize(ev_b);
-    if (e != cudaSuccess) return e;
-    float ms = 0.f;
-    e = cudaEventElapsedTime(&ms, ev_a, ev_b);
-    prof_ns[kind] += (uint64_t)(ms * 1.0e6);
-    prof_bytes[kind] += bytes;
-    prof_launches[kind]++;
-    launches++;
+    e = cudaEventRecord(b, st);
+    if (e == cudaSuccess) prof_pending.push_back(ProfRec{kind, bytes, a, b});
     return e;
   }
 
@@ -114,8 +119,15 @@ struct Store {
   cudaError_t ensure_dram();
   int reserve_index(uint64_t incoming, cudaStream_t st);
   int check_device_error(cudaStream_t st);
-  int run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped,
-                cudaStream_t st);
+  // Runs a plan's tier moves on st. With `concurrent`, the demotions run on
+  // move_stream while `concurrent()` issues other work on st; promotions
+  // (which may reuse HBM the demotions vacate) and index updates follow both.
+  int run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped, cudaStream_t st,
+                const std::function<int()> &concurrent = nullptr);
+  cudaStream_t move_stream = nullptr;
+  cudaEvent_t ev_move_in = nullptr, ev_move_done = nullptr;
+  PinnedBuf h_mscratch;  // descriptors of run_moves (separate from the callers')
+  DevBuf d_mscratch;
   // pg/copies_done: the blocks are still arriving on copy_stream (see
   // put_host); the hash kernel waits per segment and later work on st waits
   // for copies_done.

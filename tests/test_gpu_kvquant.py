@@ -220,3 +220,59 @@ def test_golden_vectors_through_the_store():
     assert found == [LOCAL_DRAM] * len(vec)
     for v, g, d in zip(vec, got, data):
         assert g == v["decompressed_size"] and sha(d) == v["decompressed_sha256"], (v["kind"], v["size"])
+
+
+@pytest.mark.parametrize("compress", [False, True])
+def test_get_promotions_overlapped_with_demotions(compress):
+    """Gets whose DRAM hits are promoted while the demotions that make room
+    run beside the gather: many DRAM hits per batch, repeated keys, outputs
+    too small to copy, and requested HBM blocks chosen as victims. Every
+    copied block must read back as expected: the bytes it was put with,
+    or, each time it comes back from the (INT8) DRAM tier, the oracle's
+    round trip of what it held before."""
+    S = 1 << 20
+    rng = np.random.default_rng(7 if compress else 8)
+    blocks = [gen("kv_fp16", 300 + i, S) for i in range(40)]
+    cfg = cascade_cpp.DistributedConfig()
+    cfg.gpu_capacity_per_device = 8 * S
+    cfg.dram_capacity = 1 << 30
+    cfg.device = 0
+    cfg.kv_compression = compress
+    store = cascade_cpp.DistributedStore(cfg)
+    ids = [store.batch_put([dev(b)])[0] for b in blocks]
+    exp = [b.tobytes() for b in blocks]
+    promoted = 0
+    for it in range(25):
+        pick = [int(x) for x in rng.integers(0, 40, 16)]
+        pick += pick[:3]  # repeats
+        caps = [S if rng.random() > 0.15 else S // 2 for _ in pick]
+        found, got, data = codes_and_bytes(store, [ids[j] for j in pick], caps)
+        read_from_dram = set()
+        for j, f, g, d, c in zip(pick, found, got, data, caps):
+            tier = f & 0x0F
+            assert tier in (LOCAL_HBM, LOCAL_DRAM), (it, j, f)
+            if c < S:
+                assert f & 0x80, (it, j, f)  # found, not copied
+                continue
+            # a DRAM hit reads back the round trip of what the block held;
+            # repeats in one batch read the same DRAM copy
+            want = KQ.roundtrip(exp[j]) if tier == LOCAL_DRAM and compress else exp[j]
+            assert d == want, (it, j, f)
+            if tier == LOCAL_DRAM:
+                read_from_dram.add(j)
+        # a promoted block now holds in HBM what the get returned; one that
+        # could not be promoted (HBM full of this batch's promotions) still
+        # holds its packed copy in DRAM
+        for j in read_from_dram:
+            if store.locate(ids[j]).is_gpu:
+                if compress:
+                    exp[j] = KQ.roundtrip(exp[j])
+                promoted += 1
+    assert promoted > 20
+    st = store.get_stats()
+    assert st.local_gpu_used <= 8 * S and st.total_blocks == 40
+    # everything still reads back as tracked
+    found, got, data = codes_and_bytes(store, ids, [S] * 40)
+    for j, (f, d) in enumerate(zip(found, data)):
+        want = KQ.roundtrip(exp[j]) if (f & 0x0F) == LOCAL_DRAM and compress else exp[j]
+        assert d == want, j
