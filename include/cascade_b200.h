@@ -72,7 +72,9 @@ typedef struct cb_config {
                                    >= 64 B in the INT8 KVCompressor format
                                    (src/cascade_core.cpp:908-967); a read of
                                    such a block returns (size/2)*2 bytes    */
-  int32_t reserved32;
+  int32_t prefix_replication;   /* DHT: cb_sync_metadata copies every prefix
+                                   block into each rank's local HBM
+                                   (broadcast_prefix_data)                   */
   uint64_t reserved[3];
 } cb_config;
 
@@ -98,6 +100,9 @@ typedef struct cb_stats {
   uint64_t tier_ns, tier_bytes, tier_launches;
   /* DHT payload bytes this rank read from / wrote to peers' pools (NVLink) */
   uint64_t peer_bytes_read, peer_bytes_written;
+  /* DHT: prefix blocks of other ranks held in this rank's HBM (replicated by
+   * cb_sync_metadata)                                                       */
+  uint64_t prefix_replicated_blocks;
 } cb_stats;
 
 /* Mirrors BlockLocation (include/cascade_distributed.hpp:62-80). */
@@ -207,6 +212,17 @@ int cb_dht_attach(cb_store *s, int32_t rank, int32_t world, const uint8_t uid[CB
 /* Collective barrier over the DHT (ncclAllReduce of one word).
  * Replaces DistributedStore::barrier (src/distributed_backend.cpp:1310-1314). */
 int cb_dht_barrier(cb_store *s);
+
+/* Cluster-wide prefix registry and prefix replication. Collective in a DHT:
+ * every rank learns every prefix block (cb_stats.prefix_blocks becomes the
+ * cluster count) and, with cb_config.prefix_replication, copies each prefix
+ * block another rank holds in HBM into its own replica region by peer loads
+ * (as space allows; these replicas are never dropped for hot-block
+ * replicas), after which gets of prefix blocks are served from local HBM.
+ * A 1-GPU store has nothing to exchange and returns CB_OK.
+ * Replaces DistributedStore::sync_metadata -> sync_prefix_registry ->
+ * broadcast_prefix_data (src/distributed_backend.cpp:958-1217, :1323-1325). */
+int cb_sync_metadata(cb_store *s);
 
 /* Rank and world size (1-GPU stores: 0 and 1). */
 int cb_rank(const cb_store *s, int32_t *rank, int32_t *world);

@@ -629,6 +629,7 @@ class DistributedStore(_StoreBase):
         c.promotion_threshold = int(cfg.promotion_threshold)
         c.replica_bytes = int(cfg.replica_bytes)
         c.kv_compression = 1 if cfg.kv_compression else 0
+        c.prefix_replication = 1 if cfg.prefix_replication else 0
         self._init_native(c)
         self._rank, self._world = 0, 1
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -675,9 +676,16 @@ class DistributedStore(_StoreBase):
         return DistributedStats(**{f: getattr(st, f) for f in L.STATS_FIELDS})
 
     def sync_metadata(self):
-        """No replication is needed: every block has one owner rank. Kept as a
-        barrier, which is what callers rely on (distributed_backend.cpp:1381)."""
-        self.barrier()
+        """DistributedStore::sync_metadata (distributed_backend.cpp:1323-1382).
+        Block locations need no replication (every block has one owner rank
+        that answers lookups); the prefix registry is merged cluster-wide and,
+        with ``prefix_replication``, every rank copies the other ranks' prefix
+        blocks into its local HBM (sync_prefix_registry /
+        broadcast_prefix_data, :958-1217). Collective; ends with a barrier."""
+        self._n.sync()
+        self._n._check(self._n.lib.cb_sync_metadata(self._n.h))
+        if self._world > 1:
+            self._n._check(self._n.lib.cb_dht_barrier(self._n.h))
 
     def barrier(self):
         self._n.sync()

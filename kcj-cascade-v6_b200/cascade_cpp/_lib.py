@@ -56,7 +56,7 @@ class cb_config(C.Structure):
         ("locality_aware", C.c_int32),
         ("promotion_threshold", C.c_uint32),
         ("kv_compression", C.c_int32),
-        ("reserved32", C.c_int32),
+        ("prefix_replication", C.c_int32),
         ("reserved", C.c_uint64 * 3),
     ]
 
@@ -70,7 +70,7 @@ STATS_FIELDS = [
     "evicted_bytes", "promoted_bytes", "dropped_blocks", "kernel_launches",
     "sha_ns", "sha_bytes", "sha_launches", "scatter_ns", "scatter_bytes", "scatter_launches",
     "gather_ns", "gather_bytes", "gather_launches", "tier_ns", "tier_bytes", "tier_launches",
-    "peer_bytes_read", "peer_bytes_written",
+    "peer_bytes_read", "peer_bytes_written", "prefix_replicated_blocks",
 ]
 
 
@@ -112,6 +112,7 @@ SIGNATURES = [
     ("cb_dht_unique_id", C.c_int, [_P]),
     ("cb_dht_attach", C.c_int, [_P, C.c_int32, C.c_int32, _P]),
     ("cb_dht_barrier", C.c_int, [_P]),
+    ("cb_sync_metadata", C.c_int, [_P]),
     ("cb_rank", C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     ("cb_hash_batch_noalloc", C.c_int, [C.c_int32, _P, _P, C.c_int32, _P, _P]),
     ("cb_owner_rank", C.c_int32, [_P, C.c_int32]),

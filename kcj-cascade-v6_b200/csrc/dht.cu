@@ -27,6 +27,7 @@
 #include <algorithm>
 #include <chrono>
 #include <thread>
+#include <unordered_set>
 #include <vector>
 
 #include "kernels.cuh"
@@ -79,10 +80,33 @@ struct DhtState {
   ExtentAllocator ralloc;
   struct Rep {
     uint64_t off, size;
-    std::list<HKey>::iterator lru;
+    std::list<HKey>::iterator lru;  // in rlru unless pinned
+    bool pinned;                    // a prefix replica: never dropped for another replica
   };
   std::unordered_map<HKey, Rep, HKeyHash> rmap;
-  std::list<HKey> rlru;  // front = most recent
+  std::list<HKey> rlru;  // hot-block replicas, front = most recent
+
+  // Prefix registry (DistributedStore::prefix_registry_,
+  // include/cascade_distributed.hpp:432): the prefix blocks this rank has
+  // stored, and after sync_metadata every prefix block of the cluster.
+  std::unordered_set<HKey, HKeyHash> registry;
+  bool replicate_prefixes = false;  // DistributedConfig::prefix_replication
+  uint64_t prefix_replicas = 0;
+
+  // Frees hot-block replicas, least recently used first, until `size` bytes
+  // fit; returns the offset or UINT64_MAX.
+  uint64_t alloc_replica(uint64_t size) {
+    uint64_t off = ralloc.alloc(size);
+    while (off == UINT64_MAX && !rlru.empty()) {
+      const HKey v = rlru.back();
+      auto it = rmap.find(v);
+      ralloc.free(it->second.off, it->second.size);
+      rlru.pop_back();
+      rmap.erase(it);
+      off = ralloc.alloc(size);
+    }
+    return off;
+  }
   struct Access {
     uint32_t total = 0, local = 0, remote = 0, wtotal = 0, wremote = 0;
     float ema = 0.f;
@@ -114,6 +138,8 @@ struct DhtState {
     rmap.clear();
     rlru.clear();
     access.clear();
+    registry.clear();
+    prefix_replicas = 0;
     ralloc.reset(rbytes, 256);
   }
 };
@@ -295,14 +321,16 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   rank = r;
   world = W;
   policy.set_direct_dram_placement(false);
-  if (cfg.locality_aware) {
+  if (cfg.locality_aware || cfg.prefix_replication) {
+    // one replica region serves hot-block replicas and prefix replicas
     uint64_t rb = cfg.replica_bytes ? cfg.replica_bytes : std::min<uint64_t>(pool_bytes / 32, 4ull << 30);
     rb = rb / 256 * 256;
     if (rb) {
       CB_TRY_CUDA(cudaMalloc(&dht->rbase, rb), "replica region");
       dht->rbytes = rb;
       dht->ralloc.reset(rb, 256);
-      dht->locality = true;
+      dht->locality = cfg.locality_aware != 0;
+      dht->replicate_prefixes = cfg.prefix_replication != 0;
       dht->threshold = cfg.promotion_threshold ? cfg.promotion_threshold : 3;
     }
   }
@@ -505,9 +533,147 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   for (int i = 0; i < n; ++i) {
     if (keys_out) memcpy(keys_out + 16 * i, &keys[i], 16);
     if (status_out) status_out[i] = status[i];
+    // DistributedStore::put registers a prefix block it has stored
+    // (src/distributed_backend.cpp:680-683)
+    if (status[i] == CB_PUT_STORED && is_prefix && is_prefix[i]) dht->registry.insert(keys[i]);
   }
   return CB_OK;
 }
+
+// ------------------------------------------------------------ prefix sync
+
+namespace {
+struct PrefixRec {
+  uint64_t klo, khi;
+  uint64_t loc;   // byte offset of the block in the owner's arena | kLocDram
+  uint64_t size;
+};
+}  // namespace
+
+// sync_prefix_registry + broadcast_prefix_data (src/distributed_backend.cpp:
+// 958-1217). The reference all-gathers every rank's prefix IDs (Allgatherv)
+// and then has each owner MPI_Bcast its prefix blocks, which every other rank
+// stores in its GPU tier. Here every prefix block has one owner that knows
+// its location, so: each owner all-gathers one 32-byte record {key,
+// location, size} per prefix block it holds (ncclAllGather, padded to the
+// largest count); every rank merges the keys into its registry and, with
+// prefix_replication, copies the blocks it does not own, and that sit in
+// their owner's HBM pool, straight from the owners' pools into its replica
+// region with one batched peer-load copy (no staging, no broadcast of
+// payload through NCCL). A block in an owner's pinned DRAM tier is
+// registered but not copied (peers cannot map that memory). Prefix replicas
+// are pinned: hot-block replicas never displace them; they may displace hot
+// replicas. A closing all-reduce keeps owners from reusing pool extents
+// before every reader is done.
+int Store::dht_sync_prefixes(cudaStream_t st) {
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  const int W = dht->W, me = dht->me;
+  std::vector<PrefixRec> mine;
+  policy.for_each([&](const HKey &k, const BlockMeta &m) {
+    if (m.prefix)
+      mine.push_back(PrefixRec{k.lo, k.hi, Policy::data_offset(m) | (m.tier == kTierDram ? kLocDram : 0), m.size});
+  });
+  // 1. counts (every rank takes every collective step below in the same order)
+  CB_TRY_CUDA(dht->h_misc.ensure(4ull * (W + 1)), "pinned");
+  CB_TRY_CUDA(dht->d_misc.ensure(4ull * (W + 1)), "device");
+  uint32_t *hc = static_cast<uint32_t *>(dht->h_misc.ptr);
+  uint32_t *dc = static_cast<uint32_t *>(dht->d_misc.ptr);
+  hc[0] = (uint32_t)mine.size();
+  CB_TRY_CUDA(cudaMemcpyAsync(dc, hc, 4, cudaMemcpyHostToDevice, st), "H2D count");
+  int rc = dht_nccl(ncclAllGather(dc, dc + 1, 1, ncclUint32, dht->comm, st), "ncclAllGather(prefix counts)");
+  if (rc) return rc;
+  CB_TRY_CUDA(cudaMemcpyAsync(hc + 1, dc + 1, 4ull * W, cudaMemcpyDeviceToHost, st), "D2H counts");
+  rc = dht_sync(st);
+  if (rc) return rc;
+  std::vector<uint32_t> counts(hc + 1, hc + 1 + W);
+  const uint32_t max_n = *std::max_element(counts.begin(), counts.end());
+  for (const PrefixRec &r : mine) dht->registry.insert(HKey{r.klo, r.khi});
+  std::vector<CopyDesc> desc;
+  std::vector<uint32_t> us;
+  uint32_t total = 0;
+  uint64_t bytes = 0;
+  if (max_n) {
+    // 2. records, padded to max_n per rank
+    const size_t rb = sizeof(PrefixRec) * max_n;
+    CB_TRY_CUDA(dht->h_send.ensure(rb), "pinned");
+    CB_TRY_CUDA(dht->d_send.ensure(rb), "device");
+    CB_TRY_CUDA(dht->h_recv.ensure(rb * W), "pinned");
+    CB_TRY_CUDA(dht->d_recv.ensure(rb * W), "device");
+    memset(dht->h_send.ptr, 0, rb);
+    if (!mine.empty()) memcpy(dht->h_send.ptr, mine.data(), sizeof(PrefixRec) * mine.size());
+    CB_TRY_CUDA(cudaMemcpyAsync(dht->d_send.ptr, dht->h_send.ptr, rb, cudaMemcpyHostToDevice, st), "H2D prefixes");
+    rc = dht_nccl(ncclAllGather(dht->d_send.ptr, dht->d_recv.ptr, rb, ncclUint8, dht->comm, st),
+                  "ncclAllGather(prefixes)");
+    if (rc) return rc;
+    CB_TRY_CUDA(cudaMemcpyAsync(dht->h_recv.ptr, dht->d_recv.ptr, rb * W, cudaMemcpyDeviceToHost, st),
+                "D2H prefixes");
+    rc = dht_sync(st);
+    if (rc) return rc;
+    // 3. merge, and plan the copies of other owners' prefix blocks
+    const PrefixRec *all = static_cast<const PrefixRec *>(dht->h_recv.ptr);
+    for (int r = 0; r < W; ++r) {
+      if (r == me) continue;
+      for (uint32_t j = 0; j < counts[r]; ++j) {
+        const PrefixRec &rec = all[(size_t)r * max_n + j];
+        const HKey k{rec.klo, rec.khi};
+        dht->registry.insert(k);
+        if (!dht->replicate_prefixes || !dht->rbase || !rec.size || (rec.loc & kLocDram)) continue;
+        const uint64_t off = rec.loc & kLocOffMask;
+        if (off > dht->pool_bytes[r] || rec.size > dht->pool_bytes[r] - off) continue;  // not a pool extent
+        auto it = dht->rmap.find(k);
+        if (it != dht->rmap.end()) {  // already a hot replica: keep it, pinned from now on
+          if (!it->second.pinned) {
+            dht->rlru.erase(it->second.lru);
+            it->second.pinned = true;
+            dht->prefix_replicas++;
+          }
+          continue;
+        }
+        const uint64_t roff = dht->alloc_replica(rec.size);
+        if (roff == UINT64_MAX) continue;  // the replica region is full of prefix replicas
+        dht->rmap.emplace(k, DhtState::Rep{roff, rec.size, {}, true});
+        us.push_back(total);
+        desc.push_back(CopyDesc{dht->pool[r] + off, (uint64_t)dht->rbase + roff, rec.size, kCopyHost});
+        total += (uint32_t)((rec.size + kCopyUnit - 1) / kCopyUnit);
+        bytes += rec.size;
+        dht->prefix_replicas++;
+      }
+    }
+  }
+  // 4. one batched copy from the owners' pools (peer loads over NVLink)
+  if (!desc.empty()) {
+    us.push_back(total);
+    const size_t o_us = align_up(sizeof(CopyDesc) * desc.size(), 256);
+    const size_t need = o_us + 4 * us.size();
+    CB_TRY_CUDA(h_scratch.ensure(need), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(need), "device");
+    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    memcpy(h, desc.data(), sizeof(CopyDesc) * desc.size());
+    memcpy(h + o_us, us.data(), 4 * us.size());
+    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, need, cudaMemcpyHostToDevice, st), "H2D prefix copies");
+    const int nd = (int)desc.size();
+    CB_TRY_CUDA(timed(2, bytes, st,
+                      [&] {
+                        return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d),
+                                                 reinterpret_cast<const uint32_t *>(d + o_us), nd, total, 2, d_err,
+                                                 num_sms, st);
+                      }),
+                "prefix copies");
+    peer_bytes_read += bytes;
+  }
+  // 5. owners keep their extents until every reader is done
+  CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
+  rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
+                "ncclAllReduce(prefix sync barrier)");
+  if (rc) return rc;
+  rc = dht_sync(st);
+  if (rc) return rc;
+  return check_device_error(st);
+}
+
+uint64_t Store::dht_registry_size() const { return dht ? dht->registry.size() : 0; }
+uint64_t Store::dht_prefix_replicas() const { return dht ? dht->prefix_replicas : 0; }
 
 // ------------------------------------------------------------ lookup
 
@@ -581,11 +747,11 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
     first.reserve(2ull * n);
     for (int i = 0; i < n; ++i) {
       const HKey k = to_hkey(keys + 16 * i);
-      if (dht->locality) {
+      if (dht->rbase) {
         auto r = dht->rmap.find(k);
         if (r != dht->rmap.end()) {
           rep_off[i] = (int64_t)r->second.off;
-          dht->rlru.splice(dht->rlru.begin(), dht->rlru, r->second.lru);
+          if (!r->second.pinned) dht->rlru.splice(dht->rlru.begin(), dht->rlru, r->second.lru);
           continue;
         }
       }
@@ -703,18 +869,10 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
       const HKey k = to_hkey(ukeys.data() + 16 * u);
       if (dht->rmap.count(k) || !dht->should_promote(k)) continue;
       const uint64_t sz = sizes_out[l];
-      uint64_t off = dht->ralloc.alloc(sz);
-      while (off == UINT64_MAX && !dht->rlru.empty()) {  // drop least recently used replicas
-        const HKey v = dht->rlru.back();
-        auto it = dht->rmap.find(v);
-        dht->ralloc.free(it->second.off, it->second.size);
-        dht->rlru.pop_back();
-        dht->rmap.erase(it);
-        off = dht->ralloc.alloc(sz);
-      }
+      const uint64_t off = dht->alloc_replica(sz);  // drops least recently used hot replicas
       if (off == UINT64_MAX) continue;
       dht->rlru.push_front(k);
-      dht->rmap.emplace(k, DhtState::Rep{off, sz, dht->rlru.begin()});
+      dht->rmap.emplace(k, DhtState::Rep{off, sz, dht->rlru.begin(), false});
       add2(dst[l], (uint64_t)dht->rbase + off, sz);
       replica_promotions++;
     }

@@ -977,7 +977,10 @@ void Store::fill_stats(cb_stats *o) const {
   o->promotions_to_local = c.promotions + replica_promotions;
   o->compression_savings = c.compression_savings;
   o->total_blocks = policy.size();
-  o->prefix_blocks = c.prefix_blocks;
+  // the prefix registry (DistributedStore::Stats, distributed_backend.cpp:
+  // 1405): prefix blocks this rank stored; after sync_metadata, the cluster's
+  o->prefix_blocks = dht ? dht_registry_size() : c.prefix_blocks;
+  o->prefix_replicated_blocks = dht_prefix_replicas();
   o->evicted_bytes = c.evicted_bytes;
   o->promoted_bytes = c.promoted_bytes;
   o->dropped_blocks = c.dropped_blocks;
@@ -1241,6 +1244,13 @@ int cb_dht_attach(cb_store *h, int32_t rank, int32_t world, const uint8_t *uid) 
   return guarded(h, [&](Store *s) -> int {
     if (!uid) return s->fail(CB_ERR_ARG, "bad arguments");
     return s->dht_attach(rank, world, uid);
+  });
+}
+
+int cb_sync_metadata(cb_store *h) {
+  return guarded(h, [&](Store *s) -> int {
+    if (!s->dht) return CB_OK;  // one GPU: the registry is already complete
+    return s->dht_sync_prefixes(s->own_stream);
   });
 }
 

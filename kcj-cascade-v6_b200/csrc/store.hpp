@@ -180,6 +180,9 @@ struct Store {
               uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
   int dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st);
   int dht_cluster_usage(cb_stats *o);
+  int dht_sync_prefixes(cudaStream_t st);
+  uint64_t dht_registry_size() const;
+  uint64_t dht_prefix_replicas() const;
 };
 
 inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }

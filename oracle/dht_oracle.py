@@ -8,6 +8,10 @@ of DistributedStore::put (cascade_Code/cpp/src/distributed_backend.cpp:
 604-608), so among byte-identical blocks put in the same round the lowest
 (rank, index) is stored and every other copy is a dedup hit; a get returns
 the bytes stored by the owner.
+
+Prefix registry (DistributedStore::prefix_registry_, distributed_backend.cpp:
+680-683, 958-1024): a rank registers each prefix block it stores (not a dedup
+hit); sync_metadata makes every rank's registry the union.
 """
 from __future__ import annotations
 
@@ -23,6 +27,7 @@ class DhtOracle:
         self.world = world
         self.shards = [SequentialStore() for _ in range(world)]
         self.dedup_hits = [0] * world  # counted on the putting rank
+        self.registry = [set() for _ in range(world)]
 
     def put_round(self, items: list[list[tuple[str, bytes, bool]]]) -> list[list[int]]:
         """items[r] = rank r's batch [(id, bytes, is_prefix)]; returns per-rank
@@ -37,7 +42,15 @@ class DhtOracle:
                     _, st = self.shards[o].put(bid, data, pf)
                     status[r][i] = st
                     self.dedup_hits[r] += st
+                    if st == 0 and pf:
+                        self.registry[r].add(bid)
         return status
+
+    def sync_prefixes(self) -> set:
+        """sync_prefix_registry: every rank's registry becomes the union."""
+        u = set().union(*self.registry)
+        self.registry = [set(u) for _ in range(self.world)]
+        return u
 
     def get(self, block_id: str):
         return self.shards[owner(block_id, self.world)].get(block_id)

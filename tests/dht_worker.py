@@ -90,6 +90,28 @@ def main():
     assert first_local >= 8, codes  # the EMA needs two full windows of remote accesses
     assert np.array_equal(hout.cpu().numpy(), by_id[hot]), "replica bytes"
     assert store.get_stats().promotions_to_local == p0 + 1
+
+    # prefix registry + replication (sync_metadata): a rank's registry holds
+    # the prefix blocks it stored; after the sync it holds the cluster's, and
+    # every prefix block owned by another rank has a local copy, so gets of
+    # it are served from local HBM without NVLink traffic
+    stored_pf = {ids_all[rank][i] for i, (s, pf) in enumerate(items[rank]) if pf and want_status[rank][i] == 0}
+    assert store.get_stats().prefix_blocks == len(stored_pf)
+    pref = {ids_all[r][i]: s for r in range(world) for i, (s, pf) in enumerate(items[r]) if pf}
+    store.sync_metadata()
+    st = store.get_stats()
+    assert st.prefix_blocks == len(pref), (st.prefix_blocks, len(pref))
+    remote_pref = sorted(b for b, s in pref.items() if owner(b, world) != rank and len(pool[s]) > 0)
+    assert st.prefix_replicated_blocks == len(remote_pref), (st.prefix_replicated_blocks, len(remote_pref))
+    pk = np.frombuffer(b"".join(bytes.fromhex(b) for b in remote_pref), np.uint8).reshape(-1, 16)
+    pouts = [torch.empty(len(pool[pref[b]]), dtype=torch.uint8, device=dev) for b in remote_pref]
+    pr0 = store.get_stats().peer_bytes_read
+    s_, codes = store.get_ptrs(pk, np.array([o.data_ptr() for o in pouts], np.uint64),
+                               np.array([o.numel() for o in pouts], np.uint64), True)
+    assert all(int(c) == 1 for c in codes), codes  # CB_FOUND_LOCAL_HBM: the replica
+    assert store.get_stats().peer_bytes_read == pr0
+    for b, o in zip(remote_pref, pouts):
+        assert np.array_equal(o.cpu().numpy(), pool[pref[b]]), ("prefix replica bytes", b)
     # host-memory outputs too
     houts = [np.empty(len(by_id[b]), np.uint8) for b in req[:20]]
     found, sizes = store.batch_get(req[:20], houts)

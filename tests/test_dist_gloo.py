@@ -105,3 +105,61 @@ def test_dht_protocol_two_gloo_ranks():
         assert out[r] == want[r], r
     # cross-rank duplicates exist and the lowest (rank, index) copy is stored
     assert sum(map(sum, want)) > 0
+
+
+def _prefix_worker(rank, world, port, out):
+    """sync_metadata's prefix exchange (csrc/dht.cu dht_sync_prefixes): each
+    owner all-gathers one record per prefix block it holds, padded to the
+    largest count; every rank merges the keys into its registry and plans a
+    local copy of each prefix block another rank owns (non-empty)."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from oracle import store_oracle as O
+    from oracle.dht_oracle import DhtOracle, owner
+
+    pool, items = _batches(world)
+    ora = DhtOracle(world)
+    ora.put_round([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
+    # what this rank's policy holds: the prefix blocks it owns
+    held = sorted({b for r in range(world) for b in ora.registry[r] if owner(b, world) == rank})
+    count = torch.tensor([len(held)], dtype=torch.int64)
+    counts = [torch.zeros(1, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(counts, count)
+    max_n = max(int(c) for c in counts)
+    rec = torch.zeros((max_n, 17), dtype=torch.int64)  # 16 key bytes + size
+    for j, b in enumerate(held):
+        rec[j, :16] = torch.tensor(list(bytes.fromhex(b)))
+        rec[j, 16] = len(next(pool[s] for s, _ in items[0] + items[1] if O.block_id(pool[s]) == b))
+    recs = [torch.zeros_like(rec) for _ in range(world)]
+    dist.all_gather(recs, rec)
+    registry = set(ora.registry[rank])
+    plan = []
+    for r in range(world):
+        for j in range(int(counts[r])):
+            row = recs[r][j].tolist()
+            b = bytes(row[:16]).hex()
+            registry.add(b)
+            if r != rank and row[16] > 0:
+                plan.append(b)
+    out[rank] = (sorted(registry), sorted(plan))
+    dist.destroy_process_group()
+
+
+def test_prefix_registry_sync_two_gloo_ranks():
+    world = 2
+    port = _free_port()
+    mgr = mp.get_context("spawn").Manager()
+    out = mgr.dict()
+    mp.start_processes(_prefix_worker, args=(world, port, out), nprocs=world, start_method="spawn", join=True)
+    from oracle import store_oracle as O
+    from oracle.dht_oracle import DhtOracle, owner
+    pool, items = _batches(world)
+    ora = DhtOracle(world)
+    ora.put_round([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
+    union = ora.sync_prefixes()
+    assert union and all(ora.registry[r] == union for r in range(world))
+    for r in range(world):
+        reg, plan = out[r]
+        assert set(reg) == union
+        assert set(plan) == {b for b in union if owner(b, world) != r}
