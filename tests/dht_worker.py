@@ -95,23 +95,24 @@ def main():
     # the prefix blocks it stored; after the sync it holds the cluster's, and
     # every prefix block owned by another rank has a local copy, so gets of
     # it are served from local HBM without NVLink traffic
-    stored_pf = {ids_all[rank][i] for i, (s, pf) in enumerate(items[rank]) if pf and want_status[rank][i] == 0}
-    assert store.get_stats().prefix_blocks == len(stored_pf)
-    pref = {ids_all[r][i]: s for r in range(world) for i, (s, pf) in enumerate(items[r]) if pf}
+    # (a prefix-flagged copy that is a dedup hit registers nothing: the empty
+    # block is stored first from a non-prefix copy here)
+    assert store.get_stats().prefix_blocks == len(ora.registry[rank])
+    union = ora.sync_prefixes()
     store.sync_metadata()
     st = store.get_stats()
-    assert st.prefix_blocks == len(pref), (st.prefix_blocks, len(pref))
-    remote_pref = sorted(b for b, s in pref.items() if owner(b, world) != rank and len(pool[s]) > 0)
+    assert st.prefix_blocks == len(union), (st.prefix_blocks, len(union))
+    remote_pref = sorted(b for b in union if owner(b, world) != rank and len(by_id[b]) > 0)
     assert st.prefix_replicated_blocks == len(remote_pref), (st.prefix_replicated_blocks, len(remote_pref))
     pk = np.frombuffer(b"".join(bytes.fromhex(b) for b in remote_pref), np.uint8).reshape(-1, 16)
-    pouts = [torch.empty(len(pool[pref[b]]), dtype=torch.uint8, device=dev) for b in remote_pref]
+    pouts = [torch.empty(len(by_id[b]), dtype=torch.uint8, device=dev) for b in remote_pref]
     pr0 = store.get_stats().peer_bytes_read
     s_, codes = store.get_ptrs(pk, np.array([o.data_ptr() for o in pouts], np.uint64),
                                np.array([o.numel() for o in pouts], np.uint64), True)
     assert all(int(c) == 1 for c in codes), codes  # CB_FOUND_LOCAL_HBM: the replica
     assert store.get_stats().peer_bytes_read == pr0
     for b, o in zip(remote_pref, pouts):
-        assert np.array_equal(o.cpu().numpy(), pool[pref[b]]), ("prefix replica bytes", b)
+        assert np.array_equal(o.cpu().numpy(), by_id[b]), ("prefix replica bytes", b)
     # host-memory outputs too
     houts = [np.empty(len(by_id[b]), np.uint8) for b in req[:20]]
     found, sizes = store.batch_get(req[:20], houts)
