@@ -129,6 +129,23 @@ int cb_destroy(cb_store *s);
  * NULL). Replaces the CUDA_CHECK fprintf of src/gpu_backend.cu:43-51. */
 const char *cb_last_error(const cb_store *s);
 
+/* Zero-copy get: addrs_out[i] = device address of block i inside this
+ * store's HBM pool, sizes_out[i] its size, found_out[i] a CB_FOUND_* code.
+ * No copy and, for HBM hits, no kernel: the addresses come from the host
+ * metadata. A DRAM-tier block is first promoted to HBM when promote_on_hit
+ * is set (otherwise, or without HBM room, it is reported
+ * CB_FOUND_LOCAL_DRAM | CB_FOUND_NOT_COPIED with address 0). Each returned
+ * address stays valid — the block is neither evicted nor moved — until
+ * cb_release_views is called for that key (one release per view). Views are
+ * read-only by contract (a block is its content hash). Not available on a
+ * DHT member. The caller-side step after DistributedStore::get_batch
+ * (src/distributed_backend.cpp:844-870), without its copy. */
+int cb_get_views(cb_store *s, const uint8_t *keys, int32_t n, uint64_t *addrs_out, uint64_t *sizes_out,
+                 uint8_t *found_out, void *stream);
+
+/* Releases one view of each key (CB_ERR_ARG if a key has none). */
+int cb_release_views(cb_store *s, const uint8_t *keys, int32_t n);
+
 /* Batched INT8 KV compression of n device blocks (srcs[i], sizes[i] >= 2
  * bytes) into dsts[i] (device memory, 8 + sizes[i]/2 bytes each) in the
  * format [f32 scale][i8 zero_point][3 zero bytes][sizes[i]/2 x i8] — the

@@ -464,6 +464,15 @@ class BlockLocation(_Record):
 
 # -------------------------------------------------------------------- store
 
+class _PoolSpan:
+    """A span of the HBM pool exposed through __cuda_array_interface__ so
+    that torch can alias it without a copy."""
+
+    def __init__(self, addr: int, size: int):
+        self.__cuda_array_interface__ = {"shape": (int(size),), "typestr": "|u1", "data": (int(addr), False),
+                                         "version": 3, "strides": None}
+
+
 class _StoreBase:
     _miss_size_is_buffer_len = True
 
@@ -559,6 +568,37 @@ class _StoreBase:
         kind = L.CB_MEM_DEVICE if device_memory else L.CB_MEM_HOST
         return self._n.put(np.ascontiguousarray(ptrs, np.uint64), np.ascontiguousarray(sizes, np.uint64),
                            kind, keys_in=keys, prefix=prefix)
+
+    def get_views(self, ids: Sequence[str]):
+        """Zero-copy batch_get: one CUDA uint8 tensor per ID that aliases the
+        block where it sits in this store's HBM pool (no copy; for HBM hits no
+        kernel either), or None for a miss (and for a DRAM-tier block that
+        could not be promoted). Each view pins its block (never evicted or
+        moved) until ``release_views`` is called for that ID. Views are
+        read-only by contract: a block is its content hash."""
+        keys = self._keys(ids)
+        n = len(keys)
+        addrs = np.zeros(n, np.uint64)
+        sizes = np.zeros(n, np.uint64)
+        found = np.zeros(n, np.uint8)
+        if n:
+            self._n._check(self._n.lib.cb_get_views(self._n.h, _ptr(keys), n, _ptr(addrs), _ptr(sizes), _ptr(found),
+                                                    self._n.stream_ptr(L.CB_MEM_DEVICE)))
+        out = []
+        for a, s, f in zip(addrs.tolist(), sizes.tolist(), found.tolist()):
+            if (f & 0x0F) != L.CB_FOUND_LOCAL_HBM:
+                out.append(None)
+            elif s == 0:
+                out.append(torch.empty(0, dtype=torch.uint8, device=f"cuda:{self._device}"))
+            else:
+                out.append(torch.as_tensor(_PoolSpan(a, s), device=f"cuda:{self._device}"))
+        return out
+
+    def release_views(self, ids: Sequence[str]):
+        """Drops one view pin of each ID (views obtained by ``get_views``)."""
+        keys = self._keys(ids)
+        if len(keys):
+            self._n._check(self._n.lib.cb_release_views(self._n.h, _ptr(keys), len(keys)))
 
     def get_ptrs(self, keys: np.ndarray, outs: np.ndarray, caps: np.ndarray, device_memory: bool):
         kind = L.CB_MEM_DEVICE if device_memory else L.CB_MEM_HOST

@@ -98,6 +98,8 @@ SIGNATURES = [
     ("cb_create", C.c_int, [C.POINTER(cb_config), C.POINTER(_P)]),
     ("cb_destroy", C.c_int, [_P]),
     ("cb_last_error", C.c_char_p, [_P]),
+    ("cb_get_views", C.c_int, [_P, _P, C.c_int32, _P, _P, _P, _P]),
+    ("cb_release_views", C.c_int, [_P, _P, C.c_int32]),
     ("cb_kv_compress_batch", C.c_int, [_P, _P, _P, _P, C.c_int32, _P]),
     ("cb_kv_decompress_batch", C.c_int, [_P, _P, _P, _P, _P, C.c_int32, _P, _P]),
     ("cb_hash_batch", C.c_int, [_P, _P, _P, C.c_int32, C.c_int32, _P, _P]),

@@ -87,6 +87,20 @@ void Policy::touch(const HKey &k) {
   m.stamp = ++clock_;
 }
 
+bool Policy::pin(const HKey &k) {
+  auto it = map_.find(k);
+  if (it == map_.end()) return false;
+  if (it->second.pins++ == 0) pinned_++;
+  return true;
+}
+
+bool Policy::unpin(const HKey &k) {
+  auto it = map_.find(k);
+  if (it == map_.end() || it->second.pins == 0) return false;
+  if (--it->second.pins == 0) pinned_--;
+  return true;
+}
+
 void Policy::protect(const HKey &k) {
   auto it = map_.find(k);
   if (it == map_.end() || it->second.pending) return;
@@ -101,6 +115,7 @@ void Policy::clear() {
   pending_.clear();
   deferred_free_.clear();
   clock_ = 0;
+  pinned_ = 0;
   hbm_.reset(hbm_cap_, 256);
   dram_.reset(dram_cap_, 256);
   hbm_used_ = dram_used_ = 0;
@@ -116,7 +131,8 @@ bool Policy::pick_victim(uint8_t tier, bool prefix_fallback, HKey &out) const {
   for (int p = 0; p < 2; ++p) {
     const std::list<HKey> &lst = lru_[tier][p];
     for (auto it = lst.rbegin(); it != lst.rend(); ++it) {
-      if (!map_.at(*it).pending) {
+      const BlockMeta &m = map_.at(*it);
+      if (!m.pending && !m.pins) {
         cand[p] = &*it;
         break;
       }

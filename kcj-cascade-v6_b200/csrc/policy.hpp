@@ -95,6 +95,7 @@ struct BlockMeta {
   uint8_t prefix = 0;
   uint8_t pending = 0;  // placed by the batch being planned; not evictable yet
   uint8_t packed = 0;   // DRAM copy in the INT8 format (size is then even)
+  uint32_t pins = 0;    // outstanding zero-copy views: never a victim, never moved
   uint64_t stamp = 0;   // recency (larger = more recent)
   std::list<HKey>::iterator lru;
 };
@@ -170,6 +171,11 @@ class Policy {
   // Keep a block out of every victim choice until commit() (a get is still
   // reading it while this plan's moves run).
   void protect(const HKey &k);
+  // Zero-copy views: a pinned block is never chosen as a victim (so it is
+  // neither moved nor dropped) until every pin is released.
+  bool pin(const HKey &k);
+  bool unpin(const HKey &k);
+  uint64_t pinned_blocks() const { return pinned_; }
   void clear();
 
   uint64_t hbm_used() const { return hbm_used_; }
@@ -217,6 +223,7 @@ class Policy {
   std::vector<HKey> pending_;
   std::vector<std::pair<uint64_t, uint64_t>> deferred_free_;  // DRAM extents freed at commit
   uint64_t clock_ = 0;
+  uint64_t pinned_ = 0;  // blocks with pins > 0
   PolicyCounters ctr_;
 };
 

@@ -848,6 +848,62 @@ int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_
 
 // ---------------------------------------------------------------- misc
 
+// Zero-copy get: the caller reads the blocks where they sit in the HBM pool
+// (a torch view, an attention kernel reading KV pages in place) instead of
+// receiving copies — the caller-side step after batch_get
+// (DistributedStore::get_batch, src/distributed_backend.cpp:844-870) without
+// its copy. HBM hits are resolved from the host metadata alone: no kernel, no
+// device round trip. DRAM-tier hits are promoted first (with promote_on_hit;
+// packed blocks are unpacked by the promotion) and then viewed. Each viewed
+// block is pinned — never a victim, so neither moved nor dropped — until
+// release_views drops the pin (one release per view).
+int Store::get_views(const uint8_t *keys, int n, uint64_t *addrs_out, uint64_t *sizes_out, uint8_t *found_out,
+                     cudaStream_t st) {
+  std::vector<TierMove> moves;
+  std::vector<HKey> dropped;
+  bool planned = false;
+  for (int i = 0; i < n; ++i) {
+    const HKey k = to_hkey(keys + 16 * i);
+    policy.touch(k);
+    const BlockMeta *m = policy.find(k);
+    if (m && m->tier == kTierDram && cfg.promote_on_hit) {
+      policy.plan_promote(k, moves, dropped);
+      planned = true;
+    }
+  }
+  int rc = run_moves(moves, dropped, st);
+  if (planned) policy.commit();
+  if (rc) return rc;
+  rc = check_device_error(st);
+  if (rc) return rc;
+  for (int i = 0; i < n; ++i) {
+    const HKey k = to_hkey(keys + 16 * i);
+    const BlockMeta *m = policy.find(k);
+    addrs_out[i] = 0;
+    sizes_out[i] = m ? m->size : 0;
+    if (!m) {
+      found_out[i] = CB_FOUND_MISS;
+      misses++;
+    } else if (m->tier == kTierDram) {  // promotion off, or no HBM room
+      found_out[i] = CB_FOUND_LOCAL_DRAM | CB_FOUND_NOT_COPIED;
+      local_dram_hits++;
+    } else {
+      found_out[i] = CB_FOUND_LOCAL_HBM;
+      addrs_out[i] = (uint64_t)pool + m->off;
+      policy.pin(k);
+      local_gpu_hits++;
+    }
+  }
+  return CB_OK;
+}
+
+int Store::release_views(const uint8_t *keys, int n) {
+  int bad = 0;
+  for (int i = 0; i < n; ++i) bad += policy.unpin(to_hkey(keys + 16 * i)) ? 0 : 1;
+  if (bad) return fail(CB_ERR_ARG, "%d key(s) had no outstanding view", bad);
+  return CB_OK;
+}
+
 // KVCompressor::compress (src/cascade_core.cpp:908-944) of n device blocks:
 // the pack kernels of the DRAM tier on caller buffers.
 int Store::kv_compress(const uint64_t *srcs, const uint64_t *sizes, const uint64_t *dsts, int n, cudaStream_t st) {
@@ -937,6 +993,9 @@ int Store::evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st) {
 }
 
 int Store::clear(cudaStream_t st) {
+  if (policy.pinned_blocks())  // a view would point at memory the store hands out again
+    return fail(CB_ERR_STATE, "%llu block(s) have outstanding zero-copy views",
+                (unsigned long long)policy.pinned_blocks());
   CB_TRY(cudaStreamSynchronize(st), "sync");
   if (dht) {  // collective, like DistributedStore::clear (barrier before and after)
     int rc = dht_barrier();
@@ -1080,6 +1139,23 @@ int cb_destroy(cb_store *h) {
 const char *cb_last_error(const cb_store *h) {
   if (!h || !h->s) return cb::g_create_error.c_str();
   return h->s->last_error.c_str();
+}
+
+int cb_get_views(cb_store *h, const uint8_t *keys, int32_t n, uint64_t *addrs_out, uint64_t *sizes_out,
+                 uint8_t *found_out, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!keys || !addrs_out || !sizes_out || !found_out))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (s->dht) return s->fail(CB_ERR_STATE, "zero-copy views are local to one store (not on a DHT member)");
+    if (n == 0) return CB_OK;
+    return s->get_views(keys, n, addrs_out, sizes_out, found_out, pick_stream(s, stream));
+  });
+}
+
+int cb_release_views(cb_store *h, const uint8_t *keys, int32_t n) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && !keys)) return s->fail(CB_ERR_ARG, "bad arguments");
+    return s->release_views(keys, n);
+  });
 }
 
 int cb_kv_compress_batch(cb_store *h, const void *const *srcs, const uint64_t *sizes, void *const *dsts,

@@ -152,6 +152,10 @@ struct Store {
   int get_host(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps,
                uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
   int evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st);
+  // Zero-copy gets: pool addresses of HBM blocks, pinned until released.
+  int get_views(const uint8_t *keys, int n, uint64_t *addrs_out, uint64_t *sizes_out, uint8_t *found_out,
+                cudaStream_t st);
+  int release_views(const uint8_t *keys, int n);
   // INT8 KV packing of device blocks outside the store (KVCompressor).
   int kv_compress(const uint64_t *srcs, const uint64_t *sizes, const uint64_t *dsts, int n, cudaStream_t st);
   int kv_decompress(const uint64_t *srcs, const uint64_t *comp_sizes, const uint64_t *orig_sizes,

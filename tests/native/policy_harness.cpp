@@ -14,6 +14,8 @@ extern "C" {
 void *ph_create(uint64_t hbm, uint64_t dram, int semantic) { return new Policy(hbm, dram, semantic != 0); }
 void ph_destroy(void *p) { delete static_cast<Policy *>(p); }
 void ph_set_compression(void *p, int on) { static_cast<Policy *>(p)->set_compression(on != 0); }
+int ph_pin(void *p, uint64_t lo, uint64_t hi) { return static_cast<Policy *>(p)->pin(HKey{lo, hi}) ? 1 : 0; }
+int ph_unpin(void *p, uint64_t lo, uint64_t hi) { return static_cast<Policy *>(p)->unpin(HKey{lo, hi}) ? 1 : 0; }
 
 // keys: n*2 u64; out_status: n; out_moves: up to cap records of 7 u64
 // (key.lo, key.hi, src_tier, dst_tier, src_off, dst_off, op); returns #moves,

@@ -28,6 +28,9 @@ def ph(tmp_path_factory):
     lib.ph_create.argtypes = [U64, U64, I]
     lib.ph_destroy.argtypes = [V]
     lib.ph_set_compression.argtypes = [V, I]
+    for f in ("ph_pin", "ph_unpin"):
+        getattr(lib, f).restype = I
+        getattr(lib, f).argtypes = [V, U64, U64]
     lib.ph_size.restype = I
     lib.ph_size.argtypes = [V, U64, U64, C.POINTER(U64)]
     lib.ph_put.restype = I
@@ -272,3 +275,28 @@ def test_compression_direct_dram_placement_is_packed(ph):
     assert st == [0] and int(places[0][2]) == 1  # DRAM tier
     assert pol.size("big") == (100_000, 1)
     assert pol.counters()["dram_used"] == 8 + 50_000
+
+
+def test_pinned_blocks_are_never_victims(ph):
+    # zero-copy views pin blocks: a pinned block is neither demoted nor
+    # dropped, whatever the LRU order, until its last pin is released
+    S = 1 << 20
+    pol = Pol(ph, 4 * S, 100 * S)
+    pol.put(["v0", "v1", "a", "b"], [S] * 4)
+    assert ph.ph_pin(pol.p, *pol.key("v0")) == 1 and ph.ph_pin(pol.p, *pol.key("v1")) == 1
+    assert ph.ph_pin(pol.p, *pol.key("v0")) == 1  # two views of v0
+    for i in range(6):
+        pol.put([f"n{i}"], [S])
+    assert pol.tier("v0") == "hbm" and pol.tier("v1") == "hbm"
+    assert pol.tier("a") == "dram" and pol.tier("b") == "dram"
+    # with every HBM block pinned but two, a put still finds room
+    st, _, _, _ = pol.put(["x"], [S])
+    assert st == [0] and pol.tier("x") == "hbm"
+    assert ph.ph_unpin(pol.p, *pol.key("v1")) == 1
+    assert ph.ph_unpin(pol.p, *pol.key("v1")) == 0  # no view left
+    pol.put(["y"], [S])
+    pol.put(["z"], [S])
+    assert pol.tier("v1") == "dram" and pol.tier("v0") == "hbm"
+    ph.ph_unpin(pol.p, *pol.key("v0"))
+    pol.put(["w"], [S])
+    assert pol.tier("v0") == "hbm"  # one pin left
