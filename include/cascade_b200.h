@@ -75,7 +75,10 @@ typedef struct cb_config {
   int32_t prefix_replication;   /* DHT: cb_sync_metadata copies every prefix
                                    block into each rank's local HBM
                                    (broadcast_prefix_data)                   */
-  uint64_t reserved[3];
+  uint64_t collective_timeout_ms; /* DHT: a collective that does not finish in
+                                   time aborts the communicator and fails
+                                   with CB_ERR_TIMEOUT (0 = 600 s)          */
+  uint64_t reserved[2];
 } cb_config;
 
 /* Mirrors DistributedStore::Stats (include/cascade_distributed.hpp:386-409). */
@@ -215,6 +218,15 @@ int cb_sync(cb_store *s);
 /* ---- multi-GPU DHT (replaces DistributedGPUBackend's MPI RMA tier,
  *      src/distributed_backend.cpp:303-514, and the metadata replication of
  *      sync_metadata, :1323-1382) ------------------------------------------ */
+
+/* Failure-path self-tests that fault, trap or hang nothing: each makes one
+ * of the store's bounded device waits run out on purpose and returns the
+ * status a caller would see; the store stays usable afterwards.
+ * CB_SELFTEST_HASH_WAIT: a hash whose input is announced as still arriving
+ * but never published; the kernel's bounded poll gives up after ~1 ms and
+ * the call returns CB_ERR_TIMEOUT. */
+#define CB_SELFTEST_HASH_WAIT 1
+int cb_selftest(cb_store *s, int32_t which);
 
 /* Size of the opaque NCCL unique id blob. */
 #define CB_UID_BYTES 128

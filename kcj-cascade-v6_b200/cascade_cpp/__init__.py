@@ -383,6 +383,7 @@ class DistributedConfig:
         self.replica_bytes = 0        # DHT: HBM for replicas of hot remote blocks (0 = auto)
         self.profile = False          # time every kernel with CUDA events (stats *_ns)
         self.hash_lanes = 32          # SHA-256 chains per warp (8, 16, 32)
+        self.collective_timeout_ms = 0  # DHT: abort a collective after this long (0 = 600 s)
 
 
 class CascadeConfig:
@@ -670,6 +671,7 @@ class DistributedStore(_StoreBase):
         c.replica_bytes = int(cfg.replica_bytes)
         c.kv_compression = 1 if cfg.kv_compression else 0
         c.prefix_replication = 1 if cfg.prefix_replication else 0
+        c.collective_timeout_ms = int(cfg.collective_timeout_ms)
         self._init_native(c)
         self._rank, self._world = 0, 1
         world = int(os.environ.get("WORLD_SIZE", "1"))

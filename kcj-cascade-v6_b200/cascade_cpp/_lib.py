@@ -21,6 +21,7 @@ CB_ERR_TIMEOUT = 5
 CB_ERR_NCCL = 6
 CB_ERR_STATE = 7
 CB_ERR_DEVICE = 8
+CB_SELFTEST_HASH_WAIT = 1
 
 CB_MEM_DEVICE = 0
 CB_MEM_HOST = 1
@@ -57,7 +58,8 @@ class cb_config(C.Structure):
         ("promotion_threshold", C.c_uint32),
         ("kv_compression", C.c_int32),
         ("prefix_replication", C.c_int32),
-        ("reserved", C.c_uint64 * 3),
+        ("collective_timeout_ms", C.c_uint64),
+        ("reserved", C.c_uint64 * 2),
     ]
 
 
@@ -98,6 +100,7 @@ SIGNATURES = [
     ("cb_create", C.c_int, [C.POINTER(cb_config), C.POINTER(_P)]),
     ("cb_destroy", C.c_int, [_P]),
     ("cb_last_error", C.c_char_p, [_P]),
+    ("cb_selftest", C.c_int, [_P, C.c_int32]),
     ("cb_get_views", C.c_int, [_P, _P, C.c_int32, _P, _P, _P, _P]),
     ("cb_release_views", C.c_int, [_P, _P, C.c_int32]),
     ("cb_kv_compress_batch", C.c_int, [_P, _P, _P, _P, C.c_int32, _P]),

@@ -263,6 +263,7 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   dht = new DhtState;
   dht->W = W;
   dht->me = r;
+  if (cfg.collective_timeout_ms) dht->timeout_s = (double)cfg.collective_timeout_ms / 1000.0;
   ncclUniqueId id;
   memcpy(&id, uid, sizeof id);
   ncclConfig_t nc = NCCL_CONFIG_INITIALIZER;

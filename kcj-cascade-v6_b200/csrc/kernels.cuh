@@ -17,6 +17,7 @@ struct HashProgress {
   const unsigned *counter;
   uint32_t seg_chunks;
   uint64_t data_chunks;
+  uint32_t wait_iters = 0;  // polls of the counter before giving up (0 = default)
 };
 
 // sha256.cu — digests: n * 8 words holding the 32 digest bytes in order.

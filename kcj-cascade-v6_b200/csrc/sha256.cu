@@ -18,7 +18,8 @@
 //    additions that are off the e-recurrence are issued as IMAD so they run
 //    on the FMA pipe beside it.
 // The ring is handed over with mbarriers (bounded waits; on timeout the
-// kernel raises kErrTimeout and both warps leave).
+// kernel raises kErrTimeout, sets the ring's abort word, which the other
+// warp's waits also watch, and both warps leave).
 #include "kernels.cuh"
 #include "sha256_core.cuh"
 
@@ -54,7 +55,9 @@ CB_D void mbar_init(uint64_t *bar, uint32_t count) {
 CB_D void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-CB_D bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait on an mbarrier phase that also gives up as soon as the other
+// warp has set *abort.
+CB_D bool mbar_wait(uint64_t *bar, uint32_t parity, const volatile uint32_t *abort) {
   const uint32_t a = smem_u32(bar);
   for (uint64_t it = 0; it < kWaitLimit; ++it) {
     uint32_t ok;
@@ -65,6 +68,7 @@ CB_D bool mbar_wait(uint64_t *bar, uint32_t parity) {
         : "r"(a), "r"(parity)
         : "memory");
     if (ok) return true;
+    if (*abort) return false;
   }
   return false;
 }
@@ -116,16 +120,27 @@ struct Ring {
   uint4 kw[kStages][16][32];  // [stage][round/4][lane]: W[t]+K[t] for 4 rounds
   uint64_t full[kStages];
   uint64_t empty[kStages];
+  uint32_t abort;  // set by a warp that gives up; the other warp's waits watch it
 };
+
+// A warp that gives up: record the error once and tell the other warp.
+CB_D void give_up(Ring &ring, unsigned *err) {
+  if ((threadIdx.x & 31) == 0) {
+    atomicOr(err, kErrTimeout);
+    *reinterpret_cast<volatile uint32_t *>(&ring.abort) = 1u;
+  }
+  __syncwarp();
+}
 
 // Waits (bounded) until the copy stream has published segment `need - 1`.
 // Called by the whole producer warp with a warp-uniform `need`; lane 0
 // polls the counter with acquire loads, the result is broadcast.
-CB_D bool wait_progress(const HashProgress &pg, uint32_t need, uint32_t &seen, unsigned *err) {
+CB_D bool wait_progress(const HashProgress &pg, uint32_t need, uint32_t &seen) {
   if (!pg.counter || seen >= need) return true;
+  const uint64_t limit = pg.wait_iters ? pg.wait_iters : kWaitLimit;
   uint32_t v = 0;
   if ((threadIdx.x & 31) == 0) {
-    for (uint64_t it = 0; it < kWaitLimit; ++it) {
+    for (uint64_t it = 0; it < limit; ++it) {
       asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(pg.counter) : "memory");
       if (v >= need) break;
       __nanosleep(128);
@@ -133,10 +148,7 @@ CB_D bool wait_progress(const HashProgress &pg, uint32_t need, uint32_t &seen, u
   }
   v = __shfl_sync(0xffffffffu, v, 0);
   __syncwarp();
-  if (v < need) {
-    if ((threadIdx.x & 31) == 0) atomicOr(err, kErrTimeout);
-    return false;
-  }
+  if (v < need) return false;
   seen = v;
   return true;
 }
@@ -164,9 +176,11 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
       mbar_init(&ring.full[s], 32);
       mbar_init(&ring.empty[s], 32);
     }
+    ring.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  const volatile uint32_t *abort = &ring.abort;
 
   if (warp == 1) {
     // ------------------------------------------------------------ producer
@@ -177,7 +191,10 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
     // When the blocks are still arriving (host put overlapped with the
     // copy), chunk c may only be read once its segment has landed.
     uint32_t seen = 0;
-    if (!wait_progress(pg, 1, seen, err)) return;
+    if (!wait_progress(pg, 1, seen)) {
+      give_up(ring, err);
+      return;
+    }
     if (aligned && nfull) {
       v0 = ld_stream16(q);
       v1 = ld_stream16(q + 1);
@@ -186,15 +203,18 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
     }
     for (uint64_t c = 0; c < maxc; ++c) {
       const int s = (int)(c % kStages);
-      if (c >= kStages && !mbar_wait(&ring.empty[s], (uint32_t)((c / kStages) - 1) & 1u)) {
-        atomicOr(err, kErrTimeout);
+      if (c >= kStages && !mbar_wait(&ring.empty[s], (uint32_t)((c / kStages) - 1) & 1u, abort)) {
+        give_up(ring, err);
         return;
       }
       if (pg.counter) {
         // this iteration reads chunk c (slow path) and prefetches chunk c+1
         const uint64_t last = pg.data_chunks ? pg.data_chunks - 1 : 0;
         const uint64_t need_chunk = c + 1 < last ? c + 1 : last;
-        if (!wait_progress(pg, (uint32_t)(need_chunk / pg.seg_chunks) + 1, seen, err)) return;
+        if (!wait_progress(pg, (uint32_t)(need_chunk / pg.seg_chunks) + 1, seen)) {
+          give_up(ring, err);
+          return;
+        }
       }
       uint32_t w[16];
       if (c < nfull && aligned) {
@@ -241,8 +261,8 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
   uint32_t st[8] = CB_SHA256_H0;
   for (uint64_t c = 0; c < maxc; ++c) {
     const int s = (int)(c % kStages);
-    if (!mbar_wait(&ring.full[s], (uint32_t)(c / kStages) & 1u)) {
-      atomicOr(err, kErrTimeout);
+    if (!mbar_wait(&ring.full[s], (uint32_t)(c / kStages) & 1u, abort)) {
+      give_up(ring, err);
       return;
     }
     uint32_t a = st[0], b = st[1], cc = st[2], d = st[3];
@@ -303,7 +323,7 @@ cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digest
                                 unsigned *d_err, cudaStream_t stream, const HashProgress *progress) {
   (void)lanes;
   if (n <= 0) return cudaSuccess;
-  const HashProgress pg = progress ? *progress : HashProgress{nullptr, 1, 0};
+  const HashProgress pg = progress ? *progress : HashProgress{nullptr, 1, 0, 0};
   sha256_pc_kernel<<<(n + 31) / 32, 64, 0, stream>>>(d_jobs, n, d_digests, d_err, 1u, pg);
   return cudaGetLastError();
 }

@@ -848,6 +848,24 @@ int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_
 
 // ---------------------------------------------------------------- misc
 
+// Failure-path self-test (cb_selftest): one 1 MiB hash whose input is
+// announced as still arriving (progress word 0, never published). The
+// producer warp's poll gives up after 4096 tries (~1 ms), raises
+// kErrTimeout and sets the ring's abort word; the consumer warp sees it and
+// leaves; the host reads the error word and reports CB_ERR_TIMEOUT. Nothing
+// faults or hangs and the context stays usable.
+int Store::selftest(int which, cudaStream_t st) {
+  if (which != CB_SELFTEST_HASH_WAIT) return fail(CB_ERR_ARG, "unknown self-test %d", which);
+  constexpr uint64_t kBytes = 1 << 20;
+  CB_TRY(cudaStreamSynchronize(copy_stream), "copy stream");
+  CB_TRY(d_staging.ensure(kBytes), "device staging");
+  CB_TRY(cudaMemsetAsync(d_staging.ptr, 0, kBytes, st), "staging");
+  CB_TRY(cudaMemsetAsync(d_progress, 0, 4, st), "progress");
+  HashProgress pg{d_progress, 1024, kBytes / 64, 4096};
+  const uint64_t ptr = (uint64_t)d_staging.ptr, size = kBytes;
+  return hash_device(&ptr, &size, 1, st, &pg);
+}
+
 // Zero-copy get: the caller reads the blocks where they sit in the HBM pool
 // (a torch view, an attention kernel reading KV pages in place) instead of
 // receiving copies — the caller-side step after batch_get
@@ -1139,6 +1157,10 @@ int cb_destroy(cb_store *h) {
 const char *cb_last_error(const cb_store *h) {
   if (!h || !h->s) return cb::g_create_error.c_str();
   return h->s->last_error.c_str();
+}
+
+int cb_selftest(cb_store *h, int32_t which) {
+  return guarded(h, [&](Store *s) -> int { return s->selftest(which, s->own_stream); });
 }
 
 int cb_get_views(cb_store *h, const uint8_t *keys, int32_t n, uint64_t *addrs_out, uint64_t *sizes_out,

@@ -152,6 +152,7 @@ struct Store {
   int get_host(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps,
                uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
   int evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st);
+  int selftest(int which, cudaStream_t st);
   // Zero-copy gets: pool addresses of HBM blocks, pinned until released.
   int get_views(const uint8_t *keys, int n, uint64_t *addrs_out, uint64_t *sizes_out, uint8_t *found_out,
                 cudaStream_t st);
