@@ -361,6 +361,7 @@ void Store::dht_detach() {
 int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
                    const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out, uint8_t *status_out,
                    cudaStream_t st) {
+  Trace tr("cb.dht_put");
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
   const int W = dht->W, me = dht->me;
   // 0. device addresses of the blocks (host blocks: one staging area)
@@ -567,6 +568,7 @@ struct PrefixRec {
 // replicas. A closing all-reduce keeps owners from reusing pool extents
 // before every reader is done.
 int Store::dht_sync_prefixes(cudaStream_t st) {
+  Trace tr("cb.dht_sync_prefixes");
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
   const int W = dht->W, me = dht->me;
   std::vector<PrefixRec> mine;
@@ -734,6 +736,7 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
 
 int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps, int mem_kind,
                    uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
+  Trace tr("cb.dht_get");
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
   const int me = dht->me;
   // Replica hits are served from local HBM. Other keys repeated inside the

@@ -285,6 +285,7 @@ static uint32_t units_of(uint64_t size) {
 // moved blocks and index erases for dropped blocks, stream-ordered on st.
 int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey> &dropped, cudaStream_t st,
                      const std::function<int()> &concurrent) {
+  Trace tr("cb.tier_moves");
   if (moves.empty() && dropped.empty()) return concurrent ? concurrent() : CB_OK;
   bool need_dram = false;
   for (const auto &m : moves) need_dram |= (m.src_tier == kTierDram || m.dst_tier == kTierDram);
@@ -425,6 +426,7 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
 // SHA-256 of device-resident blocks; digests (n*32 B) land in h_out.
 int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaStream_t st,
                        const HashProgress *pg, cudaEvent_t copies_done) {
+  Trace tr("cb.sha256");
   Layout L;
   const size_t o_jobs = L.add(sizeof(HashJob) * n);
   const size_t o_dig = L.add(32ull * n);
@@ -456,6 +458,7 @@ int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaS
 int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
                       const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
                       cudaStream_t st, const HashProgress *pg, cudaEvent_t copies_done) {
+  Trace tr("cb.put");
   std::vector<HKey> keys(n);
   if (keys_in) {
     if (copies_done) CB_TRY(cudaStreamWaitEvent(st, copies_done, 0), "wait copies");
@@ -670,6 +673,7 @@ int Store::stage_overlapped(const void *const *ptrs, const uint64_t *sizes, int 
 
 int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const uint64_t *caps,
                       uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
+  Trace tr("cb.get");
   Layout L;
   const size_t o_keys = L.add(16ull * n);
   const size_t o_outs = L.add(8ull * n);

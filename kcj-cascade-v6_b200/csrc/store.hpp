@@ -8,6 +8,8 @@
 #include <string>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "cascade_b200.h"
 #include "common.cuh"
 #include "kernels.cuh"
@@ -21,6 +23,15 @@
   } while (0)
 
 namespace cb {
+
+// NVTX range over one phase of a batch (hash, tier moves, scatter, gather,
+// DHT exchange): visible to nsys/ncu timelines, a no-op without a tool.
+struct Trace {
+  explicit Trace(const char *name) { nvtxRangePushA(name); }
+  ~Trace() { nvtxRangePop(); }
+  Trace(const Trace &) = delete;
+  Trace &operator=(const Trace &) = delete;
+};
 
 struct PinnedBuf {
   void *ptr = nullptr;
