@@ -66,6 +66,9 @@ def parse():
     p.add_argument("--spill-blocks", type=int, default=40000)
     p.add_argument("--spill-hbm-gb", type=float, default=120.0)
     p.add_argument("--spill-dram-gb", type=float, default=100.0)
+    p.add_argument("--collective-timeout-ms", type=int, default=300000,
+                   help="N>1: a DHT collective that does not finish in time fails instead of waiting")
+    p.add_argument("--trace", action="store_true", help="print per-rank phase markers to stderr")
     p.add_argument("--kv-compression", action="store_true",
                    help="spill: DRAM-tier blocks in the INT8 KVCompressor format (lossy)")
     p.add_argument("--zipf-blocks-per-gpu", type=int, default=20000)
@@ -154,9 +157,18 @@ def gpu_blocks(args, rank, device):
     return pool, ptrs.astype(np.uint64), is_prefix.astype(np.uint8)
 
 
+_TRACE = {"on": False}
+
+
+def trace(args, msg):
+    if _TRACE["on"] or (args is not None and args.trace):
+        print(f"[rank {os.environ.get('RANK', '0')} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def make_store(args, device_index, capacity, dht=False):
     import cascade_cpp
     cfg = cascade_cpp.DistributedConfig()
+    cfg.collective_timeout_ms = args.collective_timeout_ms
     cfg.gpu_capacity_per_device = capacity
     cfg.dram_capacity = 0
     cfg.device = device_index
@@ -178,6 +190,8 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
     keys_all = np.empty((n, 16), np.uint8)
     ev[0].record()
     for i in range(0, n, batch):
+        if _TRACE["on"] and (i // batch) % 16 == 0:
+            trace(None, f"  put batch {i // batch}")
         k, _ = store.put_ptrs(ptrs[i:i + batch], sizes[i:i + batch], device_memory,
                               prefix=prefix[i:i + batch])
         keys_all[i:i + batch] = k
@@ -189,6 +203,8 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
     outs_b = np.uint64(base) + np.arange(batch, dtype=np.uint64) * np.uint64(size)
     got = remote = 0
     for i in range(0, len(keys), batch):
+        if _TRACE["on"] and (i // batch) % 16 == 0:
+            trace(None, f"  get batch {i // batch} of {len(keys)} keys")
         kk = keys[i:i + batch]
         m = len(kk)
         s, f = store.get_ptrs(kk, outs_b[:m], np.full(m, size, np.uint64), device_memory)
@@ -279,6 +295,7 @@ def cpu_reference(args, n_blocks, steps=1, threads=None):
 
 def main():
     args = parse()
+    _TRACE["on"] = args.trace
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -326,13 +343,16 @@ def main():
         return spill_main(args, rank, world, local, device)
     if args.workload == "sweep":
         return sweep_main(args, rank, world, local, device)
+    trace(args, "generating blocks")
     pool, ptrs, prefix = gpu_blocks(args, rank, device)
     sizes = np.full(len(ptrs), size, np.uint64)
     n_unique = pool.numel() // size
     # DHT (N>1): an owner holds ~1/W of every rank's unique blocks; leave
     # room for the owner imbalance of a random hash placement.
     cap = n_unique * size + (256 << 20) if world == 1 else int(n_unique * size * 1.15) + (1 << 30)
+    trace(args, "creating the store")
     store = make_store(args, local, cap, dht=world > 1)
+    trace(args, "store ready")
     out_buf = torch.empty(args.batch * size, dtype=torch.uint8, device=device)
 
     def sync_all():
@@ -341,8 +361,10 @@ def main():
             torch.distributed.barrier()
 
     for w in range(args.warmup):
+        trace(args, f"warm-up pass {w}")
         store.clear()
         run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, w)
+    trace(args, "timed passes")
     st0 = store._n.stats()
     sync_all()
     run_pass.remote_bytes = 0
@@ -436,13 +458,16 @@ def main():
     line["clocks"] = clk.summary()
 
     if not args.no_sweep:
+        trace(args, "batch sweep")
         sw = batch_sweep(args, store, ptrs, sizes, prefix, out_buf, size)  # collective in a DHT
         if rank == 0:
             line["sweep"] = sw
     del pool
     torch.cuda.empty_cache()
     if not args.no_e2e:
+        trace(args, "e2e")
         line["e2e"] = e2e_run(args, rank, world, device, store)
+    trace(args, "done")
     if rank == 0 and not args.no_cpu:
         try:
             v, det = cpu_reference(args, args.cpu_blocks, steps=1)
