@@ -202,9 +202,17 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
     base = out_buf.data_ptr() if hasattr(out_buf, "data_ptr") else out_buf.ctypes.data
     outs_b = np.uint64(base) + np.arange(batch, dtype=np.uint64) * np.uint64(size)
     got = remote = 0
-    for i in range(0, len(keys), batch):
-        if _TRACE["on"] and (i // batch) % 16 == 0:
-            trace(None, f"  get batch {i // batch} of {len(keys)} keys")
+    # In a DHT every get is collective: ranks whose streams hold fewer unique
+    # blocks join the remaining calls with empty batches.
+    n_get = (len(keys) + batch - 1) // batch
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        t = torch.tensor([n_get], dtype=torch.int64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        n_get = int(t.item())
+    for j in range(n_get):
+        i = j * batch
+        if _TRACE["on"] and j % 16 == 0:
+            trace(None, f"  get batch {j} of {len(keys)} keys")
         kk = keys[i:i + batch]
         m = len(kk)
         s, f = store.get_ptrs(kk, outs_b[:m], np.full(m, size, np.uint64), device_memory)
