@@ -366,12 +366,17 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   const int W = dht->W, me = dht->me;
   // 0. device addresses of the blocks (host blocks: one staging area)
   std::vector<uint64_t> dptr(n);
+  // Host blocks at a constant stride are staged segment-major on copy_stream
+  // while the hash consumes them (stage_overlapped, as for 1-GPU host puts).
+  HashProgress pg;
+  bool overlapped = false;
   if (mem_kind == CB_MEM_HOST) {
     uint64_t total = 0;
     for (int i = 0; i < n; ++i) total += align_up(sizes[i], 256);
     CB_TRY_CUDA(d_staging.ensure(std::max<uint64_t>(total, 256)), "device staging");
+    overlapped = !keys_in && n && stage_overlapped(ptrs, sizes, n, dptr.data(), pg, st) == CB_OK;
     uint64_t off = 0;
-    for (int i = 0; i < n; ++i) {
+    for (int i = 0; i < n && !overlapped; ++i) {
       dptr[i] = (uint64_t)d_staging.ptr + off;
       if (sizes[i])
         CB_TRY_CUDA(cudaMemcpyAsync(reinterpret_cast<void *>(dptr[i]), ptrs[i], sizes[i], cudaMemcpyHostToDevice, st),
@@ -386,7 +391,12 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   if (keys_in) {
     for (int i = 0; i < n; ++i) keys[i] = to_hkey(keys_in + 16 * i);
   } else if (n) {
-    int rc = hash_device(dptr.data(), sizes, n, st);
+    // with overlapped staging, st also waits for every copy after the hash
+    int rc = hash_device(dptr.data(), sizes, n, st, overlapped ? &pg : nullptr, overlapped ? ev_copies : nullptr);
+    if (overlapped) {
+      const cudaError_t e = cudaStreamSynchronize(copy_stream);
+      if (rc == CB_OK && e != cudaSuccess) return cuda_fail(e, "copy stream");
+    }
     if (rc) return rc;
     const uint8_t *dig = static_cast<const uint8_t *>(h_out.ptr);
     for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32 * i);
@@ -927,10 +937,27 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
                 "ncclAllReduce(get barrier)");
   if (rc) return rc;
   if (mem_kind == CB_MEM_HOST) {
-    for (int i = 0; i < n; ++i) {
-      if ((found_out[i] & 0x0f) == CB_FOUND_MISS || (found_out[i] & CB_FOUND_NOT_COPIED) || !sizes_out[i]) continue;
-      CB_TRY_CUDA(cudaMemcpyAsync(outs[i], reinterpret_cast<void *>(dst[i]), sizes_out[i], cudaMemcpyDeviceToHost, st),
-                  "D2H block");
+    // one D2H per run of blocks contiguous both in staging and in the
+    // caller's memory (a caller's [n, block] buffer is one copy)
+    auto copied = [&](int i) {
+      return (found_out[i] & 0x0f) != CB_FOUND_MISS && !(found_out[i] & CB_FOUND_NOT_COPIED) && sizes_out[i];
+    };
+    int i = 0;
+    while (i < n) {
+      if (!copied(i)) {
+        ++i;
+        continue;
+      }
+      int e = i + 1;
+      uint64_t run = sizes_out[i];
+      while (e < n && copied(e) && dst[e] - dst[i] == run && dst[e] - dst[e - 1] == sizes_out[e - 1] &&
+             static_cast<uint8_t *>(outs[i]) + run == outs[e]) {
+        run += sizes_out[e];
+        ++e;
+      }
+      CB_TRY_CUDA(cudaMemcpyAsync(outs[i], reinterpret_cast<void *>(dst[i]), run, cudaMemcpyDeviceToHost, st),
+                  "D2H blocks");
+      i = e;
     }
   }
   rc = dht_sync(st);
