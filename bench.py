@@ -201,7 +201,7 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
     keys = uk[order].view(np.uint8).reshape(-1, 16)
     base = out_buf.data_ptr() if hasattr(out_buf, "data_ptr") else out_buf.ctypes.data
     outs_b = np.uint64(base) + np.arange(batch, dtype=np.uint64) * np.uint64(size)
-    got = remote = 0
+    got = 0
     # In a DHT every get is collective: ranks whose streams hold fewer unique
     # blocks join the remaining calls with empty batches.
     n_get = (len(keys) + batch - 1) // batch
@@ -218,12 +218,10 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
         s, f = store.get_ptrs(kk, outs_b[:m], np.full(m, size, np.uint64), device_memory)
         ok = (f & 0x0F) != 0
         got += int(s[ok].sum())
-        remote += int(s[(f & 0x0F) == 3].sum())  # CB_FOUND_REMOTE_HBM: crossed NVLink
     ev[2].record()
     ev[2].synchronize()
     put_s = ev[0].elapsed_time(ev[1]) / 1e3
     get_s = ev[1].elapsed_time(ev[2]) / 1e3
-    run_pass.remote_bytes = getattr(run_pass, "remote_bytes", 0) + remote
     return put_s, get_s, int(sizes.sum()), got
 
 
@@ -375,7 +373,6 @@ def main():
     trace(args, "timed passes")
     st0 = store._n.stats()
     sync_all()
-    run_pass.remote_bytes = 0
     put_t = get_t = 0.0
     put_b = get_b = 0
     t_ev0 = torch.cuda.Event(enable_timing=True)
