@@ -53,18 +53,23 @@ def test_ctypes_signatures_cover_header():
 
 
 def test_struct_layouts_match_c(tmp_path):
+    # every field of every ABI struct: the ctypes mirror's offset must be the
+    # C compiler's offsetof, and the sizes must agree
+    structs = [("cb_config", L.cb_config), ("cb_stats", L.cb_stats), ("cb_location", L.cb_location)]
+    lines, want = [], []
+    for cname, cls in structs:
+        lines.append(f'printf("%zu\\n", sizeof({cname}));')
+        want.append(C.sizeof(cls))
+        for fname, _ in cls._fields_:
+            lines.append(f'printf("%zu\\n", offsetof({cname}, {fname}));')
+            want.append(getattr(cls, fname).offset)
     prog = tmp_path / "layout.c"
-    prog.write_text(
-        '#include <stdio.h>\n#include <stddef.h>\n#include "cascade_b200.h"\n'
-        "int main(void){printf(\"%zu %zu %zu %zu %zu %zu\\n\", sizeof(cb_config), sizeof(cb_stats),"
-        " sizeof(cb_location), offsetof(cb_config, staging_bytes), offsetof(cb_location, offset),"
-        " offsetof(cb_stats, dropped_blocks)); return 0;}\n")
+    prog.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "cascade_b200.h"\n'
+                    "int main(void){" + "".join(lines) + "return 0;}\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", os.path.dirname(HEADER), str(prog), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
-    assert vals == [C.sizeof(L.cb_config), C.sizeof(L.cb_stats), C.sizeof(L.cb_location),
-                    L.cb_config.staging_bytes.offset, L.cb_location.offset.offset,
-                    L.cb_stats.dropped_blocks.offset]
+    assert vals == want
 
 
 def test_config_defaults(lib):
