@@ -425,7 +425,7 @@ def main():
         "config": config_dict(args),
         "batch_put_gbs": round(put_gbs, 3), "batch_get_gbs": round(get_gbs, 3),
         "roofline": {
-            "kernel": "sha256_batch_kernel", "bound": "hbm", "achieved": round(sha_achieved, 2),
+            "kernel": "sha256_pc_kernel", "bound": "hbm", "achieved": round(sha_achieved, 2),
             "peak": hbm_peak, "unit": "GB/s", "frac": round(sha_achieved / hbm_peak, 5),
             "peak_source": peak_src,
             # dram__bytes_read.sum + dram__bytes_write.sum of one 1024-block
