@@ -295,10 +295,11 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const CopyDesc *__restrict
 
 cudaError_t launch_batch_copy(const CopyDesc *d_desc, const uint32_t *d_unit_start, int n,
                               uint32_t total_units, int engine, unsigned *d_err, int num_sms,
-                              cudaStream_t stream) {
+                              cudaStream_t stream, int lsu_ctas_per_sm) {
   if (n <= 0 || total_units == 0) return cudaSuccess;
   if (engine == 2) {
-    const uint32_t grid = min(total_units, (uint32_t)(num_sms * kLsuCtasPerSm));
+    const int cps = lsu_ctas_per_sm > 0 && lsu_ctas_per_sm < kLsuCtasPerSm ? lsu_ctas_per_sm : kLsuCtasPerSm;
+    const uint32_t grid = min(total_units, (uint32_t)(num_sms * cps));
     copy_lsu_kernel<<<grid, kLsuThreads, 0, stream>>>(d_desc, d_unit_start, n, total_units);
     return cudaGetLastError();
   }

@@ -30,9 +30,11 @@ cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digest
 // descriptor's size is skipped. engine: 1 = TMA bulk (device memory only),
 // 2 = vector LSU. Descriptors with flags bit 0 (host memory) always take the
 // LSU path.
+// lsu_ctas_per_sm bounds the LSU engine's grid (a host-link-bound move that
+// runs beside other kernels leaves them room on every SM).
 cudaError_t launch_batch_copy(const CopyDesc *d_desc, const uint32_t *d_unit_start, int n,
                               uint32_t total_units, int engine, unsigned *d_err, int num_sms,
-                              cudaStream_t stream);
+                              cudaStream_t stream, int lsu_ctas_per_sm = 8);
 
 // kvquant.cu — INT8 packing (KVCompressor::compress format) of blocks:
 // descriptor i packs the d.size-byte block at d.src (device memory, d.size
@@ -42,7 +44,7 @@ cudaError_t launch_batch_copy(const CopyDesc *d_desc, const uint32_t *d_unit_sta
 // kernels (min/max, then pack). Unpacking is launch_batch_copy with
 // kCopyUnpack descriptors.
 cudaError_t launch_kv_pack(const CopyDesc *d_desc, const uint32_t *d_unit_start, int n, uint32_t total_units,
-                           int *d_mm, int num_sms, cudaStream_t stream);
+                           int *d_mm, int num_sms, cudaStream_t stream, int ctas_per_sm = 8);
 
 // index.cu — device index mutations and lookups.
 cudaError_t launch_index_insert(Slot *table, uint64_t mask, const IndexRec *recs, int n,

@@ -162,9 +162,10 @@ __global__ void __launch_bounds__(kThreads) kv_pack_kernel(const CopyDesc *__res
 }  // namespace
 
 cudaError_t launch_kv_pack(const CopyDesc *d_desc, const uint32_t *d_unit_start, int n, uint32_t total_units,
-                           int *d_mm, int num_sms, cudaStream_t stream) {
+                           int *d_mm, int num_sms, cudaStream_t stream, int ctas_per_sm) {
   if (n <= 0 || total_units == 0) return cudaSuccess;
-  const uint32_t grid = min(total_units, (uint32_t)(num_sms * kCtasPerSm));
+  const int cps = ctas_per_sm > 0 && ctas_per_sm < kCtasPerSm ? ctas_per_sm : kCtasPerSm;
+  const uint32_t grid = min(total_units, (uint32_t)(num_sms * cps));
   kv_minmax_kernel<<<grid, kThreads, 0, stream>>>(d_desc, d_unit_start, n, total_units, d_mm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;

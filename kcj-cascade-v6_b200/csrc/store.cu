@@ -359,6 +359,9 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     CB_TRY(cudaStreamWaitEvent(move_stream, ev_move_in, 0), "wait");
     ds = move_stream;
   }
+  // Host-link-bound demotions beside a gather take 2 CTAs per SM, so that
+  // the gather's CTAs fit next to them instead of waiting for them to drain.
+  const int move_ctas = concurrent ? 2 : 8;
   auto launch_group = [&](int g, cudaStream_t gs) -> int {
     if (grp[g].empty()) return CB_OK;
     const CopyDesc *gd = ddesc + base[g];
@@ -367,7 +370,8 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     if (g == 1) {
       CB_TRY(timed(3, grp_bytes[g], gs,
                    [&] {
-                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + o_mm), num_sms, gs);
+                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + o_mm), num_sms, gs,
+                                           g == 2 ? 8 : move_ctas);
                    }),
              "demote pack");
       launches++;  // two kernels
@@ -375,7 +379,10 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
       // host-link moves on the LSU engine; device-only groups on the store's
       const int engine = dev_only[g] ? copy_engine : 2;
       CB_TRY(timed(3, grp_bytes[g], gs,
-                   [&] { return launch_batch_copy(gd, gu, gn, total[g], engine, d_err, num_sms, gs); }),
+                   [&] {
+                     return launch_batch_copy(gd, gu, gn, total[g], engine, d_err, num_sms, gs,
+                                              g == 2 ? 8 : move_ctas);
+                   }),
              g ? "promote copy" : "demote copy");
     }
     return CB_OK;
