@@ -85,6 +85,9 @@ constexpr uint64_t kPackMinBytes = 64;    // smaller blocks are stored as they a
 constexpr uint64_t kPackLead = 8;
 inline uint64_t packed_bytes(uint64_t size) { return kPackHeaderBytes + size / 2; }
 
+// Plain tier moves of at least this many bytes go through the copy engines.
+constexpr uint64_t kDmaMinBytes = 256 * 1024;
+
 // How a tier move transforms the bytes it moves.
 enum : uint8_t { kMoveCopy = 0, kMovePack = 1, kMoveUnpack = 2 };
 

@@ -293,17 +293,26 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     cudaError_t e = ensure_dram();
     if (e != cudaSuccess) return cuda_fail(e, "pinned DRAM arena cudaHostAlloc");
   }
-  // Launch groups, in this order: demotions copied as they are, demotions
-  // packed to INT8 (kv_compression), then promotions (copies and unpacks).
-  // Every promotion runs after every demotion: its HBM destination may be an
-  // extent a demotion of the same plan vacated.
-  std::vector<const TierMove *> grp[3];
-  for (const auto &m : moves) grp[m.dst_tier == kTierDram ? (m.op == kMovePack ? 1 : 0) : 2].push_back(&m);
+  // Groups: 0 demotions copied by the LSU kernel, 1 demotions packed to INT8
+  // (kv_compression), 2 promotions by kernel (copies from a device copy,
+  // unpacks, small blocks), 3 demotions and 4 promotions of large plain
+  // blocks by the copy engines (cudaMemcpyAsync: the DMA engines move each
+  // direction at the link rate and leave the SMs' host-memory path to the
+  // kernels). Every promotion runs after every demotion: its HBM destination
+  // may be an extent a demotion of the same plan vacated.
+  constexpr int kGroups = 5;
+  auto group_of = [](const TierMove &m) {
+    const bool dma = m.op == kMoveCopy && !m.src_dev && m.size >= kDmaMinBytes;
+    if (m.dst_tier == kTierDram) return m.op == kMovePack ? 1 : (dma ? 3 : 0);
+    return dma ? 4 : 2;
+  };
+  std::vector<const TierMove *> grp[kGroups];
+  for (const auto &m : moves) grp[group_of(m)].push_back(&m);
   const int nm = (int)moves.size(), nd = (int)dropped.size(), npk = (int)grp[1].size();
   Layout L;
   const size_t o_desc = L.add(sizeof(CopyDesc) * nm);
-  size_t o_us[3];
-  for (int g = 0; g < 3; ++g) o_us[g] = L.add(sizeof(uint32_t) * (grp[g].size() + 1));
+  size_t o_us[kGroups];
+  for (int g = 0; g < kGroups; ++g) o_us[g] = L.add(sizeof(uint32_t) * (grp[g].size() + 1));
   const size_t o_mm = L.add(sizeof(int) * 2 * npk);
   const size_t o_upd = L.add(sizeof(IndexRec) * nm);
   const size_t o_era = L.add(sizeof(IndexRec) * nd);
@@ -314,12 +323,12 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
   int *mm = reinterpret_cast<int *>(h + o_mm);
   IndexRec *upd = reinterpret_cast<IndexRec *>(h + o_upd);
   IndexRec *era = reinterpret_cast<IndexRec *>(h + o_era);
-  uint32_t total[3] = {0, 0, 0};
-  uint64_t grp_bytes[3] = {0, 0, 0};
-  int base[3] = {0, 0, 0};
-  bool dev_only[3] = {true, true, true};  // no host-memory side in the group
+  uint32_t total[kGroups] = {};
+  uint64_t grp_bytes[kGroups] = {};
+  int base[kGroups] = {};
+  bool dev_only[kGroups] = {true, true, true, true, true};  // no host-memory side in the group
   int di = 0;
-  for (int g = 0; g < 3; ++g) {
+  for (int g = 0; g < kGroups; ++g) {
     uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us[g]);
     base[g] = di;
     for (size_t j = 0; j < grp[g].size(); ++j) {
@@ -387,7 +396,43 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     }
     return CB_OK;
   };
+  // DMA groups: one cudaMemcpyAsync per run of moves contiguous on both
+  // sides, bracketed by profiling events like a kernel (not counted as one).
+  auto dma_group = [&](int g, cudaStream_t gs) -> int {
+    if (grp[g].empty()) return CB_OK;
+    const bool down = g == 3;
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (profile) {
+      CB_TRY(prof_event(a), "event");
+      CB_TRY(prof_event(b), "event");
+      CB_TRY(cudaEventRecord(a, gs), "event");
+    }
+    const auto &v = grp[g];
+    size_t j = 0;
+    while (j < v.size()) {
+      uint64_t run = v[j]->size;
+      size_t e = j + 1;
+      while (e < v.size() && v[e]->src_off == v[j]->src_off + run && v[e]->dst_off == v[j]->dst_off + run) {
+        run += v[e]->size;
+        ++e;
+      }
+      if (down) {
+        CB_TRY(cudaMemcpyAsync(dram_host + v[j]->dst_off, pool + v[j]->src_off, run, cudaMemcpyDeviceToHost, gs),
+               "demote DMA");
+      } else {
+        CB_TRY(cudaMemcpyAsync(pool + v[j]->dst_off, dram_host + v[j]->src_off, run, cudaMemcpyHostToDevice, gs),
+               "promote DMA");
+      }
+      j = e;
+    }
+    if (profile) {
+      CB_TRY(cudaEventRecord(b, gs), "event");
+      prof_pending.push_back(ProfRec{3, grp_bytes[g], a, b});
+    }
+    return CB_OK;
+  };
   int rc = launch_group(0, ds);
+  if (rc == CB_OK) rc = dma_group(3, ds);
   if (rc == CB_OK) rc = launch_group(1, ds);
   if (concurrent) {
     // join: whatever happens, st waits for the demotions before going on
@@ -405,6 +450,7 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     return rc;
   }
   rc = launch_group(2, st);
+  if (rc == CB_OK) rc = dma_group(4, st);
   if (rc) {
     cudaStreamSynchronize(st);
     return rc;
