@@ -740,19 +740,35 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
   memcpy(h + o_keys, keys, 16ull * n);
   memcpy(h + o_outs, outs, 8ull * n);
-  memcpy(h + o_caps, caps, 8ull * n);
+  // DRAM hits of large plain blocks are copied by the H2D copy engine from
+  // the location the host metadata holds (the engines move each direction at
+  // the link rate, and beside the demotions' D2H DMA): the lookup kernel gets
+  // a capacity of 0 for them, so it reports them without copying.
+  uint64_t *dcaps = reinterpret_cast<uint64_t *>(h + o_caps);
+  std::vector<int> dma_req;
   uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
   uint32_t total = 0;
-  uint64_t bytes = 0;
+  uint64_t bytes = 0, dma_bytes = 0;
   for (int i = 0; i < n; ++i) {
     us[i] = total;
+    dcaps[i] = caps[i];
     const BlockMeta *m = policy.find(to_hkey(keys + 16 * i));
-    if (m && m->size <= caps[i]) {
-      total += units_of(m->size);
-      bytes += m->size;
+    if (!m || m->size > caps[i]) continue;
+    if (m->tier == kTierDram && !m->packed && m->size >= kDmaMinBytes) {
+      dma_req.push_back(i);
+      dma_bytes += m->size;
+      dcaps[i] = 0;
+      continue;
     }
+    total += units_of(m->size);
+    bytes += m->size;
   }
   us[n] = total;
+  std::vector<std::pair<uint64_t, uint64_t>> dma_src(dma_req.size());  // (arena offset, size)
+  for (size_t j = 0; j < dma_req.size(); ++j) {
+    const BlockMeta *m = policy.find(to_hkey(keys + 16 * dma_req[j]));
+    dma_src[j] = {Policy::data_offset(*m), m->size};
+  }
   // LRU touches first (CascadeStore::get touches on hit,
   // src/cascade_core.cpp:1281), so that blocks of this batch are the last
   // victims of the promotions below.
@@ -792,6 +808,32 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   }
   uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
   auto lookup_and_gather = [&]() -> int {
+    if (!dma_req.empty()) {  // runs contiguous in the arena and in the caller's memory: one copy
+      cudaEvent_t a = nullptr, b = nullptr;
+      if (profile) {
+        CB_TRY(prof_event(a), "event");
+        CB_TRY(prof_event(b), "event");
+        CB_TRY(cudaEventRecord(a, st), "event");
+      }
+      size_t j = 0;
+      while (j < dma_req.size()) {
+        uint64_t run = dma_src[j].second;
+        size_t e = j + 1;
+        while (e < dma_req.size() && dma_src[e].first == dma_src[j].first + run &&
+               outs[dma_req[e]] == outs[dma_req[j]] + run) {
+          run += dma_src[e].second;
+          ++e;
+        }
+        CB_TRY(cudaMemcpyAsync(reinterpret_cast<void *>(outs[dma_req[j]]), dram_host + dma_src[j].first, run,
+                               cudaMemcpyHostToDevice, st),
+               "DRAM hit DMA");
+        j = e;
+      }
+      if (profile) {
+        CB_TRY(cudaEventRecord(b, st), "event");
+        prof_pending.push_back(ProfRec{2, dma_bytes, a, b});
+      }
+    }
     CB_TRY(cudaMemcpyAsync(d, h, o_desc, cudaMemcpyHostToDevice, st), "H2D get");
     LookupArgs a;
     a.table = table;
@@ -826,7 +868,14 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   if (rc) return rc;
   rc = check_device_error(st);
   if (rc) return rc;
-  const GetResult *res = static_cast<const GetResult *>(h_out.ptr);
+  GetResult *res = static_cast<GetResult *>(h_out.ptr);
+  for (size_t j = 0; j < dma_req.size(); ++j) {
+    // copied by the DMA above; the lookup saw capacity 0
+    const int i = dma_req[j];
+    if ((res[i].code & 0x0f) != CB_FOUND_LOCAL_DRAM || res[i].size != dma_src[j].second)
+      return fail(CB_ERR_STATE, "device index disagrees with the host metadata for request %d", i);
+    res[i].code = CB_FOUND_LOCAL_DRAM;
+  }
   for (int i = 0; i < n; ++i) {
     sizes_out[i] = res[i].size;
     found_out[i] = (uint8_t)res[i].code;
