@@ -22,6 +22,8 @@
 #include <string>
 #include <vector>
 
+#include <cuda.h>  // CUpointer_attribute (the entry point is fetched at run time)
+
 #include "cascade_b200.h"
 #include "kernels.cuh"
 #include "policy.hpp"
@@ -43,6 +45,39 @@ inline uint64_t meta_word(uint64_t size, uint8_t prefix) {
 }
 
 }  // namespace
+
+// ------------------------------------------------------------ allocations
+
+namespace {
+using PtrAttrFn = CUresult (*)(void *, CUpointer_attribute, CUdeviceptr);
+PtrAttrFn pointer_attribute_fn() {
+  static const PtrAttrFn fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<PtrAttrFn>(nullptr);
+    return reinterpret_cast<PtrAttrFn>(f);
+  }();
+  return fn;
+}
+}  // namespace
+
+bool one_allocation(const void *p, uint64_t bytes) {
+  const PtrAttrFn fn = pointer_attribute_fn();
+  if (!fn) return false;
+  CUdeviceptr start = 0;
+  size_t size = 0;
+  const CUdeviceptr a = reinterpret_cast<CUdeviceptr>(p);
+  if (fn(&start, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, a) != CUDA_SUCCESS) {
+    cudaPointerAttributes at;
+    const bool known = cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type != cudaMemoryTypeUnregistered;
+    cudaGetLastError();
+    return !known;  // pageable host memory: any extent
+  }
+  if (fn(&size, CU_POINTER_ATTRIBUTE_RANGE_SIZE, a) != CUDA_SUCCESS) return false;
+  return a >= start && a - start + bytes <= size;
+}
 
 // ------------------------------------------------------------ buffers
 
@@ -657,7 +692,8 @@ int Store::put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_
       int e = k + 1;
       uint64_t run = sizes[k];
       while (e < j && static_cast<const uint8_t *>(ptrs[k]) + (dptrs[e - i] - dptrs[k - i]) == ptrs[e] &&
-             dptrs[e - i] - dptrs[e - 1 - i] == sizes[e - 1]) {
+             dptrs[e - i] - dptrs[e - 1 - i] == sizes[e - 1] &&
+             one_allocation(ptrs[k], dptrs[e - i] - dptrs[k - i] + sizes[e])) {
         run = dptrs[e - i] - dptrs[k - i] + sizes[e];
         ++e;
       }
@@ -695,6 +731,8 @@ int Store::stage_overlapped(const void *const *ptrs, const uint64_t *sizes, int 
     if (sizes[i] != size) return CB_ERR_ARG;
     if (static_cast<const uint8_t *>(ptrs[i]) - static_cast<const uint8_t *>(ptrs[i - 1]) != stride) return CB_ERR_ARG;
   }
+  // the strided copies read the caller's blocks as one buffer
+  if (!one_allocation(ptrs[0], (uint64_t)stride * (n - 1) + size)) return CB_ERR_ARG;
   const uint64_t slot = align_up(size, 256);
   for (int i = 0; i < n; ++i) dptrs[i] = (uint64_t)d_staging.ptr + slot * i;
   const uint32_t nseg = (uint32_t)((size + kSeg - 1) / kSeg);
@@ -820,7 +858,8 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
         uint64_t run = dma_src[j].second;
         size_t e = j + 1;
         while (e < dma_req.size() && dma_src[e].first == dma_src[j].first + run &&
-               outs[dma_req[e]] == outs[dma_req[j]] + run) {
+               outs[dma_req[e]] == outs[dma_req[j]] + run &&
+               one_allocation(reinterpret_cast<const void *>(outs[dma_req[j]]), run + dma_src[e].second)) {
           run += dma_src[e].second;
           ++e;
         }
@@ -937,7 +976,8 @@ int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_
       uint64_t run = sizes_out[k];
       while (e < j && (found_out[e] & 0x0f) != CB_FOUND_MISS && sizes_out[e] <= caps[e] &&
              static_cast<uint8_t *>(outs[k]) + (dptrs[e - i] - dptrs[k - i]) == outs[e] &&
-             dptrs[e - i] - dptrs[e - 1 - i] == sizes_out[e - 1]) {
+             dptrs[e - i] - dptrs[e - 1 - i] == sizes_out[e - 1] &&
+             one_allocation(outs[k], dptrs[e - i] - dptrs[k - i] + sizes_out[e])) {
         run = dptrs[e - i] - dptrs[k - i] + sizes_out[e];
         ++e;
       }

@@ -203,6 +203,13 @@ struct Store {
 
 inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
 
+// True when one copy may cover [p, p + bytes): the range lies inside a single
+// CUDA allocation (device, pinned or managed), or p is memory CUDA does not
+// know (pageable host memory, copied through staging whatever its extent).
+// Neighbouring caller buffers can be adjacent in the address space yet belong
+// to different allocations; a copy must not span them.
+bool one_allocation(const void *p, uint64_t bytes);
+
 inline HKey to_hkey(const uint8_t *p) {
   HKey k;
   __builtin_memcpy(&k.lo, p, 8);
