@@ -85,8 +85,11 @@ constexpr uint64_t kPackMinBytes = 64;    // smaller blocks are stored as they a
 constexpr uint64_t kPackLead = 8;
 inline uint64_t packed_bytes(uint64_t size) { return kPackHeaderBytes + size / 2; }
 
-// Plain tier moves of at least this many bytes go through the copy engines.
+// Tier moves of blocks of at least this many bytes go through the copy
+// engines (packed ones through an HBM staging area of at most
+// kPackStagingBytes per direction; the rest use the SM kernels).
 constexpr uint64_t kDmaMinBytes = 256 * 1024;
+constexpr uint64_t kPackStagingBytes = 1ull << 30;
 
 // How a tier move transforms the bytes it moves.
 enum : uint8_t { kMoveCopy = 0, kMovePack = 1, kMoveUnpack = 2 };

@@ -182,6 +182,8 @@ Store::~Store() {
   h_out.release();
   h_err.release();
   d_staging.release();
+  d_pack.release();
+  d_unpack.release();
   if (move_stream) {
     cudaStreamSynchronize(move_stream);
     cudaStreamDestroy(move_stream);
@@ -329,39 +331,55 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     if (e != cudaSuccess) return cuda_fail(e, "pinned DRAM arena cudaHostAlloc");
   }
   // Groups: 0 demotions copied by the LSU kernel, 1 demotions packed to INT8
-  // (kv_compression), 2 promotions by kernel (copies from a device copy,
-  // unpacks, small blocks), 3 demotions and 4 promotions of large plain
-  // blocks by the copy engines (cudaMemcpyAsync: the DMA engines move each
-  // direction at the link rate and leave the SMs' host-memory path to the
-  // kernels). Every promotion runs after every demotion: its HBM destination
-  // may be an extent a demotion of the same plan vacated.
-  constexpr int kGroups = 5;
-  auto group_of = [](const TierMove &m) {
-    const bool dma = m.op == kMoveCopy && !m.src_dev && m.size >= kDmaMinBytes;
-    if (m.dst_tier == kTierDram) return m.op == kMovePack ? 1 : (dma ? 3 : 0);
-    return dma ? 4 : 2;
-  };
+  // straight into the mapped arena (kv_compression), 2 promotions by kernel
+  // (copies from a device copy, unpacks, small blocks), 3 demotions and 4
+  // promotions of large plain blocks by the copy engines (cudaMemcpyAsync:
+  // the DMA engines move each direction at the link rate and overlap each
+  // other, which SM-issued host-memory traffic does not), 5 large demotions
+  // packed into an HBM staging area and moved by the D2H copy engine. Every
+  // promotion runs after every demotion: its HBM destination may be an
+  // extent a demotion of the same plan vacated.
+  constexpr int kGroups = 6;
   std::vector<const TierMove *> grp[kGroups];
-  for (const auto &m : moves) grp[group_of(m)].push_back(&m);
-  const int nm = (int)moves.size(), nd = (int)dropped.size(), npk = (int)grp[1].size();
+  std::vector<uint64_t> pslot;  // group 5: staging offsets of the packed images
+  uint64_t pstage = 0;
+  for (const auto &m : moves) {
+    const bool big = !m.src_dev && m.size >= kDmaMinBytes;
+    int g;
+    if (m.dst_tier == kTierDram && m.op == kMovePack) {
+      const uint64_t slot = align_up(kPackLead + packed_bytes(m.size), 256);
+      g = (big && pstage + slot <= kPackStagingBytes) ? 5 : 1;
+      if (g == 5) {
+        pslot.push_back(pstage);
+        pstage += slot;
+      }
+    } else if (m.dst_tier == kTierDram) {
+      g = (big && m.op == kMoveCopy) ? 3 : 0;
+    } else {
+      g = (big && m.op == kMoveCopy) ? 4 : 2;
+    }
+    grp[g].push_back(&m);
+  }
+  if (pstage) CB_TRY(d_pack.ensure(pstage), "packing staging");  // before any concurrent work
+  const int nm = (int)moves.size(), nd = (int)dropped.size();
   Layout L;
   const size_t o_desc = L.add(sizeof(CopyDesc) * nm);
   size_t o_us[kGroups];
   for (int g = 0; g < kGroups; ++g) o_us[g] = L.add(sizeof(uint32_t) * (grp[g].size() + 1));
-  const size_t o_mm = L.add(sizeof(int) * 2 * npk);
+  const size_t o_mm1 = L.add(sizeof(int) * 2 * grp[1].size());
+  const size_t o_mm5 = L.add(sizeof(int) * 2 * grp[5].size());
   const size_t o_upd = L.add(sizeof(IndexRec) * nm);
   const size_t o_era = L.add(sizeof(IndexRec) * nd);
   CB_TRY(h_mscratch.ensure(L.off), "pinned scratch");
   CB_TRY(d_mscratch.ensure(L.off), "device scratch");
   uint8_t *h = static_cast<uint8_t *>(h_mscratch.ptr);
   CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
-  int *mm = reinterpret_cast<int *>(h + o_mm);
   IndexRec *upd = reinterpret_cast<IndexRec *>(h + o_upd);
   IndexRec *era = reinterpret_cast<IndexRec *>(h + o_era);
   uint32_t total[kGroups] = {};
   uint64_t grp_bytes[kGroups] = {};
   int base[kGroups] = {};
-  bool dev_only[kGroups] = {true, true, true, true, true};  // no host-memory side in the group
+  bool dev_only[kGroups] = {true, true, true, true, true, true};  // no host-memory side in the group
   int di = 0;
   for (int g = 0; g < kGroups; ++g) {
     uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us[g]);
@@ -370,7 +388,9 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
       const TierMove &m = *grp[g][j];
       const uint64_t src = m.src_tier == kTierDram ? (uint64_t)dram_dev + m.src_off : (uint64_t)pool + m.src_off;
       const uint64_t dst = m.dst_tier == kTierDram ? (uint64_t)dram_dev + m.dst_off : (uint64_t)pool + m.dst_off;
-      if (m.src_dev) {
+      if (g == 5) {
+        desc[di + j] = CopyDesc{src, (uint64_t)d_pack.ptr + pslot[j] + kPackLead, m.size, 0};
+      } else if (m.src_dev) {
         desc[di + j] = CopyDesc{m.src_dev, dst, m.size, 0};  // device -> HBM, already unpacked
       } else {
         desc[di + j] = CopyDesc{src, dst, m.size, kCopyHost | (m.op == kMoveUnpack ? kCopyUnpack : 0)};
@@ -388,9 +408,13 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     us[grp[g].size()] = total[g];
     di += (int)grp[g].size();
   }
-  for (int j = 0; j < npk; ++j) {
-    mm[2 * j] = INT_MAX;
-    mm[2 * j + 1] = INT_MIN;
+  for (size_t o : {o_mm1, o_mm5}) {
+    int *mm = reinterpret_cast<int *>(h + o);
+    const size_t cnt = o == o_mm1 ? grp[1].size() : grp[5].size();
+    for (size_t j = 0; j < cnt; ++j) {
+      mm[2 * j] = INT_MAX;
+      mm[2 * j + 1] = INT_MIN;
+    }
   }
   for (int j = 0; j < nd; ++j) era[j] = IndexRec{dropped[j].lo, dropped[j].hi, 0, 0};
   uint8_t *d = static_cast<uint8_t *>(d_mscratch.ptr);
@@ -411,14 +435,22 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     const CopyDesc *gd = ddesc + base[g];
     const uint32_t *gu = reinterpret_cast<const uint32_t *>(d + o_us[g]);
     const int gn = (int)grp[g].size();
-    if (g == 1) {
+    if (g == 1 || g == 5) {
       CB_TRY(timed(3, grp_bytes[g], gs,
                    [&] {
-                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + o_mm), num_sms, gs,
-                                           g == 2 ? 8 : move_ctas);
+                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + (g == 1 ? o_mm1 : o_mm5)),
+                                           num_sms, gs, g == 5 ? 8 : move_ctas);
                    }),
              "demote pack");
       launches++;  // two kernels
+      if (g == 5) {  // the packed images to the arena by the D2H copy engine
+        for (size_t j = 0; j < grp[5].size(); ++j) {
+          const TierMove &m = *grp[5][j];
+          CB_TRY(cudaMemcpyAsync(dram_host + m.dst_off, static_cast<uint8_t *>(d_pack.ptr) + pslot[j] + kPackLead,
+                                 packed_bytes(m.size), cudaMemcpyDeviceToHost, gs),
+                 "packed demote DMA");
+        }
+      }
     } else {
       // host-link moves on the LSU engine; device-only groups on the store's
       const int engine = dev_only[g] ? copy_engine : 2;
@@ -468,6 +500,7 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
   };
   int rc = launch_group(0, ds);
   if (rc == CB_OK) rc = dma_group(3, ds);
+  if (rc == CB_OK) rc = launch_group(5, ds);
   if (rc == CB_OK) rc = launch_group(1, ds);
   if (concurrent) {
     // join: whatever happens, st waits for the demotions before going on
@@ -772,6 +805,8 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   const size_t o_us = L.add(4ull * (n + 1));
   const size_t o_desc = L.add(sizeof(CopyDesc) * n);
   const size_t o_res = L.add(sizeof(GetResult) * n);
+  const size_t o_udesc = L.add(sizeof(CopyDesc) * n);  // unpacks of DMA'd packed hits
+  const size_t o_uus = L.add(4ull * (n + 1));
   CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
   CB_TRY(d_scratch.ensure(L.off), "device scratch");
   CB_TRY(h_out.ensure(sizeof(GetResult) * n), "pinned out");
@@ -782,31 +817,49 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   // the location the host metadata holds (the engines move each direction at
   // the link rate, and beside the demotions' D2H DMA): the lookup kernel gets
   // a capacity of 0 for them, so it reports them without copying.
+  // Large INT8-packed DRAM hits: their packed bytes come in by DMA to an HBM
+  // staging area and are unpacked there into the caller's buffers.
   uint64_t *dcaps = reinterpret_cast<uint64_t *>(h + o_caps);
   std::vector<int> dma_req;
+  std::vector<uint64_t> pk_slot;  // staging offset per dma_req entry (packed hits)
   uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
-  uint32_t total = 0;
-  uint64_t bytes = 0, dma_bytes = 0;
+  CopyDesc *udesc = reinterpret_cast<CopyDesc *>(h + o_udesc);
+  uint32_t *uus = reinterpret_cast<uint32_t *>(h + o_uus);
+  uint32_t total = 0, utotal = 0;
+  int nu = 0;
+  uint64_t bytes = 0, dma_bytes = 0, ustage = 0;
   for (int i = 0; i < n; ++i) {
     us[i] = total;
     dcaps[i] = caps[i];
     const BlockMeta *m = policy.find(to_hkey(keys + 16 * i));
     if (!m || m->size > caps[i]) continue;
-    if (m->tier == kTierDram && !m->packed && m->size >= kDmaMinBytes) {
-      dma_req.push_back(i);
-      dma_bytes += m->size;
-      dcaps[i] = 0;
-      continue;
+    if (m->tier == kTierDram && m->size >= kDmaMinBytes) {
+      const uint64_t slot = m->packed ? align_up(kPackLead + packed_bytes(m->size), 256) : 0;
+      if (!m->packed || ustage + slot <= kPackStagingBytes) {
+        dma_req.push_back(i);
+        pk_slot.push_back(m->packed ? ustage : UINT64_MAX);
+        ustage += slot;
+        dma_bytes += m->packed ? packed_bytes(m->size) : m->size;
+        dcaps[i] = 0;
+        continue;
+      }
     }
     total += units_of(m->size);
     bytes += m->size;
   }
   us[n] = total;
+  if (ustage) CB_TRY(d_unpack.ensure(ustage), "unpacking staging");  // before any concurrent work
   std::vector<std::pair<uint64_t, uint64_t>> dma_src(dma_req.size());  // (arena offset, size)
   for (size_t j = 0; j < dma_req.size(); ++j) {
     const BlockMeta *m = policy.find(to_hkey(keys + 16 * dma_req[j]));
     dma_src[j] = {Policy::data_offset(*m), m->size};
+    if (pk_slot[j] != UINT64_MAX) {
+      uus[nu] = utotal;
+      udesc[nu++] = CopyDesc{(uint64_t)d_unpack.ptr + pk_slot[j] + kPackLead, outs[dma_req[j]], m->size, kCopyUnpack};
+      utotal += units_of(m->size);
+    }
   }
+  uus[nu] = utotal;
   // LRU touches first (CascadeStore::get touches on hit,
   // src/cascade_core.cpp:1281), so that blocks of this batch are the last
   // victims of the promotions below.
@@ -855,9 +908,17 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
       }
       size_t j = 0;
       while (j < dma_req.size()) {
+        if (pk_slot[j] != UINT64_MAX) {  // packed: its packed image into the staging area
+          CB_TRY(cudaMemcpyAsync(static_cast<uint8_t *>(d_unpack.ptr) + pk_slot[j] + kPackLead,
+                                 dram_host + dma_src[j].first, packed_bytes(dma_src[j].second), cudaMemcpyHostToDevice,
+                                 st),
+                 "packed DRAM hit DMA");
+          ++j;
+          continue;
+        }
         uint64_t run = dma_src[j].second;
         size_t e = j + 1;
-        while (e < dma_req.size() && dma_src[e].first == dma_src[j].first + run &&
+        while (e < dma_req.size() && pk_slot[e] == UINT64_MAX && dma_src[e].first == dma_src[j].first + run &&
                outs[dma_req[e]] == outs[dma_req[j]] + run &&
                one_allocation(reinterpret_cast<const void *>(outs[dma_req[j]]), run + dma_src[e].second)) {
           run += dma_src[e].second;
@@ -873,7 +934,16 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
         prof_pending.push_back(ProfRec{2, dma_bytes, a, b});
       }
     }
-    CB_TRY(cudaMemcpyAsync(d, h, o_desc, cudaMemcpyHostToDevice, st), "H2D get");
+    CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D get");
+    if (nu) {  // the DMA'd packed images, unpacked device to device
+      CB_TRY(timed(2, 0, st,
+                   [&] {
+                     return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_udesc),
+                                              reinterpret_cast<const uint32_t *>(d + o_uus), nu, utotal, 2, d_err,
+                                              num_sms, st);
+                   }),
+             "unpack");
+    }
     LookupArgs a;
     a.table = table;
     a.mask = table_slots - 1;

@@ -139,6 +139,8 @@ struct Store {
   cudaEvent_t ev_move_in = nullptr, ev_move_done = nullptr;
   PinnedBuf h_mscratch;  // descriptors of run_moves (separate from the callers')
   DevBuf d_mscratch;
+  DevBuf d_pack;    // packed images of large demotions, on their way to DRAM by DMA
+  DevBuf d_unpack;  // packed DRAM hits of a get, brought in by DMA to be unpacked
   // pg/copies_done: the blocks are still arriving on copy_stream (see
   // put_host); the hash kernel waits per segment and later work on st waits
   // for copies_done.
