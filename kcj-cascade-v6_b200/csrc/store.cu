@@ -408,10 +408,10 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     us[grp[g].size()] = total[g];
     di += (int)grp[g].size();
   }
-  for (size_t o : {o_mm1, o_mm5}) {
-    int *mm = reinterpret_cast<int *>(h + o);
-    const size_t cnt = o == o_mm1 ? grp[1].size() : grp[5].size();
-    for (size_t j = 0; j < cnt; ++j) {
+  // (an empty group's region has the next one's offset: pair each with its count)
+  for (const auto &oc : {std::make_pair(o_mm1, grp[1].size()), std::make_pair(o_mm5, grp[5].size())}) {
+    int *mm = reinterpret_cast<int *>(h + oc.first);
+    for (size_t j = 0; j < oc.second; ++j) {
       mm[2 * j] = INT_MAX;
       mm[2 * j + 1] = INT_MIN;
     }
