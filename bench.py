@@ -814,12 +814,12 @@ def spill_main(args, rank, world, local, device):
         "get_phase": {"local_gpu_hits": dd(s2, s3, "local_gpu_hits"), "local_dram_hits": dd(s2, s3, "local_dram_hits"),
                       "promotions": dd(s2, s3, "promotions_to_local"), "tier_moved_gb": round(pr_b / 1e9, 2),
                       "tier_kernel_gbs": round(pr_b / pr_ns, 2) if pr_ns else None},
-        "roofline": {"kernel": ("kv_minmax + kv_pack (INT8 into mapped pinned host)" if args.kv_compression
-                                else "copy_lsu (mapped pinned host)"), "bound": "host link",
+        "roofline": {"kernel": ("kv_minmax + kv_pack into HBM staging, then the D2H copy engine" if args.kv_compression
+                                else "D2H copy engine (cudaMemcpyAsync of 5 MiB blocks)"), "bound": "host link",
                      "achieved": round(link_b / ev_ns, 2) if ev_ns else None,
                      "peak": round(peaks["d2h"], 2), "unit": "GB/s",
                      "frac": round((link_b / ev_ns) / peaks["d2h"], 4) if ev_ns else None,
-                     "achieved_is": "host-link bytes of the demotions / their kernel time",
+                     "achieved_is": "host-link bytes of the demotions / their device time (CUDA events)",
                      "peak_source": "measured pinned D2H copy in this run", "h2d_peak": round(peaks["h2d"], 2)},
         "gpu_launches": dd(s2, s3, "kernel_launches"), "clocks": clk.summary(),
     }

@@ -436,21 +436,23 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
     const uint32_t *gu = reinterpret_cast<const uint32_t *>(d + o_us[g]);
     const int gn = (int)grp[g].size();
     if (g == 1 || g == 5) {
+      // group 5: the timed span covers the packing and the D2H copies of the
+      // packed images to the arena, i.e. the whole move
       CB_TRY(timed(3, grp_bytes[g], gs,
                    [&] {
-                     return launch_kv_pack(gd, gu, gn, total[g], reinterpret_cast<int *>(d + (g == 1 ? o_mm1 : o_mm5)),
-                                           num_sms, gs, g == 5 ? 8 : move_ctas);
+                     cudaError_t e = launch_kv_pack(gd, gu, gn, total[g],
+                                                    reinterpret_cast<int *>(d + (g == 1 ? o_mm1 : o_mm5)), num_sms,
+                                                    gs, g == 5 ? 8 : move_ctas);
+                     for (size_t j = 0; g == 5 && e == cudaSuccess && j < grp[5].size(); ++j) {
+                       const TierMove &m = *grp[5][j];
+                       e = cudaMemcpyAsync(dram_host + m.dst_off,
+                                           static_cast<uint8_t *>(d_pack.ptr) + pslot[j] + kPackLead,
+                                           packed_bytes(m.size), cudaMemcpyDeviceToHost, gs);
+                     }
+                     return e;
                    }),
              "demote pack");
       launches++;  // two kernels
-      if (g == 5) {  // the packed images to the arena by the D2H copy engine
-        for (size_t j = 0; j < grp[5].size(); ++j) {
-          const TierMove &m = *grp[5][j];
-          CB_TRY(cudaMemcpyAsync(dram_host + m.dst_off, static_cast<uint8_t *>(d_pack.ptr) + pslot[j] + kPackLead,
-                                 packed_bytes(m.size), cudaMemcpyDeviceToHost, gs),
-                 "packed demote DMA");
-        }
-      }
     } else {
       // host-link moves on the LSU engine; device-only groups on the store's
       const int engine = dev_only[g] ? copy_engine : 2;
