@@ -950,8 +950,9 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
       }
       int e = i + 1;
       uint64_t run = sizes_out[i];
+      const AddrRange rg = e < n ? alloc_range(outs[i]) : AddrRange{0, 0};
       while (e < n && copied(e) && dst[e] - dst[i] == run && dst[e] - dst[e - 1] == sizes_out[e - 1] &&
-             static_cast<uint8_t *>(outs[i]) + run == outs[e] && one_allocation(outs[i], run + sizes_out[e])) {
+             static_cast<uint8_t *>(outs[i]) + run == outs[e] && rg.holds(outs[i], run + sizes_out[e])) {
         run += sizes_out[e];
         ++e;
       }

@@ -63,20 +63,20 @@ PtrAttrFn pointer_attribute_fn() {
 }
 }  // namespace
 
-bool one_allocation(const void *p, uint64_t bytes) {
+AddrRange alloc_range(const void *p) {
+  const uint64_t a = reinterpret_cast<uint64_t>(p);
   const PtrAttrFn fn = pointer_attribute_fn();
-  if (!fn) return false;
+  if (!fn) return AddrRange{a, a};
   CUdeviceptr start = 0;
   size_t size = 0;
-  const CUdeviceptr a = reinterpret_cast<CUdeviceptr>(p);
-  if (fn(&start, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, a) != CUDA_SUCCESS) {
+  if (fn(&start, CU_POINTER_ATTRIBUTE_RANGE_START_ADDR, static_cast<CUdeviceptr>(a)) != CUDA_SUCCESS) {
     cudaPointerAttributes at;
     const bool known = cudaPointerGetAttributes(&at, p) == cudaSuccess && at.type != cudaMemoryTypeUnregistered;
     cudaGetLastError();
-    return !known;  // pageable host memory: any extent
+    return known ? AddrRange{a, a} : AddrRange{0, UINT64_MAX};  // pageable host memory: any extent
   }
-  if (fn(&size, CU_POINTER_ATTRIBUTE_RANGE_SIZE, a) != CUDA_SUCCESS) return false;
-  return a >= start && a - start + bytes <= size;
+  if (fn(&size, CU_POINTER_ATTRIBUTE_RANGE_SIZE, static_cast<CUdeviceptr>(a)) != CUDA_SUCCESS) return AddrRange{a, a};
+  return AddrRange{static_cast<uint64_t>(start), static_cast<uint64_t>(start) + size};
 }
 
 // ------------------------------------------------------------ buffers
@@ -726,9 +726,10 @@ int Store::put_host(const void *const *ptrs, const uint64_t *sizes, const uint8_
     while (k < j) {
       int e = k + 1;
       uint64_t run = sizes[k];
+      const AddrRange rg = e < j ? alloc_range(ptrs[k]) : AddrRange{0, 0};
       while (e < j && static_cast<const uint8_t *>(ptrs[k]) + (dptrs[e - i] - dptrs[k - i]) == ptrs[e] &&
              dptrs[e - i] - dptrs[e - 1 - i] == sizes[e - 1] &&
-             one_allocation(ptrs[k], dptrs[e - i] - dptrs[k - i] + sizes[e])) {
+             rg.holds(ptrs[k], dptrs[e - i] - dptrs[k - i] + sizes[e])) {
         run = dptrs[e - i] - dptrs[k - i] + sizes[e];
         ++e;
       }
@@ -920,9 +921,10 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
         }
         uint64_t run = dma_src[j].second;
         size_t e = j + 1;
+        const void *o0 = reinterpret_cast<const void *>(outs[dma_req[j]]);
+        const AddrRange rg = e < dma_req.size() ? alloc_range(o0) : AddrRange{0, 0};
         while (e < dma_req.size() && pk_slot[e] == UINT64_MAX && dma_src[e].first == dma_src[j].first + run &&
-               outs[dma_req[e]] == outs[dma_req[j]] + run &&
-               one_allocation(reinterpret_cast<const void *>(outs[dma_req[j]]), run + dma_src[e].second)) {
+               outs[dma_req[e]] == outs[dma_req[j]] + run && rg.holds(o0, run + dma_src[e].second)) {
           run += dma_src[e].second;
           ++e;
         }
@@ -1046,10 +1048,11 @@ int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_
       }
       int e = k + 1;
       uint64_t run = sizes_out[k];
+      const AddrRange rg = e < j ? alloc_range(outs[k]) : AddrRange{0, 0};
       while (e < j && (found_out[e] & 0x0f) != CB_FOUND_MISS && sizes_out[e] <= caps[e] &&
              static_cast<uint8_t *>(outs[k]) + (dptrs[e - i] - dptrs[k - i]) == outs[e] &&
              dptrs[e - i] - dptrs[e - 1 - i] == sizes_out[e - 1] &&
-             one_allocation(outs[k], dptrs[e - i] - dptrs[k - i] + sizes_out[e])) {
+             rg.holds(outs[k], dptrs[e - i] - dptrs[k - i] + sizes_out[e])) {
         run = dptrs[e - i] - dptrs[k - i] + sizes_out[e];
         ++e;
       }

@@ -205,12 +205,21 @@ struct Store {
 
 inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
 
-// True when one copy may cover [p, p + bytes): the range lies inside a single
-// CUDA allocation (device, pinned or managed), or p is memory CUDA does not
-// know (pageable host memory, copied through staging whatever its extent).
-// Neighbouring caller buffers can be adjacent in the address space yet belong
-// to different allocations; a copy must not span them.
-bool one_allocation(const void *p, uint64_t bytes);
+// The address range one copy starting at p may cover: the CUDA allocation
+// that contains p (device, pinned or managed), or everything when p is memory
+// CUDA does not know (pageable host memory, copied through staging whatever
+// its extent). Neighbouring caller buffers can be adjacent in the address
+// space yet belong to different allocations; a copy must not span them.
+// Returns [p, p) when the range cannot be determined.
+struct AddrRange {
+  uint64_t lo, hi;
+  bool holds(const void *p, uint64_t bytes) const {
+    const uint64_t a = reinterpret_cast<uint64_t>(p);
+    return a >= lo && a <= hi && bytes <= hi - a;
+  }
+};
+AddrRange alloc_range(const void *p);
+inline bool one_allocation(const void *p, uint64_t bytes) { return alloc_range(p).holds(p, bytes); }
 
 inline HKey to_hkey(const uint8_t *p) {
   HKey k;
