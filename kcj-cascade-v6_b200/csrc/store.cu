@@ -1,7 +1,11 @@
 // The B200 store behind the C ABI: one HBM slab pool + device index per GPU,
 // an optional pinned DRAM arena, and the host policy. Every batch becomes a
 // handful of launches: SHA-256 -> (host dedup/placement plan) -> tier moves ->
-// scatter -> index mutations for put; index lookup -> gather for get.
+// scatter -> index mutations for put; index lookup -> gather for get (with
+// the promotions of DRAM hits planned before the lookup, their room-making
+// demotions on a second stream). Moves between HBM and the pinned arena of
+// blocks >= 256 KiB use the copy engines (INT8-packed ones through an HBM
+// staging area); smaller ones use the copy kernels on the mapped arena.
 //
 // Reference call stacks this replaces:
 //   put  : DistributedStore::put (src/distributed_backend.cpp:601-692) ->
