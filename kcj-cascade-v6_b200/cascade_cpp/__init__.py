@@ -576,7 +576,8 @@ class _StoreBase:
         kernel either), or None for a miss (and for a DRAM-tier block that
         could not be promoted). Each view pins its block (never evicted or
         moved) until ``release_views`` is called for that ID. Views are
-        read-only by contract: a block is its content hash."""
+        read-only by contract: a block is its content hash, and they alias
+        memory the store owns: drop them before ``close()``."""
         keys = self._keys(ids)
         n = len(keys)
         addrs = np.zeros(n, np.uint64)
