@@ -52,3 +52,43 @@ def test_odd_size_drops_last_byte():
     comp = KQ.compress(a)
     assert len(comp) == 8 + 50
     assert len(KQ.decompress(comp, 101)) == 100
+
+
+def _reference_module():
+    import os
+    import sys
+    here = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    ref = os.path.join(here, "oracle", "_ref")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    try:
+        import cascade_ref  # the reference, compiled from its sources (oracle/Makefile)
+    except ImportError:
+        return None
+    return cascade_ref if hasattr(cascade_ref, "kv_compress") else None
+
+
+def test_oracle_matches_compiled_reference_on_random_blocks():
+    ref = _reference_module()
+    if ref is None:
+        pytest.skip("oracle/_ref (the compiled reference) is not built here")
+    rng = np.random.default_rng(2026)
+    for t in range(300):
+        kind = t % 5
+        n = int(rng.integers(32, 3000))
+        if kind == 0:
+            a = rng.standard_normal(n).astype(np.float16).view(np.uint8)
+        elif kind == 1:
+            a = (rng.standard_normal(n) * 10 ** rng.uniform(-4, 4)).astype(np.float16).view(np.uint8)
+        elif kind == 2:
+            a = rng.integers(-32768, 32768, n, dtype=np.int64).astype(np.int16).view(np.uint8)
+        elif kind == 3:
+            a = rng.integers(0, 256, 2 * n + int(rng.integers(0, 2)), dtype=np.uint8)
+        else:
+            lo = int(rng.integers(-32768, 32767))
+            a = rng.integers(lo, min(32768, lo + int(rng.integers(1, 600))), n).astype(np.int16).view(np.uint8)
+        a = np.ascontiguousarray(a)
+        comp = ref.kv_compress(a)
+        assert KQ.compress(a) == comp, (t, kind, a.size)
+        ok, dec = ref.kv_decompress(np.frombuffer(comp, np.uint8), a.size)
+        assert ok and KQ.decompress(comp, a.size) == dec, (t, kind, a.size)
