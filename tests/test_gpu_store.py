@@ -358,3 +358,29 @@ def test_config2_slice_device_roundtrip():
         assert all(found)
         want = torch.stack([blocks[j] for j in sel])
         assert torch.equal(outs.view(len(sel), size), want)
+
+
+@pytest.mark.parametrize("buffers", ["numpy", "pinned_views", "pinned_separate"])
+def test_dram_hits_into_host_buffers(buffers):
+    """Large plain DRAM-tier blocks (copied by the copy engines) read into
+    host memory: pageable numpy arrays, views of one pinned buffer (runs
+    merged into one copy), and separate pinned tensors (never merged across
+    allocations). Bytes must equal what was put."""
+    S = 1 << 20
+    blocks = [W.kv_block_fp16(4000 + i, S) for i in range(12)]
+    store = make_store(hbm=16 * S, dram=64 * S)
+    ids = store.batch_put([torch.from_numpy(b).to(DEV) for b in blocks])
+    store.evict(16 * S)
+    assert not any(store.locate(i).is_gpu for i in ids)
+    if buffers == "numpy":
+        outs = [np.empty(S, np.uint8) for _ in ids]
+    elif buffers == "pinned_views":
+        big = torch.empty(len(ids) * S, dtype=torch.uint8, pin_memory=True)
+        outs = [big[k * S:(k + 1) * S] for k in range(len(ids))]
+    else:
+        outs = [torch.empty(S, dtype=torch.uint8, pin_memory=True) for _ in ids]
+    found, sizes = store.batch_get(ids, outs)
+    assert all(found) and sizes == [S] * len(ids)
+    for o, b in zip(outs, blocks):
+        got = o if isinstance(o, np.ndarray) else o.numpy()
+        assert np.array_equal(got, b)
