@@ -44,3 +44,11 @@ def test_new_config_fields_reach_the_c_struct():
     cfg = cascade_cpp.DistributedConfig()
     assert cfg.kv_compression is False and cfg.prefix_replication is True
     assert cfg.collective_timeout_ms == 0
+
+
+def test_connector_rejects_non_cuda_caches():
+    from cascade_cpp.connector import KVPageConnector
+    with pytest.raises(TypeError):
+        KVPageConnector(None, torch.zeros(4, 16))
+    with pytest.raises(TypeError):
+        KVPageConnector(None, np.zeros((4, 16)))
