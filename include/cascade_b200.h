@@ -219,13 +219,19 @@ int cb_sync(cb_store *s);
  *      src/distributed_backend.cpp:303-514, and the metadata replication of
  *      sync_metadata, :1323-1382) ------------------------------------------ */
 
-/* Failure-path self-tests that fault, trap or hang nothing: each makes one
- * of the store's bounded device waits run out on purpose and returns the
- * status a caller would see; the store stays usable afterwards.
+/* Failure-path self-tests that fault, trap or hang nothing.
  * CB_SELFTEST_HASH_WAIT: a hash whose input is announced as still arriving
  * but never published; the kernel's bounded poll gives up after ~1 ms and
- * the call returns CB_ERR_TIMEOUT. */
+ * the call returns CB_ERR_TIMEOUT; the store stays usable afterwards.
+ * CB_SELFTEST_FAIL_MOVES: arms a host-side failure of the next tier-move
+ * plan, before any of its copies is issued (as a failed pinned-arena
+ * allocation would). The call that planned the moves returns
+ * CB_ERR_NOSPACE; its planned placements are no longer backed by memory,
+ * so every later put/get/contains/locate/evict/view call returns
+ * CB_ERR_STATE until cb_clear() empties the store. Any failure of a call
+ * after its batch was planned puts the store in that state. */
 #define CB_SELFTEST_HASH_WAIT 1
+#define CB_SELFTEST_FAIL_MOVES 2
 int cb_selftest(cb_store *s, int32_t which);
 
 /* Size of the opaque NCCL unique id blob. */

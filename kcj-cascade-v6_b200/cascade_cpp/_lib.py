@@ -22,6 +22,7 @@ CB_ERR_NCCL = 6
 CB_ERR_STATE = 7
 CB_ERR_DEVICE = 8
 CB_SELFTEST_HASH_WAIT = 1
+CB_SELFTEST_FAIL_MOVES = 2
 
 CB_MEM_DEVICE = 0
 CB_MEM_HOST = 1

@@ -216,15 +216,24 @@ int Store::dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_rec
   const int W = dht->W;
   int rc = dht_nccl(ncclGroupStart(), "ncclGroupStart");
   if (rc) return rc;
+  // Inside the group the calls only enqueue (completion is checked at
+  // ncclGroupEnd); a failed enqueue still closes the group, so no NCCL group
+  // stays open on this thread for the caller's next NCCL call.
+  auto enqueued = [&](ncclResult_t r, const char *what) -> int {
+    if (r == ncclSuccess || r == ncclInProgress) return CB_OK;
+    ncclGroupEnd();
+    return fail(CB_ERR_NCCL, "%s: %s", what, ncclGetErrorString(r));
+  };
   size_t so = 0, ro = 0;
   for (int r = 0; r < W; ++r) {
     if (scount[r]) {
-      rc = dht_nccl(ncclSend(static_cast<const uint8_t *>(d_send) + so, scount[r] * rec, ncclUint8, r, dht->comm, st),
-                    "ncclSend");
+      rc = enqueued(
+          ncclSend(static_cast<const uint8_t *>(d_send) + so, scount[r] * rec, ncclUint8, r, dht->comm, st),
+          "ncclSend");
       if (rc) return rc;
     }
     if (rcount[r]) {
-      rc = dht_nccl(ncclRecv(static_cast<uint8_t *>(d_recv) + ro, rcount[r] * rec, ncclUint8, r, dht->comm, st),
+      rc = enqueued(ncclRecv(static_cast<uint8_t *>(d_recv) + ro, rcount[r] * rec, ncclUint8, r, dht->comm, st),
                     "ncclRecv");
       if (rc) return rc;
     }
@@ -235,7 +244,7 @@ int Store::dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_rec
 }
 
 int Store::dht_barrier() {
-  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
   int rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, own_stream),
                     "ncclAllReduce(barrier)");
@@ -362,7 +371,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
                    const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out, uint8_t *status_out,
                    cudaStream_t st) {
   Trace tr("cb.dht_put");
-  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   const int W = dht->W, me = dht->me;
   // 0. device addresses of the blocks (host blocks: one staging area)
   std::vector<uint64_t> dptr(n);
@@ -445,6 +454,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   if (rc) return rc;
   PutPlan &plan = put_plan;
   policy.plan_put(okeys.data(), osizes.data(), oprefix.data(), (int)nrecv, cfg.dedup_enabled != 0, plan);
+  plan_open = true;
   rc = run_moves(plan.moves, plan.dropped, st);
   if (rc) {
     policy.commit();
@@ -579,7 +589,7 @@ struct PrefixRec {
 // before every reader is done.
 int Store::dht_sync_prefixes(cudaStream_t st) {
   Trace tr("cb.dht_sync_prefixes");
-  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   const int W = dht->W, me = dht->me;
   std::vector<PrefixRec> mine;
   policy.for_each([&](const HKey &k, const BlockMeta &m) {
@@ -747,7 +757,7 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
 int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps, int mem_kind,
                    uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st) {
   Trace tr("cb.dht_get");
-  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   const int me = dht->me;
   // Replica hits are served from local HBM. Other keys repeated inside the
   // batch (hot keys under a skewed access pattern) are looked up and fetched
@@ -967,7 +977,7 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
 }
 
 int Store::dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st) {
-  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   std::vector<uint64_t> reps;
   std::vector<int> owner;
   int rc = dht_lookup(keys, n, reps, owner, st);
@@ -979,7 +989,7 @@ int Store::dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStre
 // One-sided probe of the owner's index through its peer mapping (locate is
 // not collective in the reference either: it reads local metadata).
 int Store::dht_locate(const uint8_t *key, cb_location *out, int32_t *found) {
-  if (!dht) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   const HKey k = to_hkey(key);
   const int o = (int)be_owner(k, dht->W);
   CB_TRY_CUDA(h_scratch.ensure(64), "pinned");
@@ -1010,7 +1020,7 @@ int Store::dht_locate(const uint8_t *key, cb_location *out, int32_t *found) {
 }
 
 int Store::dht_cluster_usage(cb_stats *o) {
-  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached");
+  if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   CB_TRY_CUDA(dht->h_misc.ensure(64), "pinned");
   CB_TRY_CUDA(dht->d_misc.ensure(64), "device");
   uint64_t *h = static_cast<uint64_t *>(dht->h_misc.ptr);

@@ -208,15 +208,23 @@ Store::~Store() {
   if (own_stream) cudaStreamDestroy(own_stream);
 }
 
+// The new index is allocated and cleared before the old one is released, so
+// a growth that fails leaves the store on its previous, still valid index.
 cudaError_t Store::alloc_table(uint64_t slots) {
-  if (table) cudaFree(table);
-  table = nullptr;
-  cudaError_t e = cudaMalloc(&table, slots * sizeof(Slot));
+  Slot *t = nullptr;
+  cudaError_t e = cudaMalloc(&t, slots * sizeof(Slot));
   if (e != cudaSuccess) return e;
+  e = cudaMemset(t, 0, slots * sizeof(Slot));
+  if (e != cudaSuccess) {
+    cudaFree(t);
+    return e;
+  }
+  if (table) cudaFree(table);
+  table = t;
   table_slots = slots;
   table_used = 0;
   table_tombs = 0;
-  return cudaMemset(table, 0, slots * sizeof(Slot));
+  return cudaSuccess;
 }
 
 cudaError_t Store::ensure_dram() {
@@ -328,6 +336,10 @@ int Store::run_moves(const std::vector<TierMove> &moves, const std::vector<HKey>
                      const std::function<int()> &concurrent) {
   Trace tr("cb.tier_moves");
   if (moves.empty() && dropped.empty()) return concurrent ? concurrent() : CB_OK;
+  if (fake_move_failures > 0) {  // before any copy is issued, like a failed arena allocation
+    --fake_move_failures;
+    return fail(CB_ERR_NOSPACE, "injected tier-move failure (self-test)");
+  }
   bool need_dram = false;
   for (const auto &m : moves) need_dram |= (m.src_tier == kTierDram || m.dst_tier == kTierDram);
   if (need_dram) {
@@ -600,6 +612,7 @@ int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t
   if (rc) return rc;
   PutPlan &plan = put_plan;
   policy.plan_put(keys.data(), sizes, is_prefix, n, cfg.dedup_enabled != 0, plan);
+  plan_open = true;
   rc = run_moves(plan.moves, plan.dropped, st);
   if (rc) return rc;
 
@@ -903,6 +916,7 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
       if (it != copy_of.end()) mv.src_dev = it->second;
     }
     planned = !order.empty();
+    plan_open |= planned;
   }
   uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
   auto lookup_and_gather = [&]() -> int {
@@ -1080,6 +1094,10 @@ int Store::get_host(const uint8_t *keys, int n, void *const *outs, const uint64_
 // leaves; the host reads the error word and reports CB_ERR_TIMEOUT. Nothing
 // faults or hangs and the context stays usable.
 int Store::selftest(int which, cudaStream_t st) {
+  if (which == CB_SELFTEST_FAIL_MOVES) {
+    fake_move_failures = 1;
+    return CB_OK;
+  }
   if (which != CB_SELFTEST_HASH_WAIT) return fail(CB_ERR_ARG, "unknown self-test %d", which);
   constexpr uint64_t kBytes = 1 << 20;
   CB_TRY(cudaStreamSynchronize(copy_stream), "copy stream");
@@ -1114,6 +1132,7 @@ int Store::get_views(const uint8_t *keys, int n, uint64_t *addrs_out, uint64_t *
       planned = true;
     }
   }
+  plan_open |= planned;
   int rc = run_moves(moves, dropped, st);
   if (planned) policy.commit();
   if (rc) return rc;
@@ -1227,6 +1246,7 @@ int Store::evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st) {
   std::vector<TierMove> moves;
   std::vector<HKey> dropped;
   const uint64_t freed = policy.plan_evict(bytes, moves, dropped);
+  plan_open |= !moves.empty() || !dropped.empty();
   int rc = run_moves(moves, dropped, st);
   policy.commit();
   if (rc) return rc;
@@ -1248,6 +1268,8 @@ int Store::clear(cudaStream_t st) {
   CB_TRY(cudaMemsetAsync(table, 0, table_slots * sizeof(Slot), st), "index clear");
   CB_TRY(cudaStreamSynchronize(st), "sync");
   table_used = table_tombs = 0;
+  lost.clear();  // metadata and memory agree again: both are empty
+  fake_move_failures = 0;
   local_gpu_hits = local_dram_hits = remote_gpu_hits = remote_dram_hits = misses = 0;
   remote_dedup_hits = remote_dedup_bytes = 0;
   replica_promotions = 0;
@@ -1317,20 +1339,31 @@ cudaStream_t pick_stream(Store *s, void *stream) {
   return stream ? static_cast<cudaStream_t>(stream) : s->own_stream;
 }
 
+// kData calls read or change stored blocks: they are refused once a call
+// failed after planning (Store::lost) until clear(). kAny calls (hashing,
+// statistics, clear, releases, barriers) run in that state too.
+enum Access { kData, kAny };
+
 template <class F>
-int guarded(cb_store *h, F f) {
+int guarded(cb_store *h, F f, Access access = kData) {
   if (!h || !h->s) return CB_ERR_ARG;
   Store *s = h->s;
   std::lock_guard<std::mutex> g(s->mu);
+  if (access == kData && !s->lost.empty())
+    return s->fail(CB_ERR_STATE, "store state lost after a failed call (%s); clear() resets it", s->lost.c_str());
+  s->plan_open = false;
+  int rc;
   try {
     cudaError_t e = cudaSetDevice(s->device);
-    if (e != cudaSuccess) return s->cuda_fail(e, "cudaSetDevice");
-    return f(s);
+    rc = e != cudaSuccess ? s->cuda_fail(e, "cudaSetDevice") : f(s);
   } catch (const std::bad_alloc &) {
-    return s->fail(CB_ERR_NOSPACE, "host allocation failed");
+    rc = s->fail(CB_ERR_NOSPACE, "host allocation failed");
   } catch (const std::exception &ex) {
-    return s->fail(CB_ERR_STATE, "%s", ex.what());
+    rc = s->fail(CB_ERR_STATE, "%s", ex.what());
   }
+  if (rc != CB_OK && s->plan_open && s->lost.empty()) s->lost = s->last_error;
+  s->plan_open = false;
+  return rc;
 }
 
 }  // namespace
@@ -1385,7 +1418,7 @@ const char *cb_last_error(const cb_store *h) {
 }
 
 int cb_selftest(cb_store *h, int32_t which) {
-  return guarded(h, [&](Store *s) -> int { return s->selftest(which, s->own_stream); });
+  return guarded(h, [&](Store *s) -> int { return s->selftest(which, s->own_stream); }, kAny);
 }
 
 int cb_get_views(cb_store *h, const uint8_t *keys, int32_t n, uint64_t *addrs_out, uint64_t *sizes_out,
@@ -1402,7 +1435,7 @@ int cb_release_views(cb_store *h, const uint8_t *keys, int32_t n) {
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && !keys)) return s->fail(CB_ERR_ARG, "bad arguments");
     return s->release_views(keys, n);
-  });
+  }, kAny);
 }
 
 int cb_kv_compress_batch(cb_store *h, const void *const *srcs, const uint64_t *sizes, void *const *dsts,
@@ -1416,7 +1449,7 @@ int cb_kv_compress_batch(cb_store *h, const void *const *srcs, const uint64_t *s
       dst[i] = (uint64_t)dsts[i];
     }
     return s->kv_compress(src.data(), sizes, dst.data(), n, pick_stream(s, stream));
-  });
+  }, kAny);
 }
 
 int cb_kv_decompress_batch(cb_store *h, const void *const *srcs, const uint64_t *comp_sizes,
@@ -1431,13 +1464,14 @@ int cb_kv_decompress_batch(cb_store *h, const void *const *srcs, const uint64_t 
       dst[i] = (uint64_t)dsts[i];
     }
     return s->kv_decompress(src.data(), comp_sizes, orig_sizes, dst.data(), n, ok_out, pick_stream(s, stream));
-  });
+  }, kAny);
 }
 
 int cb_hash_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, int32_t n,
                   int32_t mem_kind, uint8_t *digests_out, void *stream) {
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && (!ptrs || !sizes || !digests_out))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (mem_kind != CB_MEM_DEVICE && mem_kind != CB_MEM_HOST) return s->fail(CB_ERR_ARG, "unknown mem_kind %d", mem_kind);
     if (n == 0) return CB_OK;
     cudaStream_t st = pick_stream(s, stream);
     if (mem_kind == CB_MEM_DEVICE) {
@@ -1474,7 +1508,7 @@ int cb_hash_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, i
       i = j;
     }
     return CB_OK;
-  });
+  }, kAny);
 }
 
 int cb_put_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
@@ -1482,6 +1516,7 @@ int cb_put_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, co
                  uint8_t *status_out, void *stream) {
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && (!ptrs || !sizes))) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (mem_kind != CB_MEM_DEVICE && mem_kind != CB_MEM_HOST) return s->fail(CB_ERR_ARG, "unknown mem_kind %d", mem_kind);
     for (int i = 0; i < n; ++i)
       if (sizes[i] > cb::kSizeMask) return s->fail(CB_ERR_ARG, "block %d too large", i);
     cudaStream_t st = pick_stream(s, stream);
@@ -1500,6 +1535,7 @@ int cb_get_batch(cb_store *h, const uint8_t *keys, int32_t n, void *const *outs,
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && (!keys || !outs || !out_caps || !sizes_out || !found_out)))
       return s->fail(CB_ERR_ARG, "bad arguments");
+    if (mem_kind != CB_MEM_DEVICE && mem_kind != CB_MEM_HOST) return s->fail(CB_ERR_ARG, "unknown mem_kind %d", mem_kind);
     cudaStream_t st = pick_stream(s, stream);
     if (s->world > 1) return s->dht_get(keys, n, outs, out_caps, mem_kind, sizes_out, found_out, st);
     if (n == 0) return CB_OK;
@@ -1548,11 +1584,11 @@ int cb_get_stats(cb_store *h, cb_stats *out) {
     s->fill_stats(out);
     if (s->world > 1) return s->dht_cluster_usage(out);
     return CB_OK;
-  });
+  }, kAny);
 }
 
 int cb_clear(cb_store *h) {
-  return guarded(h, [&](Store *s) -> int { return s->clear(s->own_stream); });
+  return guarded(h, [&](Store *s) -> int { return s->clear(s->own_stream); }, kAny);
 }
 
 int cb_sync(cb_store *h) {
@@ -1560,14 +1596,14 @@ int cb_sync(cb_store *h) {
     cudaError_t e = cudaStreamSynchronize(s->own_stream);
     if (e != cudaSuccess) return s->cuda_fail(e, "sync");
     return CB_OK;
-  });
+  }, kAny);
 }
 
 int cb_dht_attach(cb_store *h, int32_t rank, int32_t world, const uint8_t *uid) {
   return guarded(h, [&](Store *s) -> int {
     if (!uid) return s->fail(CB_ERR_ARG, "bad arguments");
     return s->dht_attach(rank, world, uid);
-  });
+  }, kAny);
 }
 
 int cb_sync_metadata(cb_store *h) {
@@ -1578,7 +1614,7 @@ int cb_sync_metadata(cb_store *h) {
 }
 
 int cb_dht_barrier(cb_store *h) {
-  return guarded(h, [&](Store *s) -> int { return s->world > 1 ? s->dht_barrier() : CB_OK; });
+  return guarded(h, [&](Store *s) -> int { return s->world > 1 ? s->dht_barrier() : CB_OK; }, kAny);
 }
 
 int32_t cb_owner_rank(const uint8_t *key, int32_t world) {

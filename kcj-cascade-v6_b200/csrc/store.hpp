@@ -78,6 +78,13 @@ struct Store {
   PutPlan put_plan;
   std::mutex mu;
   std::string last_error;
+  // The host metadata records a batch's placements and tier moves when the
+  // batch is planned. A call that fails after planning (plan_open still set
+  // when it returns) may leave metadata that its memory does not match, so
+  // the store refuses data calls (`lost` holds the first error) until clear().
+  bool plan_open = false;
+  std::string lost;
+  int fake_move_failures = 0;  // CB_SELFTEST_FAIL_MOVES: host-side injection
 
   uint64_t local_gpu_hits = 0, local_dram_hits = 0, remote_gpu_hits = 0, remote_dram_hits = 0,
            misses = 0, remote_dedup_hits = 0, remote_dedup_bytes = 0;

@@ -52,6 +52,21 @@ def test_ctypes_signatures_cover_header():
     assert sorted(n for n, _, _ in L.SIGNATURES) == header_functions()
 
 
+def test_constants_match_header():
+    # every integer #define of the header has the same value in the ctypes layer
+    headers = [HEADER] + [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include"))
+                          if f.endswith(".h") and f != os.path.basename(HEADER)]
+    defs = {}
+    for h in headers:
+        for name, val in re.findall(r"^#define\s+(CB_\w+)\s+(0x[0-9A-Fa-f]+|\d+)\b", open(h).read(), re.M):
+            defs[name] = int(val, 0)
+    assert len(defs) >= 24
+    missing = [k for k in defs if not hasattr(L, k)]
+    assert not missing, missing
+    wrong = {k: (v, getattr(L, k)) for k, v in defs.items() if getattr(L, k) != v}
+    assert not wrong, wrong
+
+
 def test_struct_layouts_match_c(tmp_path):
     # every field of every ABI struct: the ctypes mirror's offset must be the
     # C compiler's offsetof, and the sizes must agree
