@@ -52,3 +52,31 @@ def test_connector_rejects_non_cuda_caches():
         KVPageConnector(None, torch.zeros(4, 16))
     with pytest.raises(TypeError):
         KVPageConnector(None, np.zeros((4, 16)))
+
+
+def test_hex_ids_parse_to_their_bytes():
+    rng = np.random.default_rng(21)
+    for _ in range(64):
+        k = rng.integers(0, 256, 16, dtype=np.uint8).tobytes()
+        bid = k.hex()
+        assert cascade_cpp.block_id_to_key(bid) == k
+        assert cascade_cpp.key_to_block_id(cascade_cpp.block_id_to_key(bid)) == bid
+
+
+def test_other_ids_are_hashed_deterministically_and_distinctly():
+    lower = "0123456789abcdef0123456789abcdef"
+    others = [lower.upper(), lower[:-1], lower + "0", "", "block-7", "blöck-7", "block-8"]
+    keys = [cascade_cpp.block_id_to_key(s) for s in others]
+    assert all(len(k) == 16 for k in keys)
+    assert keys == [cascade_cpp.block_id_to_key(s) for s in others]  # deterministic
+    assert len(set(keys)) == len(keys)
+    assert cascade_cpp.block_id_to_key(lower) not in keys  # hex parse and string hash stay apart
+
+
+def test_owner_rank_matches_oracle_rule():
+    from oracle.dht_oracle import owner
+    rng = np.random.default_rng(22)
+    ids = [rng.integers(0, 256, 16, dtype=np.uint8).tobytes().hex() for _ in range(256)]
+    ids += ["ff" * 16, "00" * 16, "80" + "00" * 15]
+    for world in (1, 2, 3, 4, 7, 8):
+        assert [cascade_cpp.owner_rank(b, world) for b in ids] == [owner(b, world) for b in ids]
