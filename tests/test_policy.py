@@ -19,7 +19,12 @@ CSRC = os.path.join(ROOT, "kcj-cascade-v6_b200", "csrc")
 @pytest.fixture(scope="module")
 def ph(tmp_path_factory):
     out = tmp_path_factory.mktemp("policy") / "libpolicy_harness.so"
-    subprocess.run(["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-I{CSRC}",
+    # CB_SANITIZE=1 builds the harness with ASan + UBSan; run pytest with
+    # LD_PRELOAD="$(gcc -print-file-name=libasan.so) $(gcc -print-file-name=libubsan.so)"
+    # and ASAN_OPTIONS=detect_leaks=0 so the runtimes load first.
+    opt = (["-O1", "-g", "-fno-omit-frame-pointer", "-fsanitize=address,undefined",
+            "-fno-sanitize-recover=undefined"] if os.environ.get("CB_SANITIZE") == "1" else ["-O2"])
+    subprocess.run(["g++", *opt, "-std=c++17", "-shared", "-fPIC", f"-I{CSRC}",
                     os.path.join(HERE, "native", "policy_harness.cpp"), os.path.join(CSRC, "policy.cpp"),
                     "-o", str(out)], check=True)
     lib = C.CDLL(str(out))
