@@ -56,7 +56,7 @@ def parse():
     p.add_argument("--e2e-blocks", type=int, default=4096)
     p.add_argument("--cpu-blocks", type=int, default=1024)
     p.add_argument("--copy-engine", type=int, default=0)
-    p.add_argument("--hash-lanes", type=int, default=32)
+    p.add_argument("--hash-lanes", type=int, default=32, help="reserved; the SHA-256 kernel runs 32 chains per warp")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")

@@ -64,7 +64,8 @@ typedef struct cb_config {
   int32_t copy_engine;          /* 0 auto, 1 TMA bulk, 2 vector LSU         */
   uint64_t staging_bytes;       /* device staging for host-memory callers   */
   int32_t profile;              /* 1: time each kernel with CUDA events     */
-  int32_t hash_lanes;           /* SHA-256 chains per warp: 8, 16 or 32     */
+  int32_t hash_lanes;           /* reserved: the SHA-256 kernel always runs
+                                   32 chains per warp; accepted, ignored   */
   uint64_t replica_bytes;       /* DHT: HBM for replicas of hot remote blocks */
   int32_t locality_aware;       /* DHT: replicate hot remote blocks locally */
   uint32_t promotion_threshold; /* accesses before a block may be replicated */

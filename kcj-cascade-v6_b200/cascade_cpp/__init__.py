@@ -382,7 +382,7 @@ class DistributedConfig:
         self.dht = None               # None: shard over all ranks when WORLD_SIZE > 1
         self.replica_bytes = 0        # DHT: HBM for replicas of hot remote blocks (0 = auto)
         self.profile = False          # time every kernel with CUDA events (stats *_ns)
-        self.hash_lanes = 32          # SHA-256 chains per warp (8, 16, 32)
+        self.hash_lanes = 32          # reserved (the SHA-256 kernel runs 32 chains per warp)
         self.collective_timeout_ms = 0  # DHT: abort a collective after this long (0 = 600 s)
 
 
