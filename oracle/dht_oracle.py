@@ -2,10 +2,10 @@
 
 Sequential restatement of the multi-rank store semantics of the B200 DHT:
 every block has one owner rank, owner = first 8 ID bytes (big-endian) mod
-world; within one collective put round an owner applies the requests it
+world; within one collective put step an owner applies the requests it
 receives in (source rank, batch index) order with the sequential dedup rule
 of DistributedStore::put (cascade_Code/cpp/src/distributed_backend.cpp:
-604-608), so among byte-identical blocks put in the same round the lowest
+604-608), so among byte-identical blocks put in the same step the lowest
 (rank, index) is stored and every other copy is a dedup hit; a get returns
 the bytes stored by the owner.
 
@@ -29,7 +29,7 @@ class DhtOracle:
         self.dedup_hits = [0] * world  # counted on the putting rank
         self.registry = [set() for _ in range(world)]
 
-    def put_round(self, items: list[list[tuple[str, bytes, bool]]]) -> list[list[int]]:
+    def put_step(self, items: list[list[tuple[str, bytes, bool]]]) -> list[list[int]]:
         """items[r] = rank r's batch [(id, bytes, is_prefix)]; returns per-rank
         status lists (0 stored, 1 dedup hit)."""
         status = [[None] * len(b) for b in items]

@@ -44,10 +44,10 @@ def main():
     pool, items = batches(world, 11)
     ids_all = [[O.block_id(pool[s]) for s, _ in items[r]] for r in range(world)]
     ora = DhtOracle(world)
-    want_status = ora.put_round([[(ids_all[r][i], pool[s].tobytes(), pf) for i, (s, pf) in enumerate(items[r])]
+    want_status = ora.put_step([[(ids_all[r][i], pool[s].tobytes(), pf) for i, (s, pf) in enumerate(items[r])]
                                  for r in range(world)])
 
-    # round 1: device tensors, GPU hashing
+    # phase 1: device tensors, GPU hashing
     blocks = [torch.from_numpy(pool[s].copy()).to(dev) for s, _ in items[rank]]
     ids, status = store.batch_put(blocks, is_prefix=[pf for _, pf in items[rank]], return_status=True)
     assert ids == ids_all[rank], "ids"
@@ -127,9 +127,9 @@ def main():
     assert loc is not None and loc.node_id == owner(uniq[0], world) and loc.is_gpu
     assert store.locate(missing) is None
 
-    # round 2: host numpy blocks, everything is already stored
+    # phase 2: host numpy blocks, everything is already stored
     ids2, status2 = store.batch_put([pool[s] for s, _ in items[rank]], return_status=True)
-    assert ids2 == ids_all[rank] and status2 == [1] * len(ids2), "round 2"
+    assert ids2 == ids_all[rank] and status2 == [1] * len(ids2), "phase 2"
 
     # cluster usage sums the shards; total blocks per owner add up
     st = store.get_stats()

@@ -100,7 +100,7 @@ def test_dht_protocol_two_gloo_ranks():
     from oracle.dht_oracle import DhtOracle
     pool, items = _batches(world)
     ora = DhtOracle(world)
-    want = ora.put_round([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
+    want = ora.put_step([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
     for r in range(world):
         assert out[r] == want[r], r
     # cross-rank duplicates exist and the lowest (rank, index) copy is stored
@@ -120,7 +120,7 @@ def _prefix_worker(rank, world, port, out):
 
     pool, items = _batches(world)
     ora = DhtOracle(world)
-    ora.put_round([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
+    ora.put_step([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
     # what this rank's policy holds: the prefix blocks it owns
     held = sorted({b for r in range(world) for b in ora.registry[r] if owner(b, world) == rank})
     count = torch.tensor([len(held)], dtype=torch.int64)
@@ -156,7 +156,7 @@ def test_prefix_registry_sync_two_gloo_ranks():
     from oracle.dht_oracle import DhtOracle, owner
     pool, items = _batches(world)
     ora = DhtOracle(world)
-    ora.put_round([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
+    ora.put_step([[(O.block_id(pool[s]), pool[s], pf) for s, pf in items[r]] for r in range(world)])
     union = ora.sync_prefixes()
     assert union and all(ora.registry[r] == union for r in range(world))
     for r in range(world):
