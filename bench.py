@@ -55,6 +55,8 @@ def parse():
     p.add_argument("--block-bytes", type=int, default=917504)
     p.add_argument("--e2e-blocks", type=int, default=4096)
     p.add_argument("--cpu-blocks", type=int, default=1024)
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="cpu_baseline: repeat passes over the sample until this much put + get time is timed")
     p.add_argument("--copy-engine", type=int, default=0)
     p.add_argument("--hash-lanes", type=int, default=32, help="reserved; the SHA-256 kernel runs 32 chains per warp")
     p.add_argument("--no-sweep", action="store_true")
@@ -247,10 +249,14 @@ def reduce_sum(x, world):
 
 # --------------------------------------------------------------- baseline
 
-def cpu_reference(args, n_blocks, steps=1, threads=None):
+def cpu_reference(args, n_blocks, steps=1, threads=None, min_seconds=0.0, max_passes=200, skip=0):
     """The reference's CPU path (oracle/_ref): OpenMP compute_block_id over
     the batch, CascadeStore::put_batch into its SHM tier, shuffled
-    get_batch. Returns (GB/s, details)."""
+    get_batch. One store serves every pass (cleared between passes, untimed,
+    like the GPU step's clear). The first `skip` passes are warm-up; then at
+    least `steps` timed passes, more until `min_seconds` of timed put + get
+    have accumulated (at most `max_passes`); the median pass is reported.
+    Returns (GB/s, details)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle", "_ref"))
     import cascade_ref
     from cascade_cpp import workloads as W
@@ -268,25 +274,31 @@ def cpu_reference(args, n_blocks, steps=1, threads=None):
     cap = len(uniq) * size + (64 << 20)
     out = np.empty(len(uniq) * size, np.uint8)
     out_off = (np.arange(len(uniq)) * size).astype(np.uint64)
-    times = []
-    for _ in range(steps):
-        store = cascade_ref.CascadeStore(shm_capacity=cap, shm_path=shm)
-        t0 = time.perf_counter()
-        for i in range(0, n_blocks, args.batch):
-            ids = cascade_ref.compute_block_ids(packed_u, offsets[i:i + args.batch], sizes[i:i + args.batch],
-                                                threads)
-            store.put_batch(ids, packed_u, offsets[i:i + args.batch], sizes[i:i + args.batch])
-        t1 = time.perf_counter()
-        all_ids = list(dict.fromkeys(cascade_ref.compute_block_ids(packed_u, out_off, np.full(len(uniq), size,
-                                                                                            np.uint64), threads)))
-        order = np.random.default_rng(5).permutation(len(all_ids))
-        t2 = time.perf_counter()
-        for i in range(0, len(order), args.batch):
-            sel = order[i:i + args.batch]
-            found, _ = store.get_batch([all_ids[j] for j in sel], out, out_off[:len(sel)])
-            assert found == len(sel)
-        t3 = time.perf_counter()
-        times.append((t1 - t0, t3 - t2))
+    # the IDs read back (untimed; the same every pass)
+    all_ids = list(dict.fromkeys(cascade_ref.compute_block_ids(packed_u, out_off,
+                                                               np.full(len(uniq), size, np.uint64), threads)))
+    order = np.random.default_rng(5).permutation(len(all_ids))
+    store = cascade_ref.CascadeStore(shm_capacity=cap, shm_path=shm)
+    times, done = [], 0
+    try:
+        while done < skip or len(times) < steps or (sum(a + b for a, b in times) < min_seconds
+                                                    and len(times) < max_passes):
+            t0 = time.perf_counter()
+            for i in range(0, n_blocks, args.batch):
+                ids = cascade_ref.compute_block_ids(packed_u, offsets[i:i + args.batch], sizes[i:i + args.batch],
+                                                    threads)
+                store.put_batch(ids, packed_u, offsets[i:i + args.batch], sizes[i:i + args.batch])
+            t1 = time.perf_counter()
+            for i in range(0, len(order), args.batch):
+                sel = order[i:i + args.batch]
+                found, _ = store.get_batch([all_ids[j] for j in sel], out, out_off[:len(sel)])
+                assert found == len(sel)
+            t2 = time.perf_counter()
+            if done >= skip:
+                times.append((t1 - t0, t2 - t1))
+            done += 1
+            store.clear()
+    finally:
         del store
         shutil.rmtree(shm, ignore_errors=True)
     put_s = float(np.median([t[0] for t in times]))
@@ -294,7 +306,9 @@ def cpu_reference(args, n_blocks, steps=1, threads=None):
     put_b, get_b = n_blocks * size, len(uniq) * size
     return (put_b + get_b) / (put_s + get_s) / GB, {
         "put_gbs": put_b / put_s / GB, "get_gbs": get_b / get_s / GB, "cores": threads, "seconds": put_s + get_s,
-        "sample": f"{n_blocks} x {size} B blocks (25% copies), batch {args.batch}"}
+        "passes": len(times), "pass_seconds": [a + b for a, b in times],
+        "sample": f"{n_blocks} x {size} B blocks (25% copies), batch {args.batch}; median of {len(times)} "
+                  f"passes ({sum(a + b for a, b in times):.1f} s timed)"}
 
 
 # ------------------------------------------------------------------- main
@@ -313,16 +327,8 @@ def main():
         if not ok:
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built"}))
             return
-        vals, secs = [], []
-        for _ in range(args.warmup):
-            cpu_reference(args, args.cpu_blocks)
-        det = None
-        for _ in range(args.steps):
-            v, det = cpu_reference(args, args.cpu_blocks)
-            vals.append(v)
-            secs.append(det["seconds"])  # timed put + get (block generation excluded)
-        el = float(np.sum(secs))
-        v = float(np.median(vals))
+        v, det = cpu_reference(args, args.cpu_blocks, steps=args.steps, skip=args.warmup)
+        el = float(np.sum(det["pass_seconds"]))  # timed put + get of the K steps (generation excluded)
         print(json.dumps({
             "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 2),
@@ -473,9 +479,9 @@ def main():
         trace(args, "e2e")
         line["e2e"] = e2e_run(args, rank, world, device, store)
     trace(args, "done")
-    if rank == 0 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu:  # the CPU baseline is an N=1 figure
         try:
-            v, det = cpu_reference(args, args.cpu_blocks, steps=1)
+            v, det = cpu_reference(args, args.cpu_blocks, steps=1, min_seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": det["cores"],
                                     "kind": "reference", "sample": det["sample"],
                                     "put_gbs": round(det["put_gbs"], 3), "get_gbs": round(det["get_gbs"], 3)}
