@@ -1,4 +1,4 @@
-"""N>1 host-side logic on CPU: two gloo ranks run the DHT routing protocol
+"""N>1 host-side logic on CPU: 2 and 4 gloo ranks run the DHT routing protocol
 (owner = cb_owner_rank, per-owner buckets in batch order, counts all-gather,
 all-to-all of requests, owner-side sequential dedup in (source rank, index)
 order) and must reach exactly the sequential DhtOracle's decisions."""
@@ -90,8 +90,8 @@ def _worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_dht_protocol_two_gloo_ranks():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_dht_protocol_gloo_ranks(world):
     port = _free_port()
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
@@ -130,7 +130,7 @@ def _prefix_worker(rank, world, port, out):
     rec = torch.zeros((max_n, 17), dtype=torch.int64)  # 16 key bytes + size
     for j, b in enumerate(held):
         rec[j, :16] = torch.tensor(list(bytes.fromhex(b)))
-        rec[j, 16] = len(next(pool[s] for s, _ in items[0] + items[1] if O.block_id(pool[s]) == b))
+        rec[j, 16] = len(next(pool[s] for s, _ in sum(items, []) if O.block_id(pool[s]) == b))
     recs = [torch.zeros_like(rec) for _ in range(world)]
     dist.all_gather(recs, rec)
     registry = set(ora.registry[rank])
@@ -146,8 +146,8 @@ def _prefix_worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
-def test_prefix_registry_sync_two_gloo_ranks():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_prefix_registry_sync_gloo_ranks(world):
     port = _free_port()
     mgr = mp.get_context("spawn").Manager()
     out = mgr.dict()
