@@ -45,6 +45,7 @@ __all__ = [
 
 _lib_handle = None
 _lib_lock = threading.Lock()
+_cache_lock = threading.Lock()  # the per-device helper stores (hashing, KVCompressor)
 
 
 def _native_lib():
@@ -223,16 +224,17 @@ _hashers: dict[int, _Native] = {}
 
 
 def _hasher(device: int) -> _Native:
-    h = _hashers.get(device)
-    if h is None:
-        cfg = L.cb_config()
-        _native_lib().cb_config_init(C.byref(cfg))
-        cfg.gpu_capacity_bytes = 0
-        cfg.dram_capacity_bytes = 0
-        cfg.index_log2 = 8
-        cfg.device = device
-        h = _hashers[device] = _Native(cfg)
-    return h
+    with _cache_lock:  # one helper store per device, also when threads race here
+        h = _hashers.get(device)
+        if h is None:
+            cfg = L.cb_config()
+            _native_lib().cb_config_init(C.byref(cfg))
+            cfg.gpu_capacity_bytes = 0
+            cfg.dram_capacity_bytes = 0
+            cfg.index_log2 = 8
+            cfg.device = device
+            h = _hashers[device] = _Native(cfg)
+        return h
 
 
 def _default_device() -> int:
@@ -290,16 +292,17 @@ class KVCompressor:
 
     @classmethod
     def _native(cls, device: int) -> "_Native":
-        n = cls._stores.get(device)
-        if n is None:
-            c = L.cb_config()
-            _native_lib().cb_config_init(C.byref(c))
-            c.gpu_capacity_bytes = 0  # no pool: the store only lends its scratch buffers and stream
-            c.dram_capacity_bytes = 0
-            c.index_log2 = 4
-            c.device = device
-            n = cls._stores[device] = _Native(c)
-        return n
+        with _cache_lock:
+            n = cls._stores.get(device)
+            if n is None:
+                c = L.cb_config()
+                _native_lib().cb_config_init(C.byref(c))
+                c.gpu_capacity_bytes = 0  # no pool: the store only lends its scratch buffers and stream
+                c.dram_capacity_bytes = 0
+                c.index_log2 = 4
+                c.device = device
+                n = cls._stores[device] = _Native(c)
+            return n
 
     @staticmethod
     def _check_blocks(blocks) -> int:

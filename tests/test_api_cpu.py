@@ -80,3 +80,28 @@ def test_owner_rank_matches_oracle_rule():
     ids += ["ff" * 16, "00" * 16, "80" + "00" * 15]
     for world in (1, 2, 3, 4, 7, 8):
         assert [cascade_cpp.owner_rank(b, world) for b in ids] == [owner(b, world) for b in ids]
+
+
+def test_helper_store_caches_create_one_store_per_device(monkeypatch):
+    # threads that hash (or compress) at once on a device share one helper store
+    import threading
+    import time
+    made = []
+
+    class FakeNative:
+        def __init__(self, cfg):
+            time.sleep(0.02)  # widen the window a racing thread would use
+            made.append(cfg.device)
+
+    monkeypatch.setattr(cascade_cpp, "_Native", FakeNative)
+    monkeypatch.setattr(cascade_cpp, "_hashers", {})
+    monkeypatch.setattr(cascade_cpp.KVCompressor, "_stores", {})
+    for get in (cascade_cpp._hasher, cascade_cpp.KVCompressor._native):
+        made.clear()
+        got = []
+        ts = [threading.Thread(target=lambda: got.append(get(3))) for _ in range(8)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        assert made == [3] and len({id(g) for g in got}) == 1
