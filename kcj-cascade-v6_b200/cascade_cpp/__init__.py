@@ -129,8 +129,7 @@ class _Native:
             raise CascadeError(rc, lib.cb_last_error(None).decode(errors="replace"))
         self.lib = lib
         self.h = h
-        self.device = cfg.device
-        self._lock = threading.Lock()
+        self.device = cfg.device  # calls on one store are serialised by the library's own mutex
 
     def _check(self, rc: int):
         if rc:
