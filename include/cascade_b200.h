@@ -130,7 +130,8 @@ int cb_create(const cb_config *cfg, cb_store **out);
 int cb_destroy(cb_store *s);
 
 /* Message of the last failed call on this store (or of cb_create when s is
- * NULL). Replaces the CUDA_CHECK fprintf of src/gpu_backend.cu:43-51. */
+ * NULL). The string stays valid until the same thread calls cb_last_error
+ * again. Replaces the CUDA_CHECK fprintf of src/gpu_backend.cu:43-51. */
 const char *cb_last_error(const cb_store *s);
 
 /* Zero-copy get: addrs_out[i] = device address of block i inside this

@@ -1412,9 +1412,15 @@ int cb_destroy(cb_store *h) {
   return CB_OK;
 }
 
+// The message is copied under the store's mutex into a per-thread buffer: a
+// call from another thread may replace the store's message meanwhile, and
+// the pointer returned here must stay valid until this thread asks again.
 const char *cb_last_error(const cb_store *h) {
+  static thread_local std::string copy;
   if (!h || !h->s) return cb::g_create_error.c_str();
-  return h->s->last_error.c_str();
+  std::lock_guard<std::mutex> g(h->s->mu);
+  copy = h->s->last_error;
+  return copy.c_str();
 }
 
 int cb_selftest(cb_store *h, int32_t which) {
