@@ -249,6 +249,21 @@ def reduce_sum(x, world):
 
 # --------------------------------------------------------------- baseline
 
+def host_cpu():
+    """(model name, SHA-NI present) of this host, from /proc/cpuinfo."""
+    model, sha = "unknown", False
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name") and model == "unknown":
+                    model = line.split(":", 1)[1].strip()
+                elif line.startswith("flags"):
+                    sha = sha or "sha_ni" in line.split()
+    except OSError:
+        pass
+    return model, sha
+
+
 def cpu_reference(args, n_blocks, steps=1, threads=None, min_seconds=0.0, max_passes=200, skip=0):
     """The reference's CPU path (oracle/_ref): OpenMP compute_block_id over
     the batch, CascadeStore::put_batch into its SHM tier, shuffled
@@ -307,6 +322,7 @@ def cpu_reference(args, n_blocks, steps=1, threads=None, min_seconds=0.0, max_pa
     return (put_b + get_b) / (put_s + get_s) / GB, {
         "put_gbs": put_b / put_s / GB, "get_gbs": get_b / get_s / GB, "cores": threads, "seconds": put_s + get_s,
         "passes": len(times), "pass_seconds": [a + b for a, b in times],
+        "cpu_model": host_cpu()[0], "sha_ni": host_cpu()[1],
         "sample": f"{n_blocks} x {size} B blocks (25% copies), batch {args.batch}; median of {len(times)} "
                   f"passes ({sum(a + b for a, b in times):.1f} s timed)"}
 
@@ -336,7 +352,8 @@ def main():
             "data": "synthetic", "config": config_dict(args),
             "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": det["cores"], "kind": "reference",
                              "sample": det["sample"], "put_gbs": round(det["put_gbs"], 3),
-                             "get_gbs": round(det["get_gbs"], 3)},
+                             "get_gbs": round(det["get_gbs"], 3), "cpu_model": det["cpu_model"],
+                             "sha_ni": det["sha_ni"]},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
         return
 
@@ -484,7 +501,8 @@ def main():
             v, det = cpu_reference(args, args.cpu_blocks, steps=1, min_seconds=args.cpu_seconds)
             line["cpu_baseline"] = {"value": round(v, 3), "unit": "GB/s", "cores": det["cores"],
                                     "kind": "reference", "sample": det["sample"],
-                                    "put_gbs": round(det["put_gbs"], 3), "get_gbs": round(det["get_gbs"], 3)}
+                                    "put_gbs": round(det["put_gbs"], 3), "get_gbs": round(det["get_gbs"], 3),
+                                    "cpu_model": det["cpu_model"], "sha_ni": det["sha_ni"]}
         except Exception as e:  # pragma: no cover
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     if rank == 0:

@@ -39,6 +39,7 @@ def test_reference_arm_line():
     assert "workload" in line["config"]
     cb = line["cpu_baseline"]
     assert cb["kind"] == "reference" and cb["value"] == line["value"] and cb["cores"] >= 1 and "128" in cb["sample"]
+    assert isinstance(cb["cpu_model"], str) and isinstance(cb["sha_ni"], bool)
     e2e = line["e2e"]
     assert e2e["value"] == line["value"] and e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
     # ms_per_step is the timed put + get of the step: value x time = the
