@@ -35,6 +35,7 @@ def test_reference_arm_line():
               "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
         assert k in line, k
     assert line["unit"] == "GB/s" and line["value"] > 0 and line["higher_is_better"] is True
+    assert abs(line["value_gibs"] - line["value"] * 1e9 / 2**30) < 0.01
     assert line["steps"] == 1 and line["n_gpus"] == 1 and line["vs_baseline"] is None
     assert "workload" in line["config"]
     cb = line["cpu_baseline"]
