@@ -305,3 +305,30 @@ def test_pinned_blocks_are_never_victims(ph):
     ph.ph_unpin(pol.p, *pol.key("v0"))
     pol.put(["w"], [S])
     assert pol.tier("v0") == "hbm"  # one pin left
+
+
+@pytest.mark.parametrize("semantic", [True, False])
+def test_reference_semantic_eviction_scenario(ph, semantic):
+    # The reference's own check (benchmark/scripts/v6_distributed_bench.py:
+    # 151-207): 5 MB GPU, 20 MB DRAM, dedup off, 10 prefix then 40 regular
+    # 2 MB blocks put one by one; with semantic eviction every prefix block
+    # must still be readable afterwards. Placement equals the oracle model's.
+    S, MB = 2 << 20, 1 << 20
+    pol = Pol(ph, 5 * MB, 20 * MB, semantic=semantic)
+    model = TierModel(5 * MB, 20 * MB, semantic=semantic)
+    names = [f"prefix_{i:04d}" for i in range(10)] + [f"regular_{i:04d}" for i in range(40)]
+    for nm in names:
+        pf = nm.startswith("prefix")
+        st, _, _, _ = pol.put([nm], [S], [1 if pf else 0], dedup=False)
+        assert st == [0]
+        model.put(nm, S, pf)
+    assert [pol.tier(n) for n in names] == [model.tier(n) for n in names]
+    kept = sum(pol.tier(f"prefix_{i:04d}") is not None for i in range(10))
+    if semantic:
+        assert kept == 10  # the reference's "10/10 prefix readback"
+    else:
+        assert kept < 10   # plain LRU drops old prefix blocks like any other
+    c = pol.counters()
+    # prefix_blocks counts prefix blocks the store holds: a dropped block is
+    # gone here (the reference would still hold it on its Lustre tier)
+    assert c["size"] == 12 and c["prefix_blocks"] == kept
