@@ -136,3 +136,34 @@ def test_integration_snippets_compile(tmp_path):
                         "-I", pybind11.get_include(), "-I", sysconfig.get_paths()["include"], str(src)],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_plain_c_program_links_and_calls_the_library(lib, tmp_path):
+    # the boundary from C: compile against the header, link the library,
+    # call the entry points that need no GPU
+    prog = tmp_path / "use.c"
+    prog.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "cascade_b200.h"
+int main(void) {
+  cb_config c;
+  cb_config_init(&c);
+  if (c.dedup_enabled != 1 || c.gpu_capacity_bytes != (32ull << 30)) return 1;
+  uint8_t key[16];
+  memset(key, 0, sizeof key);
+  key[7] = 5;                                  /* first 8 bytes big-endian = 5 */
+  if (cb_owner_rank(key, 4) != 1) return 2;    /* 5 mod 4 */
+  if (cb_owner_rank(key, 0) != -1) return 3;   /* bad world */
+  if (cb_put_batch(NULL, NULL, NULL, NULL, NULL, 1, CB_MEM_DEVICE, NULL, NULL, NULL) != CB_ERR_ARG) return 4;
+  if (cb_destroy(NULL) != CB_OK) return 5;
+  puts("ok");
+  return 0;
+}
+''')
+    exe = tmp_path / "use"
+    libdir = os.path.dirname(L.LIB_PATH)
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.dirname(HEADER), str(prog), "-o", str(exe),
+                    f"-L{libdir}", "-l:" + os.path.basename(L.LIB_PATH), f"-Wl,-rpath,{libdir}"], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", (r.returncode, r.stdout, r.stderr)
