@@ -454,8 +454,8 @@ def main():
             "peak": hbm_peak, "unit": "GB/s", "frac": round(sha_achieved / hbm_peak, 5),
             "peak_source": peak_src,
             # dram__bytes_read.sum + dram__bytes_write.sum of one 1024-block
-            # launch from the ncu capture in profiles/sha256_pc_kernel_1024x917504.md
-            # (704.9 MB + 6.3 MB; the 25 % copies are read from L2, not DRAM)
+            # launch from an ncu capture of this workload (704.9 MB + 6.3 MB;
+            # the 25 % copies are read from L2, not DRAM)
             "traffic": SHA_TRAFFIC_PER_1024_LAUNCH if args.batch == 1024 else None,
             "bytes_per_launch": int(sha_bytes_launch),
             "note": "bytes = block bytes read once per launch; binding limit is the SHA-256 chain latency "
@@ -735,6 +735,10 @@ def spill_main(args, rank, world, local, device):
     cfg.dht = False
     cfg.index_log2 = 17
     cfg.kv_compression = bool(args.kv_compression)
+    # the configuration asks for promotion to run: CascadeStore's rule (every
+    # DRAM hit moves back to HBM), not DistributedStore's locality rule, under
+    # which a single store's own DRAM hits are never promoted
+    cfg.promote_on_hit = True
     store = cascade_cpp.DistributedStore(cfg)
     rng = np.random.default_rng(33)
     prefix = (rng.random(nb) < 0.10).astype(np.uint8)

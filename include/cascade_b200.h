@@ -79,8 +79,24 @@ typedef struct cb_config {
   uint64_t collective_timeout_ms; /* DHT: a collective that does not finish in
                                    time aborts the communicator and fails
                                    with CB_ERR_TIMEOUT (0 = 600 s)          */
-  uint64_t reserved[2];
+  int32_t promotion_rule;       /* which DRAM-tier get hits promote_on_hit
+                                   moves back to HBM: CB_PROMOTE_*          */
+  int32_t reserved32;
+  uint64_t reserved[1];
 } cb_config;
+
+/* cb_config.promotion_rule. CB_PROMOTE_EVERY_HIT: every DRAM-tier hit of a
+ * get (CascadeStore::get -> promote_to_gpu, src/cascade_core.cpp:1303-1307).
+ * CB_PROMOTE_LOCALITY: DistributedStore::get's rule
+ * (src/distributed_backend.cpp:721-724, :1224-1265): only with
+ * locality_aware, after >= promotion_threshold accesses and an EMA (window
+ * 8, alpha 0.3) of the block's remote-access rate above 0.5. Every access a
+ * rank makes to a block in its own DRAM tier is local, so under this rule a
+ * DRAM hit is never promoted (the reference's 1-rank DistributedStore never
+ * promotes either). Zero-copy views (cb_get_views) promote whenever
+ * promote_on_hit is set: a view must alias HBM. */
+#define CB_PROMOTE_EVERY_HIT 0
+#define CB_PROMOTE_LOCALITY 1
 
 /* Mirrors DistributedStore::Stats (include/cascade_distributed.hpp:386-409). */
 typedef struct cb_stats {
@@ -284,9 +300,16 @@ int32_t cb_owner_rank(const uint8_t *key, int32_t world);
  * CB_NOALLOC_MAX_BLOCKS is rejected with CB_ERR_ARG. Its scratch is one
  * static device array of ~66 KB that every GPU loading the library keeps
  * until exit; all calls share it, so calls that overlap on the GPU race.
- * The first call on a device looks up that array's address (make it before
- * any stream capture). Results are final when the call returns; errors are
- * reported by cb_last_error(NULL). */
+ * The first call on a device (an empty call, n = 0, does only this) looks up
+ * that array's address and, under lazy module loading, loads this entry
+ * point's GPU code and the array's backing: the only device memory it ever
+ * causes to be allocated, so make that first call at start-up. Later calls
+ * allocate nothing. The looked-up address is kept for the process lifetime:
+ * do not call this on a device after cudaDeviceReset of that device. A call
+ * on a stream that is being captured is refused with CB_ERR_ARG before
+ * anything is enqueued (each call copies from pageable host memory and waits
+ * for its own completion). Results are final when the call returns; errors
+ * are reported by cb_last_error(NULL). */
 int cb_hash_batch_noalloc(int32_t device, const void *const *ptrs, const uint64_t *sizes, int32_t n,
                           uint8_t *digests_out, void *stream);
 

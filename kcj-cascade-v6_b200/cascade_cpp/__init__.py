@@ -377,7 +377,11 @@ class DistributedConfig:
         self.agg_file_size = 256 * 1024 * 1024
         # B200 additions
         self.device = None            # default: LOCAL_RANK / current CUDA device
-        self.promote_on_hit = True    # move DRAM-tier hits back to HBM
+        # DRAM-tier get hits back to HBM: None = DistributedStore::get's rule
+        # (locality-gated, distributed_backend.cpp:721-724: a store's own DRAM
+        # hits are local accesses and are never promoted), True = every hit
+        # (CascadeStore::get's rule, cascade_core.cpp:1303-1307), False = never
+        self.promote_on_hit = None
         self.copy_engine = 0          # 0 auto (TMA bulk), 1 TMA bulk, 2 LSU vectors
         self.index_log2 = 16
         self.staging_bytes = 1 << 30  # device staging for host-memory callers
@@ -663,7 +667,8 @@ class DistributedStore(_StoreBase):
         c.device = _resolve_device(cfg.device)
         c.dedup_enabled = 1 if cfg.dedup_enabled else 0
         c.semantic_eviction = 1 if cfg.semantic_eviction else 0
-        c.promote_on_hit = 1 if cfg.promote_on_hit else 0
+        c.promote_on_hit = 0 if cfg.promote_on_hit is False else 1
+        c.promotion_rule = L.CB_PROMOTE_EVERY_HIT if cfg.promote_on_hit is True else L.CB_PROMOTE_LOCALITY
         c.index_log2 = int(cfg.index_log2)
         c.copy_engine = int(cfg.copy_engine)
         c.staging_bytes = int(cfg.staging_bytes)
@@ -754,6 +759,7 @@ class CascadeStore(_StoreBase):
         c.dedup_enabled = 1 if cfg.dedup_enabled else 0
         c.semantic_eviction = 1 if cfg.semantic_eviction else 0
         c.promote_on_hit = 1 if cfg.promotion_enabled else 0
+        c.promotion_rule = L.CB_PROMOTE_EVERY_HIT  # CascadeStore::get promotes every SHM hit
         c.index_log2 = int(cfg.index_log2)
         c.copy_engine = int(cfg.copy_engine)
         c.staging_bytes = int(cfg.staging_bytes)

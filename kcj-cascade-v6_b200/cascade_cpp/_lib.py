@@ -21,6 +21,8 @@ CB_ERR_TIMEOUT = 5
 CB_ERR_NCCL = 6
 CB_ERR_STATE = 7
 CB_ERR_DEVICE = 8
+CB_PROMOTE_EVERY_HIT = 0
+CB_PROMOTE_LOCALITY = 1
 CB_SELFTEST_HASH_WAIT = 1
 CB_SELFTEST_FAIL_MOVES = 2
 
@@ -60,7 +62,9 @@ class cb_config(C.Structure):
         ("kv_compression", C.c_int32),
         ("prefix_replication", C.c_int32),
         ("collective_timeout_ms", C.c_uint64),
-        ("reserved", C.c_uint64 * 2),
+        ("promotion_rule", C.c_int32),
+        ("reserved32", C.c_int32),
+        ("reserved", C.c_uint64 * 1),
     ]
 
 

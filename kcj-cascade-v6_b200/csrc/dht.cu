@@ -8,8 +8,10 @@
 // IPC and mapped into every other rank at attach time, so payloads move by
 // direct peer loads/stores over NVLink; only 16-32-byte lookup records travel
 // through NCCL (grouped send/recv = all-to-all, preceded by an all-gather of
-// the per-peer counts). No TMA multicast is used; peer payload reads may use
-// non-multicast TMA loads, peer payload writes use plain vector stores.
+// the per-peer counts). Every copy whose source or destination is a peer's
+// memory (or pinned host memory) runs on the LSU engine: plain 16-byte loads
+// and stores. No TMA copy of any kind ever touches peer memory, and no TMA
+// multicast is used anywhere.
 //
 // batch_put : local SHA-256 -> requests to owners -> owners dedup in
 //             (source rank, batch index) order, allocate, insert into their

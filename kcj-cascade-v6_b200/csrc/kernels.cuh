@@ -24,6 +24,9 @@ struct HashProgress {
 // One CTA (producer + consumer warp) per 32 blocks. progress may be null.
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
                                 unsigned *d_err, cudaStream_t stream, const HashProgress *progress = nullptr);
+// Loads the SHA-256 kernel's module on the current device now (with lazy
+// module loading it would otherwise load, and allocate, at its first launch).
+cudaError_t prepare_sha256_kernel();
 
 // copy.cu — batched copies. Descriptor i covers units
 // [unit_start[i], unit_start[i+1]) of kCopyUnit bytes each; a unit past the

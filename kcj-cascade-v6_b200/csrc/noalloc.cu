@@ -14,6 +14,12 @@
 // process exits. The caller passes the blocks (device memory) and a device
 // output buffer for the digests. The call makes no cudaMalloc / cudaFree /
 // allocating library call.
+//
+// With lazy module loading (the CUDA 12 default) the GPU code of this file
+// and of the SHA-256 kernel, and the backing of the array, are loaded on
+// first use. The per-device set-up below forces that loading, so it happens
+// in the first call on a device (an empty call, n = 0, does only the
+// set-up); every later call allocates nothing at all.
 #include <stdint.h>
 #include <string.h>
 
@@ -51,13 +57,18 @@ int noalloc_fail(int code, const char *msg, cudaError_t e = cudaSuccess) {
 
 // The host-side name of g_noalloc_scratch is only a stand-in: its device
 // address differs per device and must be looked up with that device current.
-// Done once per device, on the first call that targets it.
+// Done once per device, on the first call that targets it, together with the
+// loading of the SHA-256 kernel, so that no later call loads anything. The
+// address is kept for the life of the process: a cudaDeviceReset of that
+// device invalidates it.
 int scratch_for(int device, unsigned char **out) {
   std::lock_guard<std::mutex> g(g_setup_mu);
   if (!g_scratch_addr[device]) {
     void *p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) return noalloc_fail(CB_ERR_CUDA, "cudaGetSymbolAddress(noalloc scratch)", e);
+    if ((e = prepare_sha256_kernel()) != cudaSuccess)
+      return noalloc_fail(CB_ERR_CUDA, "cb_hash_batch_noalloc: loading the SHA-256 kernel", e);
     g_scratch_addr[device] = p;
   }
   *out = static_cast<unsigned char *>(g_scratch_addr[device]);
@@ -79,9 +90,9 @@ extern "C" int cb_hash_batch_noalloc(int32_t device, const void *const *ptrs, co
   if (device < 0 || device >= kMaxDevices) return noalloc_fail(CB_ERR_ARG, "cb_hash_batch_noalloc: bad device");
   if (reinterpret_cast<uintptr_t>(digests_out) & 15)
     return noalloc_fail(CB_ERR_ARG, "cb_hash_batch_noalloc: digests_out must be 16-byte aligned");
-  if (n == 0) return CB_OK;
   for (int i = 0; i < n; ++i)
     if (sizes[i] > kSizeMask) return noalloc_fail(CB_ERR_ARG, "cb_hash_batch_noalloc: block too large");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   int prev = -1;
   cudaError_t e = cudaGetDevice(&prev);
@@ -91,10 +102,22 @@ extern "C" int cb_hash_batch_noalloc(int32_t device, const void *const *ptrs, co
 
   int rc = CB_OK;
   unsigned char *scratch = nullptr;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   unsigned host_err = 0;
   do {
-    if ((rc = scratch_for(device, &scratch)) != CB_OK) break;
+    // Each call copies its descriptors from pageable host memory and waits
+    // for its own completion; neither is allowed on a stream under capture,
+    // so refuse before anything is enqueued (the caller's capture stays
+    // valid).
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if ((e = cudaStreamIsCapturing(st, &cap)) != cudaSuccess) {
+      rc = noalloc_fail(CB_ERR_CUDA, "cb_hash_batch_noalloc: cudaStreamIsCapturing", e);
+      break;
+    }
+    if (cap != cudaStreamCaptureStatusNone) {
+      rc = noalloc_fail(CB_ERR_ARG, "cb_hash_batch_noalloc: the stream is being captured (not supported)");
+      break;
+    }
+    if ((rc = scratch_for(device, &scratch)) != CB_OK || n == 0) break;
     HashJob *jobs = reinterpret_cast<HashJob *>(scratch);
     unsigned *err = reinterpret_cast<unsigned *>(scratch + kNoAllocJobBytes);
     // Job descriptors: the caller's two host arrays are interleaved into the

@@ -319,6 +319,11 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
 
 }  // namespace
 
+cudaError_t prepare_sha256_kernel() {
+  cudaFuncAttributes a;
+  return cudaFuncGetAttributes(&a, sha256_pc_kernel);
+}
+
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
                                 unsigned *d_err, cudaStream_t stream, const HashProgress *progress) {
   (void)lanes;

@@ -884,9 +884,14 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   // src/cascade_core.cpp:1281), so that blocks of this batch are the last
   // victims of the promotions below.
   for (int i = 0; i < n; ++i) policy.touch(to_hkey(keys + 16 * i));
-  // Promotion on a DRAM hit (CascadeStore::get -> promote_to_gpu,
-  // src/cascade_core.cpp:1303-1307, :1166-1185; DistributedStore::get ->
-  // promote_to_local_gpu(id, out, size), src/distributed_backend.cpp:721-723).
+  // Promotion on a DRAM hit. CB_PROMOTE_EVERY_HIT is CascadeStore's rule
+  // (CascadeStore::get -> promote_to_gpu, src/cascade_core.cpp:1303-1307,
+  // :1166-1185). CB_PROMOTE_LOCALITY is DistributedStore::get's
+  // (src/distributed_backend.cpp:721-724): promote_to_local_gpu only when
+  // locality_aware and should_promote_local (:1257-1265), i.e. after
+  // >= promotion_threshold accesses with an EMA remote-access rate > 0.5.
+  // Every access a store makes to its own DRAM tier is a local one, so the
+  // EMA stays 0 and the rule never fires: such stores do not promote.
   // The host metadata already knows which requests are DRAM hits that will
   // be copied, so the promotions are planned before the lookup: the
   // demotions that make room for them (HBM -> DRAM, the device-to-host
@@ -897,7 +902,8 @@ int Store::get_device(const uint8_t *keys, int n, const uint64_t *outs, const ui
   std::vector<TierMove> moves;
   std::vector<HKey> dropped;
   bool planned = false;
-  if (cfg.promote_on_hit && policy.dram_used() > 0) {
+  const bool promote = cfg.promote_on_hit && cfg.promotion_rule == CB_PROMOTE_EVERY_HIT;
+  if (promote && policy.dram_used() > 0) {
     std::unordered_map<HKey, uint64_t, HKeyHash> copy_of;
     std::vector<HKey> order;
     for (int i = 0; i < n; ++i) {
@@ -1379,6 +1385,7 @@ void cb_config_init(cb_config *c) {
   c->dedup_enabled = 1;
   c->semantic_eviction = 1;
   c->promote_on_hit = 1;
+  c->promotion_rule = CB_PROMOTE_LOCALITY;  // DistributedStore::get's rule
   c->index_log2 = 16;
   c->copy_engine = 0;
   c->staging_bytes = 1ull << 30;

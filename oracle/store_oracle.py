@@ -238,3 +238,65 @@ class TierModel:
         if k in self.dram:
             return "dram"
         return None
+
+
+class LocalityTracker:
+    """DistributedStore::record_access / should_promote_local
+    (src/distributed_backend.cpp:1224-1265; AccessRecord,
+    include/cascade_distributed.hpp:162-180): per block, total and windowed
+    access counts; when a window of 8 accesses is full, the remote fraction
+    of the window enters an EMA with alpha 0.3 (float32 arithmetic, like the
+    reference). A block may be promoted after >= threshold accesses with an
+    EMA above 0.5."""
+
+    WINDOW = 8
+    ALPHA = np.float32(0.3)
+
+    def __init__(self, threshold: int = 3):
+        self.threshold = threshold
+        self.rec: dict[str, list] = {}  # id -> [total, window_total, window_remote, ema(float32)]
+
+    def record(self, k: str, remote: bool):
+        r = self.rec.setdefault(k, [0, 0, 0, np.float32(0.0)])
+        r[0] += 1
+        r[1] += 1
+        if remote:
+            r[2] += 1
+        if r[1] >= self.WINDOW:
+            cur = np.float32(r[2]) / np.float32(r[1])
+            r[3] = np.float32(self.ALPHA * cur + (np.float32(1.0) - self.ALPHA) * r[3])
+            r[1] = r[2] = 0
+
+    def should_promote(self, k: str) -> bool:
+        r = self.rec.get(k)
+        return r is not None and r[0] >= self.threshold and float(r[3]) > 0.5
+
+
+def distributed_gets(model: TierModel, tracker: LocalityTracker, batches, locality_aware: bool = True):
+    """Tier of every get of a 1-rank DistributedStore (DistributedStore::get,
+    src/distributed_backend.cpp:698-795) over ``batches`` of IDs: an HBM hit
+    or a DRAM hit (recorded as a local access), promoted only when
+    ``locality_aware and should_promote_local`` (:721-724). Returns
+    (codes per batch: 1 HBM / 2 DRAM / 0 miss, counters)."""
+    ctr = {"local_gpu_hits": 0, "local_dram_hits": 0, "misses": 0, "promotions_to_local": 0}
+    out = []
+    for batch in batches:
+        codes = []
+        for k in batch:
+            t = model.tier(k)
+            if t is None:
+                ctr["misses"] += 1
+                codes.append(0)
+                continue
+            model.touch(k)
+            tracker.record(k, remote=False)
+            if t == "hbm":
+                ctr["local_gpu_hits"] += 1
+                codes.append(1)
+            else:
+                ctr["local_dram_hits"] += 1
+                codes.append(2)
+                if locality_aware and tracker.should_promote(k) and model.promote(k):
+                    ctr["promotions_to_local"] += 1
+        out.append(codes)
+    return out, ctr

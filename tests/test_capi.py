@@ -123,17 +123,13 @@ def test_product_never_imports_oracle():
                 assert "sha256_oracle" not in txt, f
 
 
-def test_integration_snippets_compile(tmp_path):
-    # the C++ bindings shown to maintainers compile against this header
+def test_integration_snippets_compile():
+    # the C++ binding shown to maintainers compiles against this header
     pybind11 = pytest.importorskip("pybind11")
     import sysconfig
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    blocks = re.findall(r"```cpp\n(.*?)```", text, re.S)
-    assert len(blocks) >= 2
-    src = tmp_path / "integration.cpp"
-    src.write_text("#include <stdexcept>\n#include <string>\n" + "\n".join(blocks))
+    src = os.path.join(ROOT, "tests", "snippets", "pybind_binding.cpp")
     r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I", os.path.dirname(HEADER),
-                        "-I", pybind11.get_include(), "-I", sysconfig.get_paths()["include"], str(src)],
+                        "-I", pybind11.get_include(), "-I", sysconfig.get_paths()["include"], src],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr[-2000:]
 

@@ -175,7 +175,7 @@ def test_demoted_blocks_read_back_through_the_int8_tier(cls, memory):
 def test_evict_then_promote_on_hit():
     S = 65_536 + 2
     blocks = [gen("kv_fp16", 200 + i, S) for i in range(4)]
-    store = make_store(hbm=8 * S, dram=1 << 28)
+    store = make_store(hbm=8 * S, dram=1 << 28, promote_on_hit=True)  # CascadeStore's every-hit rule
     ids = store.batch_put([dev(b) for b in blocks])
     store.evict(4 * S)
     st = store.get_stats()
@@ -238,6 +238,7 @@ def test_get_promotions_overlapped_with_demotions(compress):
     cfg.dram_capacity = 1 << 30
     cfg.device = 0
     cfg.kv_compression = compress
+    cfg.promote_on_hit = True  # every DRAM hit is promoted (CascadeStore's rule)
     store = cascade_cpp.DistributedStore(cfg)
     ids = [store.batch_put([dev(b)])[0] for b in blocks]
     exp = [b.tobytes() for b in blocks]

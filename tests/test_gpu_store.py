@@ -230,6 +230,59 @@ def test_promotion_on_dram_hit():
         assert np.array_equal(out.cpu().numpy(), blocks[i])
 
 
+@pytest.mark.parametrize("cls", ["dist", "cascade"])
+def test_dram_hit_promotion_rule_matches_oracle(cls):
+    """DistributedStore promotes a DRAM hit only under its locality rule
+    (distributed_backend.cpp:721-724: locality_aware, >= 3 accesses, EMA of
+    the remote-access rate > 0.5), which a store's own accesses never meet;
+    CascadeStore promotes every DRAM hit (cascade_core.cpp:1303-1307). Tier
+    codes of every get, hit counters and promotions equal the oracle's."""
+    S = 128 * 1024
+    rng = np.random.default_rng(21)
+    blocks = [rng.integers(0, 256, S, dtype=np.uint8) for _ in range(16)]
+    store = make_store(hbm=8 * S, dram=32 * S, cls=cls)
+    ids = [store.batch_put([torch.from_numpy(b).to(DEV)])[0] for b in blocks]
+    model = O.TierModel(8 * S, 32 * S)
+    for i in ids:
+        assert model.put(i, S) in ("hbm", "dram")
+    if cls == "dist":  # placement after the puts (only DistributedStore has locate)
+        assert [store.locate(i).is_gpu for i in ids] == [model.tier(i) == "hbm" for i in ids]
+    batches = [[ids[j] for j in rng.integers(0, 16, 8)] for _ in range(12)]
+    if cls == "dist":
+        want, ctr = O.distributed_gets(model, O.LocalityTracker(3), batches)
+    else:
+        want, ctr = [], {"local_gpu_hits": 0, "local_dram_hits": 0, "promotions_to_local": 0}
+        for b in batches:  # CascadeStore: touch the batch, then promote its DRAM hits in order
+            codes = [1 if model.tier(k) == "hbm" else 2 for k in b]
+            for k in b:
+                model.touch(k)
+            for k, c in zip(b, codes):
+                if c == 2 and model.tier(k) == "dram" and model.promote(k):
+                    ctr["promotions_to_local"] += 1
+            ctr["local_gpu_hits"] += codes.count(1)
+            ctr["local_dram_hits"] += codes.count(2)
+            want.append(codes)
+    outs = [torch.empty(S, dtype=torch.uint8, device=DEV) for _ in range(8)]
+    for b, w in zip(batches, want):
+        keys = np.frombuffer(b"".join(bytes.fromhex(k) for k in b), np.uint8).reshape(-1, 16)
+        sizes, found = store.get_ptrs(keys, np.array([o.data_ptr() for o in outs], np.uint64),
+                                      np.full(8, S, np.uint64), True)
+        assert list(found) == w
+        for k, o in zip(b, outs):
+            assert np.array_equal(o.cpu().numpy(), blocks[ids.index(k)])
+    st = store.get_stats()
+    gpu_hits = st.gpu_hits if cls == "cascade" else st.local_gpu_hits
+    dram_hits = st.shm_hits if cls == "cascade" else st.local_dram_hits
+    promos = st.promotions_to_gpu if cls == "cascade" else st.promotions_to_local
+    assert (gpu_hits, dram_hits, promos) == (ctr["local_gpu_hits"], ctr["local_dram_hits"],
+                                             ctr["promotions_to_local"])
+    if cls == "dist":
+        assert promos == 0 and dram_hits > 0
+        assert [store.locate(i).is_gpu for i in ids] == [model.tier(i) == "hbm" for i in ids]
+    else:
+        assert promos > 0
+
+
 def test_explicit_evict_then_get():
     S = 1 << 20
     store = make_store(hbm=16 * S, dram=16 * S)

@@ -104,3 +104,22 @@ def test_tier_model_protection_rule():
     assert [k for k in m.hbm] == ["p1", "p2", "p3", "n5"]
     assert [k for k in m.dram] == ["p0", "n0", "n1", "n2", "n3", "n4"]
     assert m.evictions == 6
+
+
+def test_locality_tracker_follows_the_reference_rule():
+    # EMA updates once per window of 8 accesses: after one all-remote window
+    # the EMA is 0.3 (no promotion), after two it is 0.3 + 0.7 * 0.3 = 0.51
+    t = O.LocalityTracker(threshold=3)
+    for i in range(15):
+        t.record("a", remote=True)
+        assert not t.should_promote("a"), i
+    t.record("a", remote=True)
+    assert t.should_promote("a")
+    # local accesses only: the EMA stays 0, never promoted
+    for _ in range(100):
+        t.record("b", remote=False)
+    assert not t.should_promote("b")
+    # half remote windows: EMA converges to 0.5 from below, never > 0.5
+    for i in range(400):
+        t.record("c", remote=i % 2 == 0)
+    assert not t.should_promote("c")
