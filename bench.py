@@ -182,21 +182,33 @@ def make_store(args, device_index, capacity, dht=False):
     return cascade_cpp.DistributedStore(cfg)
 
 
-def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_memory=True):
+def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_memory=True, pipelined=True,
+             keys_all=None):
     """One step: put everything in batches, then get every stored key in a
-    shuffled order into out_buf (one batch at a time). Returns (put_s, get_s,
-    put_bytes, get_bytes) measured with CUDA events on the current stream."""
+    shuffled order into out_buf (one batch at a time). Device blocks go
+    through the pipelined put (each batch's SHA-256 launched at submission,
+    batches placed in order; one wait at the end) and the stream-ordered get;
+    host blocks through the synchronous calls. Returns (put_s, get_s,
+    put_bytes, get_bytes) measured with CUDA events on the current stream
+    (the put phase ends with a host wait for every placement)."""
     import torch
     n = len(ptrs)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-    keys_all = np.empty((n, 16), np.uint8)
+    if keys_all is None:
+        keys_all = np.empty((n, 16), np.uint8)
     ev[0].record()
     for i in range(0, n, batch):
         if _TRACE["on"] and (i // batch) % 16 == 0:
             trace(None, f"  put batch {i // batch}")
-        k, _ = store.put_ptrs(ptrs[i:i + batch], sizes[i:i + batch], device_memory,
-                              prefix=prefix[i:i + batch])
-        keys_all[i:i + batch] = k
+        if device_memory and pipelined:
+            store.put_ptrs_async(ptrs[i:i + batch], sizes[i:i + batch], keys_out=keys_all[i:i + batch],
+                                 prefix=prefix[i:i + batch])
+        else:
+            k, _ = store.put_ptrs(ptrs[i:i + batch], sizes[i:i + batch], device_memory,
+                                  prefix=prefix[i:i + batch])
+            keys_all[i:i + batch] = k
+    if device_memory and pipelined:
+        store.wait_puts()
     ev[1].record()
     uk = np.unique(keys_all.view(np.dtype((np.void, 16))).reshape(-1))
     order = np.random.default_rng(rng_seed).permutation(len(uk))
@@ -211,13 +223,17 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
         t = torch.tensor([n_get], dtype=torch.int64, device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         n_get = int(t.item())
+    caps = np.full(batch, size, np.uint64)
     for j in range(n_get):
         i = j * batch
         if _TRACE["on"] and j % 16 == 0:
             trace(None, f"  get batch {j} of {len(keys)} keys")
         kk = keys[i:i + batch]
         m = len(kk)
-        s, f = store.get_ptrs(kk, outs_b[:m], np.full(m, size, np.uint64), device_memory)
+        if device_memory and pipelined:
+            s, f = store.get_ptrs_async(kk, outs_b[:m], caps[:m])
+        else:
+            s, f = store.get_ptrs(kk, outs_b[:m], caps[:m], device_memory)
         ok = (f & 0x0F) != 0
         got += int(s[ok].sum())
     ev[2].record()
@@ -870,13 +886,19 @@ def config_dict(args):
 
 def batch_sweep(args, store, ptrs, sizes, prefix, out_buf, size):
     """batch_put / batch_get GB/s at batch 64 / 256 / 1024 on an 8192-block
-    slice of the same stream."""
+    slice of the same stream: the pipelined put and stream-ordered get (the
+    bench's path) and, beside them, the synchronous calls."""
     res = {}
     n = min(8192, len(ptrs))
     for b in (64, 256, 1024):
-        store.clear()
-        ps, gs, pb, gb = run_pass(store, ptrs[:n], sizes[:n], prefix[:n], b, out_buf, size, 7)
-        res[str(b)] = {"put_gbs": round(pb / ps / GB, 3), "get_gbs": round(gb / gs / GB, 3)}
+        r = {}
+        for mode, pipelined in (("", True), ("sync_", False)):
+            store.clear()
+            ps, gs, pb, gb = run_pass(store, ptrs[:n], sizes[:n], prefix[:n], b, out_buf, size, 7,
+                                      pipelined=pipelined)
+            r[mode + "put_gbs"] = round(pb / ps / GB, 3)
+            r[mode + "get_gbs"] = round(gb / gs / GB, 3)
+        res[str(b)] = r
     store.clear()
     return res
 

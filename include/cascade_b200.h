@@ -82,7 +82,8 @@ typedef struct cb_config {
   int32_t promotion_rule;       /* which DRAM-tier get hits promote_on_hit
                                    moves back to HBM: CB_PROMOTE_*          */
   int32_t reserved32;
-  uint64_t reserved[1];
+  uint64_t pipeline_blocks;     /* cb_put_batch_async: blocks whose SHA-256
+                                   may run ahead of placement (0 = 16384)   */
 } cb_config;
 
 /* cb_config.promotion_rule. CB_PROMOTE_EVERY_HIT: every DRAM-tier hit of a
@@ -250,7 +251,55 @@ int cb_sync(cb_store *s);
  * after its batch was planned puts the store in that state. */
 #define CB_SELFTEST_HASH_WAIT 1
 #define CB_SELFTEST_FAIL_MOVES 2
+/* CB_SELFTEST_GET_ERROR: the next cb_get_batch_async adds one descriptor
+ * whose copy kernel reports a device-side error without touching memory;
+ * the next settling call (cb_sync, any synchronous data call) returns
+ * CB_ERR_DEVICE, and the store stays usable. */
+#define CB_SELFTEST_GET_ERROR 3
 int cb_selftest(cb_store *s, int32_t which);
+
+/* ---- stream-ordered (pipelined) puts and gets --------------------------- */
+
+/* Pipelined batched put: the GPU form of CascadeStore::put_batch's OpenMP
+ * loop over the batch (src/cascade_core.cpp:1358-1373), with the results of
+ * DistributedStore::put_batch (src/distributed_backend.cpp:813-841). The
+ * call launches the batch's SHA-256 (after prior work on `stream`) and
+ * returns at once with *ticket_out; batches are placed (sequential dedup,
+ * tier moves, scatter, index insert) strictly in ticket order, so IDs,
+ * statuses and dedup counts equal those of the same batches put one by one
+ * with cb_put_batch. keys_out / status_out (may be NULL) are written when the
+ * batch is placed: at the latest when cb_put_wait covers its ticket, or when
+ * any other data call of the store runs; they must stay valid until then,
+ * and the blocks must stay unchanged until then. Up to
+ * cb_config.pipeline_blocks blocks hash ahead of placement. CB_MEM_HOST
+ * blocks are placed before the call returns. On a DHT member every rank
+ * must submit the same number of batches (n may be 0) and wait on the same
+ * tickets: placement there is collective. */
+int cb_put_batch_async(cb_store *s, const void *const *ptrs, const uint64_t *sizes,
+                       const uint8_t *is_prefix, const uint8_t *keys_in, int32_t n, int32_t mem_kind,
+                       uint8_t *keys_out, uint8_t *status_out, uint64_t *ticket_out, void *stream);
+
+/* Places every batch up to `ticket` (0: every batch submitted) and waits for
+ * their device work; *placed_out (may be NULL) = highest ticket placed. A
+ * device-side error of a placement is returned here and leaves the store
+ * refusing data calls until cb_clear. */
+int cb_put_wait(cb_store *s, uint64_t ticket, uint64_t *placed_out);
+
+/* Highest ticket placed so far, without waiting. */
+int cb_put_placed(cb_store *s, uint64_t *placed_out);
+
+/* Stream-ordered batched get into device buffers outs[i] (out_caps[i]
+ * bytes): found_out / sizes_out are final when the call returns; the bytes
+ * land in stream order on `stream`. When every requested block is in the
+ * HBM tier (or missing) the call builds the gather from the host metadata -
+ * no device lookup, no device round trip - and returns without waiting;
+ * other batches (DRAM-tier blocks, DHT members) take the synchronous path
+ * of cb_get_batch. A device-side error of the gather is returned by the next
+ * settling call (cb_sync, cb_put_wait, any synchronous data call). Sees every
+ * put submitted before it. Same results as cb_get_batch
+ * (DistributedStore::get_batch, src/distributed_backend.cpp:844-870). */
+int cb_get_batch_async(cb_store *s, const uint8_t *keys, int32_t n, void *const *outs,
+                       const uint64_t *out_caps, uint64_t *sizes_out, uint8_t *found_out, void *stream);
 
 /* Size of the opaque NCCL unique id blob. */
 #define CB_UID_BYTES 128
@@ -279,6 +328,32 @@ int cb_sync_metadata(cb_store *s);
 
 /* Rank and world size (1-GPU stores: 0 and 1). */
 int cb_rank(const cb_store *s, int32_t *rank, int32_t *world);
+
+/* Writer side of the DHT routing, host-only: owner_out[i] = owner rank of
+ * key i (cb_owner_rank), order_out = the batch indices in the order they
+ * are sent (grouped by owner rank, batch order inside a group), counts_out
+ * [world] = keys per owner. cb_put_batch / cb_get_batch on a DHT member route
+ * with this function. Replaces the per-block target choice of
+ * DistributedGPUBackend::get_target_node (src/distributed_backend.cpp:
+ * 396-398) for a whole batch. */
+int cb_dht_route(const uint8_t *keys, int32_t n, int32_t world, int32_t *owner_out, int32_t *order_out,
+                 uint32_t *counts_out);
+
+/* Owner side of a DHT put step without a GPU: a planner holds an owner's
+ * host policy (HBM pool and DRAM arena capacities, prefix-protected
+ * eviction, dedup); cb_dht_plan_put applies n requests (16-byte key, size,
+ * prefix flag) received in (source rank, batch index) order with the
+ * sequential dedup rule of DistributedStore::put
+ * (src/distributed_backend.cpp:604-608) and returns status_out[i]
+ * (CB_PUT_*) and loc_out[i] (pool offset of a stored block, bit 63 set for
+ * the DRAM tier; 0 otherwise). It is the function a DHT owner runs inside
+ * cb_put_batch; tier moves it plans are not executed here. */
+typedef struct cb_planner cb_planner;
+int cb_planner_create(uint64_t gpu_capacity_bytes, uint64_t dram_capacity_bytes, int32_t semantic_eviction,
+                      int32_t dedup_enabled, cb_planner **out);
+int cb_planner_destroy(cb_planner *p);
+int cb_dht_plan_put(cb_planner *p, const uint8_t *keys, const uint64_t *sizes, const uint8_t *prefix,
+                    int32_t n, uint8_t *status_out, uint64_t *loc_out);
 
 /* Owner rank of a key in a `world`-rank DHT: the first 8 key bytes read as a
  * big-endian integer, modulo world. Host-only, no GPU needed. Replaces

@@ -17,7 +17,8 @@ INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "cascade_cpp", "libcascade_b200.so")
 
-SOURCES = ["sha256.cu", "copy.cu", "kvquant.cu", "index.cu", "store.cu", "dht.cu", "policy.cpp", "noalloc.cu"]
+SOURCES = ["sha256.cu", "copy.cu", "kvquant.cu", "index.cu", "store.cu", "pipeline.cu", "dht.cu", "policy.cpp",
+           "noalloc.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

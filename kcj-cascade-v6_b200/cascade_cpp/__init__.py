@@ -41,6 +41,7 @@ __all__ = [
     "DistributedConfig", "DistributedStore", "DistributedStats", "BlockLocation",
     "CascadeConfig", "CascadeStore", "CascadeStats", "compute_block_id",
     "compute_block_ids", "block_id_to_key", "key_to_block_id", "CascadeError", "KVCompressor",
+    "PutFuture", "DhtPlanner", "dht_route",
 ]
 
 _lib_handle = None
@@ -78,6 +79,60 @@ def owner_rank(block_id: str, world: int) -> int:
     """Rank that owns ``block_id`` in a ``world``-rank DHT (cb_owner_rank)."""
     k = np.frombuffer(block_id_to_key(block_id), np.uint8).copy()
     return int(_native_lib().cb_owner_rank(C.c_void_p(k.ctypes.data), int(world)))
+
+
+def dht_route(keys: np.ndarray, world: int):
+    """Writer-side DHT routing of a batch of 16-byte keys (cb_dht_route):
+    (owner per key, send order grouped by owner in batch order, keys per
+    owner). Host-only."""
+    keys = np.ascontiguousarray(keys, np.uint8).reshape(-1, 16)
+    n = len(keys)
+    owner = np.zeros(n, np.int32)
+    order = np.zeros(n, np.int32)
+    counts = np.zeros(int(world), np.uint32)
+    rc = _native_lib().cb_dht_route(_ptr(keys), n, int(world), _ptr(owner), _ptr(order), _ptr(counts))
+    if rc:
+        raise CascadeError(rc, "cb_dht_route: bad arguments")
+    return owner, order, counts
+
+
+class DhtPlanner:
+    """A DHT owner's host policy without a GPU (cb_planner_create /
+    cb_dht_plan_put): the function an owner runs on the requests of one put
+    step, in (source rank, batch index) order."""
+
+    def __init__(self, gpu_capacity: int, dram_capacity: int = 0, semantic_eviction: bool = True,
+                 dedup_enabled: bool = True):
+        self._lib = _native_lib()
+        self._p = C.c_void_p()
+        rc = self._lib.cb_planner_create(int(gpu_capacity), int(dram_capacity), int(bool(semantic_eviction)),
+                                         int(bool(dedup_enabled)), C.byref(self._p))
+        if rc:
+            raise CascadeError(rc, "cb_planner_create failed")
+
+    def plan_put(self, keys: np.ndarray, sizes: np.ndarray, prefix: np.ndarray | None = None):
+        """-> (status per request: CB_PUT_*, location word per request)."""
+        keys = np.ascontiguousarray(keys, np.uint8).reshape(-1, 16)
+        n = len(keys)
+        sizes = np.ascontiguousarray(sizes, np.uint64)
+        pf = None if prefix is None else np.ascontiguousarray(prefix, np.uint8)
+        status = np.zeros(n, np.uint8)
+        loc = np.zeros(n, np.uint64)
+        rc = self._lib.cb_dht_plan_put(self._p, _ptr(keys), _ptr(sizes), _ptr(pf), n, _ptr(status), _ptr(loc))
+        if rc:
+            raise CascadeError(rc, "cb_dht_plan_put failed")
+        return status, loc
+
+    def close(self):
+        if self._p:
+            self._lib.cb_planner_destroy(self._p)
+            self._p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 # ------------------------------------------------------------------ buffers
@@ -163,6 +218,31 @@ class _Native:
         found = np.zeros(n, np.uint8)
         self._check(self.lib.cb_get_batch(self.h, _ptr(keys), n, _ptr(outs), _ptr(caps), kind,
                                           _ptr(sizes), _ptr(found), self.stream_ptr(kind)))
+        return sizes, found
+
+    def put_async(self, ptrs, sizes, kind, keys_out, status_out, keys_in=None, prefix=None) -> int:
+        t = C.c_uint64(0)
+        self._check(self.lib.cb_put_batch_async(self.h, _ptr(ptrs), _ptr(sizes), _ptr(prefix), _ptr(keys_in),
+                                                len(ptrs), kind, _ptr(keys_out), _ptr(status_out), C.byref(t),
+                                                self.stream_ptr(kind)))
+        return t.value
+
+    def put_wait(self, ticket: int = 0) -> int:
+        placed = C.c_uint64(0)
+        self._check(self.lib.cb_put_wait(self.h, int(ticket), C.byref(placed)))
+        return placed.value
+
+    def put_placed(self) -> int:
+        placed = C.c_uint64(0)
+        self._check(self.lib.cb_put_placed(self.h, C.byref(placed)))
+        return placed.value
+
+    def get_async(self, keys, outs, caps):
+        n = len(keys)
+        sizes = np.zeros(n, np.uint64)
+        found = np.zeros(n, np.uint8)
+        self._check(self.lib.cb_get_batch_async(self.h, _ptr(keys), n, _ptr(outs), _ptr(caps), _ptr(sizes),
+                                                _ptr(found), self.stream_ptr(L.CB_MEM_DEVICE)))
         return sizes, found
 
     def kv_compress(self, srcs, sizes, dsts):
@@ -487,6 +567,17 @@ class _StoreBase:
         self._n = _Native(cfg)
         self._device = cfg.device
         self._strkeys: dict[bytes, str] = {}
+        # pipelined puts: ticket -> what the library reads or writes when the
+        # batch is placed (inputs, output arrays), kept alive until then
+        self._inflight: dict[int, tuple] = {}
+
+    def _release_placed(self, placed: int | None = None):
+        if not self._inflight:
+            return
+        if placed is None:
+            placed = self._n.put_placed()
+        for t in [t for t in self._inflight if t <= placed]:
+            del self._inflight[t]
 
     # -- ids
     def _key(self, block_id: str) -> bytes:
@@ -576,6 +667,77 @@ class _StoreBase:
         return self._n.put(np.ascontiguousarray(ptrs, np.uint64), np.ascontiguousarray(sizes, np.uint64),
                            kind, keys_in=keys, prefix=prefix)
 
+    def put_ptrs_async(self, ptrs: np.ndarray, sizes: np.ndarray, keys_out: np.ndarray | None = None,
+                       status_out: np.ndarray | None = None, prefix: np.ndarray | None = None,
+                       keys: np.ndarray | None = None, device_memory: bool = True) -> int:
+        """Pipelined put of one batch of device blocks (cb_put_batch_async):
+        launches the batch's SHA-256 and returns a ticket at once; batches
+        are placed in ticket order (same IDs, statuses and dedup counts as
+        put_ptrs one batch after the other). ``keys_out`` ((n, 16) uint8) and
+        ``status_out`` ((n,) uint8), when given, are filled when the batch
+        is placed: after ``wait_puts`` covering the ticket, or any other
+        call of the store. The blocks must stay unchanged until then."""
+        ptrs = np.ascontiguousarray(ptrs, np.uint64)
+        sizes = np.ascontiguousarray(sizes, np.uint64)
+        for a, shape in ((keys_out, (len(ptrs), 16)), (status_out, (len(ptrs),))):
+            if a is not None and (a.dtype != np.uint8 or a.shape != shape or not a.flags.c_contiguous
+                                  or not a.flags.writeable):
+                raise ValueError(f"output must be a writable C-contiguous uint8 array of shape {shape}")
+        prefix = None if prefix is None else np.ascontiguousarray(prefix, np.uint8)
+        keys = None if keys is None else np.ascontiguousarray(keys, np.uint8)
+        kind = L.CB_MEM_DEVICE if device_memory else L.CB_MEM_HOST
+        t = self._n.put_async(ptrs, sizes, kind, keys_out, status_out, keys_in=keys, prefix=prefix)
+        self._inflight[t] = (keys_out, status_out)
+        self._release_placed()
+        return t
+
+    def wait_puts(self, ticket: int = 0) -> int:
+        """Places every pipelined batch up to ``ticket`` (0: all) and waits
+        for their device work. Returns the highest ticket placed."""
+        placed = self._n.put_wait(ticket)
+        self._release_placed(placed)
+        return placed
+
+    def batch_put_async(self, blocks: Sequence, is_prefix: Sequence[bool] | None = None,
+                        ids: Sequence[str] | None = None) -> "PutFuture":
+        """Pipelined ``batch_put`` of CUDA tensors: returns a future at once;
+        ``future.result()`` gives the IDs (and statuses) once the batch is
+        placed. Batches are placed in submission order, so IDs, statuses and
+        dedup counts are those of ``batch_put`` called batch after batch."""
+        views = [_block_view(b) for b in blocks]
+        kind = self._check_device(views)
+        n = len(views)
+        ptrs = np.array([v[0] for v in views], np.uint64)
+        sizes = np.array([v[1] for v in views], np.uint64)
+        keys_in = self._keys(ids) if ids is not None else None
+        prefix = None if is_prefix is None else np.array([1 if p else 0 for p in is_prefix], np.uint8)
+        keys = np.empty((n, 16), np.uint8)
+        status = np.empty(n, np.uint8)
+        t = self._n.put_async(ptrs, sizes, kind, keys, status, keys_in=keys_in, prefix=prefix)
+        self._inflight[t] = (keys, status, views)
+        self._release_placed()
+        return PutFuture(self, t, keys, status, None if ids is None else list(ids))
+
+    def get_ptrs_async(self, keys: np.ndarray, outs: np.ndarray, caps: np.ndarray):
+        """Stream-ordered get into device buffers (cb_get_batch_async):
+        returns (sizes, found) final at once; the bytes land in order on the
+        current CUDA stream."""
+        return self._n.get_async(np.ascontiguousarray(keys, np.uint8), np.ascontiguousarray(outs, np.uint64),
+                                 np.ascontiguousarray(caps, np.uint64))
+
+    def batch_get_async(self, ids: Sequence[str], outs: Sequence):
+        """``batch_get`` into CUDA tensors, stream-ordered: (found, sizes)
+        are final when it returns, the bytes land in order on the current
+        CUDA stream (read them on that stream)."""
+        views = [_block_view(o, writable=True) for o in outs]
+        if len(views) != len(ids):
+            raise ValueError("ids and outs differ in length")
+        if self._check_device(views) != L.CB_MEM_DEVICE:
+            raise ValueError("batch_get_async writes CUDA tensors; use batch_get for host buffers")
+        sizes, found = self._n.get_async(self._keys(ids), np.array([v[0] for v in views], np.uint64),
+                                         np.array([v[1] for v in views], np.uint64))
+        return [(int(f) & 0x0F) != L.CB_FOUND_MISS for f in found], [int(s) for s in sizes]
+
     def get_views(self, ids: Sequence[str]):
         """Zero-copy batch_get: one CUDA uint8 tensor per ID that aliases the
         block where it sits in this store's HBM pool (no copy; for HBM hits no
@@ -620,12 +782,31 @@ class _StoreBase:
     def clear(self):
         self._n.clear()
         self._strkeys.clear()
+        self._inflight.clear()  # placed or dropped by the clear
 
     def flush(self):
         self._n.sync()
 
     def close(self):
         self._n.close()
+
+
+class PutFuture:
+    """Result of ``batch_put_async``: ``result()`` waits until the batch is
+    placed and returns its IDs (with ``return_status``, also the per-block
+    CB_PUT_* codes)."""
+
+    def __init__(self, store: "_StoreBase", ticket: int, keys: np.ndarray, status: np.ndarray, ids):
+        self._store, self.ticket, self._keys, self._status, self._ids = store, ticket, keys, status, ids
+
+    def done(self) -> bool:
+        return self._store._n.put_placed() >= self.ticket
+
+    def result(self, return_status: bool = False):
+        if not self.done():
+            self._store.wait_puts(self.ticket)
+        out = self._ids if self._ids is not None else [k.tobytes().hex() for k in self._keys]
+        return (out, self._status.tolist()) if return_status else out
 
 
 def _resolve_device(dev) -> int:

@@ -25,6 +25,7 @@ CB_PROMOTE_EVERY_HIT = 0
 CB_PROMOTE_LOCALITY = 1
 CB_SELFTEST_HASH_WAIT = 1
 CB_SELFTEST_FAIL_MOVES = 2
+CB_SELFTEST_GET_ERROR = 3
 
 CB_MEM_DEVICE = 0
 CB_MEM_HOST = 1
@@ -64,7 +65,7 @@ class cb_config(C.Structure):
         ("collective_timeout_ms", C.c_uint64),
         ("promotion_rule", C.c_int32),
         ("reserved32", C.c_int32),
-        ("reserved", C.c_uint64 * 1),
+        ("pipeline_blocks", C.c_uint64),
     ]
 
 
@@ -124,8 +125,16 @@ SIGNATURES = [
     ("cb_dht_barrier", C.c_int, [_P]),
     ("cb_sync_metadata", C.c_int, [_P]),
     ("cb_rank", C.c_int, [_P, C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    ("cb_put_batch_async", C.c_int, [_P, _P, _P, _P, _P, C.c_int32, C.c_int32, _P, _P, _P, _P]),
+    ("cb_put_wait", C.c_int, [_P, C.c_uint64, _P]),
+    ("cb_put_placed", C.c_int, [_P, _P]),
+    ("cb_get_batch_async", C.c_int, [_P, _P, C.c_int32, _P, _P, _P, _P, _P]),
     ("cb_hash_batch_noalloc", C.c_int, [C.c_int32, _P, _P, C.c_int32, _P, _P]),
     ("cb_owner_rank", C.c_int32, [_P, C.c_int32]),
+    ("cb_dht_route", C.c_int, [_P, C.c_int32, C.c_int32, _P, _P, _P]),
+    ("cb_planner_create", C.c_int, [C.c_uint64, C.c_uint64, C.c_int32, C.c_int32, C.POINTER(_P)]),
+    ("cb_planner_destroy", C.c_int, [_P]),
+    ("cb_dht_plan_put", C.c_int, [_P, _P, _P, _P, C.c_int32, _P, _P]),
 ]
 
 CB_NOALLOC_MAX_BLOCKS = 4096

@@ -75,10 +75,11 @@ struct CopyDesc {
   uint64_t src;
   uint64_t dst;
   uint64_t size;
-  uint64_t flags;  // kCopyHost | kCopyUnpack
+  uint64_t flags;  // kCopyHost | kCopyUnpack | kCopyFault
 };
 constexpr uint64_t kCopyHost = 1;    // either side is host or peer memory (no TMA)
 constexpr uint64_t kCopyUnpack = 2;  // src is an INT8-packed block; size = unpacked bytes
+constexpr uint64_t kCopyFault = 4;   // self-test: report kErrBounds, touch no memory
 
 // Result of a device lookup for one get request.
 struct GetResult {

@@ -92,9 +92,12 @@ CB_D void copy_range_lsu(const uint8_t *s, uint8_t *d, uint64_t len, int tid, in
   }
 }
 
-// One unit of a descriptor through the LSU: a plain copy or an unpack.
-CB_D void lsu_unit(const CopyDesc &d, uint64_t off, uint64_t len, int tid, int nt) {
-  if (d.flags & kCopyUnpack) {
+// One unit of a descriptor through the LSU: a plain copy or an unpack (or,
+// for a self-test descriptor, an error report without any memory access).
+CB_D void lsu_unit(const CopyDesc &d, uint64_t off, uint64_t len, int tid, int nt, unsigned *err) {
+  if (d.flags & kCopyFault) {
+    if (tid == 0 && off == 0) atomicOr(err, kErrBounds);
+  } else if (d.flags & kCopyUnpack) {
     unpack_range(reinterpret_cast<const uint8_t *>(d.src), reinterpret_cast<uint8_t *>(d.dst), off, len, tid,
                  nt);
   } else {
@@ -105,7 +108,7 @@ CB_D void lsu_unit(const CopyDesc &d, uint64_t off, uint64_t len, int tid, int n
 
 __global__ void __launch_bounds__(kLsuThreads, kLsuCtasPerSm) copy_lsu_kernel(const CopyDesc *__restrict__ desc,
                                                                const uint32_t *__restrict__ unit_start,
-                                                               int n, uint32_t total_units) {
+                                                               int n, uint32_t total_units, unsigned *err) {
   uint32_t u0, u1;
   cta_unit_range(total_units, u0, u1);
   if (u0 >= u1) return;
@@ -116,7 +119,7 @@ __global__ void __launch_bounds__(kLsuThreads, kLsuCtasPerSm) copy_lsu_kernel(co
     const uint64_t off = (uint64_t)(u - unit_start[i]) * kCopyUnit;
     if (off >= d.size) continue;
     const uint64_t len = min(kCopyUnit, d.size - off);
-    lsu_unit(d, off, len, threadIdx.x, blockDim.x);
+    lsu_unit(d, off, len, threadIdx.x, blockDim.x, err);
   }
 }
 
@@ -175,7 +178,7 @@ struct PieceIter {
 };
 
 CB_D bool tma_unit(const CopyDesc &d, uint64_t off) {
-  return !(d.flags & (kCopyHost | kCopyUnpack)) && (((d.src + off) | (d.dst + off)) & 15) == 0;
+  return !(d.flags & (kCopyHost | kCopyUnpack | kCopyFault)) && (((d.src + off) | (d.dst + off)) & 15) == 0;
 }
 
 // Next TMA piece (<= kTmaStageBytes, 16-byte multiple) of the CTA's range.
@@ -221,7 +224,7 @@ __global__ void __launch_bounds__(32) copy_tma_kernel(const CopyDesc *__restrict
       if (off >= d.size) continue;
       const uint64_t len = min(kCopyUnit, d.size - off);
       if (!tma_unit(d, off)) {
-        lsu_unit(d, off, len, lane, 32);
+        lsu_unit(d, off, len, lane, 32, err);
       } else if (len & 15) {
         const uint8_t *s = reinterpret_cast<const uint8_t *>(d.src) + off;
         uint8_t *t = reinterpret_cast<uint8_t *>(d.dst) + off;
@@ -300,7 +303,7 @@ cudaError_t launch_batch_copy(const CopyDesc *d_desc, const uint32_t *d_unit_sta
   if (engine == 2) {
     const int cps = lsu_ctas_per_sm > 0 && lsu_ctas_per_sm < kLsuCtasPerSm ? lsu_ctas_per_sm : kLsuCtasPerSm;
     const uint32_t grid = min(total_units, (uint32_t)(num_sms * cps));
-    copy_lsu_kernel<<<grid, kLsuThreads, 0, stream>>>(d_desc, d_unit_start, n, total_units);
+    copy_lsu_kernel<<<grid, kLsuThreads, 0, stream>>>(d_desc, d_unit_start, n, total_units, d_err);
     return cudaGetLastError();
   }
   static thread_local int configured_device = -1;

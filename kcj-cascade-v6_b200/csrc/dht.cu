@@ -59,6 +59,36 @@ inline uint64_t be_owner(const HKey &k, int world) {
 
 }  // namespace
 
+// Writer side of a DHT batch: the owner rank of every key, the order in
+// which the keys are sent (grouped by owner, batch order inside a group) and
+// the number of keys per owner. The requests an owner receives are
+// therefore in (source rank, batch index) order.
+void dht_route(const HKey *keys, int n, int W, int *owner, int *order, uint32_t *scount) {
+  for (int r = 0; r < W; ++r) scount[r] = 0;
+  for (int i = 0; i < n; ++i) {
+    owner[i] = (int)be_owner(keys[i], W);
+    scount[owner[i]]++;
+  }
+  std::vector<uint32_t> pos(W, 0);
+  for (int r = 1; r < W; ++r) pos[r] = pos[r - 1] + scount[r - 1];
+  for (int i = 0; i < n; ++i) order[pos[owner[i]]++] = i;
+}
+
+// Owner side of a DHT put step: the requests of every rank, in (source
+// rank, batch index) order, go through the owner's policy with the
+// sequential dedup rule of DistributedStore::put (src/distributed_backend.cpp:
+// 604-608) - among equal keys of one step the lowest (rank, index) is stored,
+// every other one is a dedup hit - and get one reply each {status, location}.
+void dht_owner_plan(Policy &policy, const HKey *keys, const uint64_t *sizes, const uint8_t *prefix, uint32_t n,
+                    bool dedup, PutPlan &plan, uint32_t *status, uint64_t *loc) {
+  policy.plan_put(keys, sizes, prefix, (int)n, dedup, plan);
+  for (uint32_t j = 0; j < n; ++j) {
+    status[j] = plan.status[j];
+    loc[j] = 0;
+  }
+  for (const Placement &p : plan.places) loc[p.idx] = p.off | (p.tier == kTierDram ? kLocDram : 0);
+}
+
 struct DhtState {
   ncclComm_t comm = nullptr;
   int W = 1, me = 0;
@@ -414,13 +444,8 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   }
   // 2. bucket by owner (batch order inside each bucket)
   std::vector<uint32_t> scount(W, 0), rcount(W, 0);
-  std::vector<int> order(n);
-  for (int i = 0; i < n; ++i) scount[be_owner(keys[i], W)]++;
-  {
-    std::vector<uint32_t> pos(W, 0);
-    for (int r = 1; r < W; ++r) pos[r] = pos[r - 1] + scount[r - 1];
-    for (int i = 0; i < n; ++i) order[pos[be_owner(keys[i], W)]++] = i;
-  }
+  std::vector<int> order(n), kowner(n);
+  dht_route(keys.data(), n, W, kowner.data(), order.data(), scount.data());
   int rc = dht_counts(scount.data(), rcount.data(), st);
   if (rc) return rc;
   uint32_t nrecv = 0;
@@ -455,7 +480,10 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   rc = reserve_index(nrecv, st);
   if (rc) return rc;
   PutPlan &plan = put_plan;
-  policy.plan_put(okeys.data(), osizes.data(), oprefix.data(), (int)nrecv, cfg.dedup_enabled != 0, plan);
+  std::vector<uint32_t> ostatus(nrecv);
+  std::vector<uint64_t> oloc(nrecv);
+  dht_owner_plan(policy, okeys.data(), osizes.data(), oprefix.data(), nrecv, cfg.dedup_enabled != 0, plan,
+                 ostatus.data(), oloc.data());
   plan_open = true;
   rc = run_moves(plan.moves, plan.dropped, st);
   if (rc) {
@@ -463,14 +491,11 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
     return rc;
   }
   std::vector<PutRep> reps(nrecv);
-  for (uint32_t j = 0; j < nrecv; ++j) reps[j] = PutRep{0, plan.status[j], 0};
+  for (uint32_t j = 0; j < nrecv; ++j) reps[j] = PutRep{oloc[j], ostatus[j], 0};
   std::vector<IndexRec> ins;
   ins.reserve(plan.places.size());
-  for (const Placement &p : plan.places) {
-    const uint64_t loc = p.off | (p.tier == kTierDram ? kLocDram : 0);
-    reps[p.idx].loc = loc;
-    ins.push_back(IndexRec{p.key.lo, p.key.hi, loc, (p.size & kSizeMask) | (p.prefix ? kMetaPrefix : 0)});
-  }
+  for (const Placement &p : plan.places)
+    ins.push_back(IndexRec{p.key.lo, p.key.hi, oloc[p.idx], (p.size & kSizeMask) | (p.prefix ? kMetaPrefix : 0)});
   policy.commit();
   // replies reuse the request buffers (PutRep <= PutReq)
   memcpy(dht->h_recv.ptr, reps.data(), sizeof(PutRep) * nrecv);
@@ -505,7 +530,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   std::vector<uint8_t> status(n, CB_PUT_FAILED);
   for (int j = 0; j < n; ++j) {
     const int i = order[j];
-    const int owner = (int)be_owner(keys[i], W);
+    const int owner = kowner[i];
     status[i] = (uint8_t)mine[j].status;
     if (mine[j].status == CB_PUT_DEDUP) {
       remote_dedup_hits += cfg.dedup_enabled ? 1 : 0;
@@ -710,14 +735,10 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
   std::vector<uint32_t> scount(W, 0), rcount(W, 0);
   std::vector<int> order(n);
   owner.assign(n, 0);
-  for (int i = 0; i < n; ++i) {
-    owner[i] = (int)be_owner(to_hkey(keys + 16 * i), W);
-    scount[owner[i]]++;
-  }
   {
-    std::vector<uint32_t> pos(W, 0);
-    for (int r = 1; r < W; ++r) pos[r] = pos[r - 1] + scount[r - 1];
-    for (int i = 0; i < n; ++i) order[pos[owner[i]]++] = i;
+    std::vector<HKey> hk(n);
+    for (int i = 0; i < n; ++i) hk[i] = to_hkey(keys + 16 * i);
+    dht_route(hk.data(), n, W, owner.data(), order.data(), scount.data());
   }
   int rc = dht_counts(scount.data(), rcount.data(), st);
   if (rc) return rc;
@@ -1042,7 +1063,68 @@ int Store::dht_cluster_usage(cb_stats *o) {
 
 }  // namespace cb
 
+// Host-only planner: the DHT owner's policy without a GPU (cb_planner_*).
+struct cb_planner {
+  cb::Policy policy;
+  bool dedup;
+  cb::PutPlan plan;
+  cb_planner(uint64_t hbm, uint64_t dram, bool semantic, bool dd) : policy(hbm, dram, semantic), dedup(dd) {
+    policy.set_direct_dram_placement(false);  // as a DHT owner (cb_dht_attach)
+  }
+};
+
 extern "C" {
+
+int cb_dht_route(const uint8_t *keys, int32_t n, int32_t world, int32_t *owner_out, int32_t *order_out,
+                 uint32_t *counts_out) {
+  if (n < 0 || world < 1 || (n > 0 && (!keys || !owner_out || !order_out)) || !counts_out) return CB_ERR_ARG;
+  std::vector<cb::HKey> hk(n);
+  for (int i = 0; i < n; ++i) hk[i] = cb::to_hkey(keys + 16ull * i);
+  std::vector<int> owner(n), order(n);
+  cb::dht_route(hk.data(), n, world, owner.data(), order.data(), counts_out);
+  for (int i = 0; i < n; ++i) {
+    owner_out[i] = owner[i];
+    order_out[i] = order[i];
+  }
+  return CB_OK;
+}
+
+int cb_planner_create(uint64_t gpu_capacity_bytes, uint64_t dram_capacity_bytes, int32_t semantic_eviction,
+                      int32_t dedup_enabled, cb_planner **out) {
+  if (!out) return CB_ERR_ARG;
+  try {
+    *out = new cb_planner(gpu_capacity_bytes, dram_capacity_bytes, semantic_eviction != 0, dedup_enabled != 0);
+  } catch (...) {
+    *out = nullptr;
+    return CB_ERR_NOSPACE;
+  }
+  return CB_OK;
+}
+
+int cb_planner_destroy(cb_planner *p) {
+  delete p;
+  return CB_OK;
+}
+
+int cb_dht_plan_put(cb_planner *p, const uint8_t *keys, const uint64_t *sizes, const uint8_t *prefix, int32_t n,
+                    uint8_t *status_out, uint64_t *loc_out) {
+  if (!p || n < 0 || (n > 0 && (!keys || !sizes || !status_out || !loc_out))) return CB_ERR_ARG;
+  try {
+    std::vector<cb::HKey> hk(n);
+    for (int i = 0; i < n; ++i) hk[i] = cb::to_hkey(keys + 16ull * i);
+    std::vector<uint32_t> st(n);
+    std::vector<uint64_t> loc(n);
+    cb::dht_owner_plan(p->policy, hk.data(), sizes, prefix, (uint32_t)n, p->dedup, p->plan, st.data(), loc.data());
+    p->policy.commit();
+    for (int i = 0; i < n; ++i) {
+      status_out[i] = (uint8_t)st[i];
+      loc_out[i] = loc[i];
+    }
+  } catch (...) {
+    return CB_ERR_NOSPACE;
+  }
+  return CB_OK;
+}
 
 int cb_dht_unique_id(uint8_t *uid_out) {
   if (!uid_out) return CB_ERR_ARG;

@@ -1,0 +1,482 @@
+// Stream-ordered (pipelined) puts and gets of one store.
+//
+// A synchronous batch_put hashes its batch, plans it and scatters it before
+// it returns, so at most `batch` SHA-256 chains run at once: one chain per
+// block, 32 per CTA, 32 CTAs for a 1024-block batch on a 148-SM GPU. The
+// reference's CPU put_batch keeps every core busy at any batch size with
+// OpenMP over the batch (src/cascade_core.cpp:1358-1373); the GPU form of
+// that is to keep many batches hashing at once:
+//
+//  * cb_put_batch_async launches the batch's SHA-256 at submission on one of
+//    kHashSlots side streams (small batches queued back to back share one
+//    launch of up to kLaunchBlocks blocks) and returns a ticket;
+//  * batches are placed - sequential dedup plan, tier moves, scatter into the
+//    pool, index insert - strictly in ticket order, each as soon as its
+//    digests are back and, at the latest, when more than `pipeline_blocks`
+//    blocks are waiting, or when cb_put_wait / any other data call needs
+//    them. Placement in ticket order keeps the sequential dedup rule of
+//    DistributedStore::put_batch (src/distributed_backend.cpp:813-841)
+//    exactly: a block is a dedup hit iff its key was stored before it.
+//
+// On a DHT member the placement of a batch is the collective DHT put with
+// the digests as keys. Every rank must make the same sequence of calls, so
+// placement there is driven by batch counts alone (never by timing or block
+// counts, which differ between ranks): a batch is placed once kDhtPending
+// later batches were submitted, or at a wait.
+//
+// cb_get_batch_async serves the common case of a 1-GPU get without a device
+// round trip: when every requested block is in the HBM tier (or missing),
+// the host metadata - authoritative on one GPU - already holds each block's
+// pool offset and size, so the call builds the gather descriptors from it,
+// enqueues the gather on the caller's stream and returns with found/sizes
+// final and the bytes landing in stream order. A batch that touches the DRAM
+// tier takes the synchronous path. Pool extents a stream-ordered gather may
+// still read are protected: every later pool write (scatter, tier move)
+// waits for those gathers on the device (fence_reads).
+//
+// Device-side errors of stream-ordered work surface at the next call that
+// settles (cb_put_wait, cb_sync, and every synchronous data call): that call
+// returns the error. A failed placement leaves the host metadata ahead of
+// the pool, so the store then refuses data calls until cb_clear.
+#include <string.h>
+
+#include <algorithm>
+
+#include "kernels.cuh"
+#include "store.hpp"
+
+namespace cb {
+
+namespace {
+
+constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
+constexpr uint64_t kDefaultPipelineBlocks = 16384;  // blocks hashing ahead of placement (1 GPU)
+constexpr size_t kDhtPending = 8;                // DHT: batches submitted and not placed (every rank alike)
+constexpr int kScatterLsuCtasPerSm = 4;          // pipelined scatters share the SMs with the hashes
+
+inline size_t digest_offset(int cap) { return align_up(sizeof(HashJob) * (size_t)cap, 256); }
+
+}  // namespace
+
+int Store::pipeline_init() {
+  if (pipeline_ready) return CB_OK;
+  for (HashSlot &h : hslots) {
+    if (!h.stream) CB_TRY_CUDA(cudaStreamCreateWithFlags(&h.stream, cudaStreamNonBlocking), "hash stream");
+    if (!h.done) CB_TRY_CUDA(cudaEventCreateWithFlags(&h.done, cudaEventDisableTiming), "event");
+  }
+  for (ScratchSlot &s : sslots)
+    if (!s.done) CB_TRY_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "event");
+  if (!put_stream) CB_TRY_CUDA(cudaStreamCreateWithFlags(&put_stream, cudaStreamNonBlocking), "put stream");
+  if (!ev_submit) CB_TRY_CUDA(cudaEventCreateWithFlags(&ev_submit, cudaEventDisableTiming), "event");
+  if (!d_err_get) {
+    CB_TRY_CUDA(cudaMalloc(&d_err_get, sizeof(unsigned)), "error word");
+    CB_TRY_CUDA(cudaMemset(d_err_get, 0, sizeof(unsigned)), "error word");
+  }
+  pipeline_ready = true;
+  return CB_OK;
+}
+
+// Waits for everything the pipeline has in flight and forgets the batches
+// not placed yet (clear(), destruction).
+void Store::drop_pipeline() {
+  if (!pipeline_ready) return;
+  for (HashSlot &h : hslots) {
+    cudaStreamSynchronize(h.stream);
+    h.users = 0;
+    h.n = 0;
+    h.launched = false;
+  }
+  for (ScratchSlot &s : sslots) {
+    if (s.pending) cudaEventSynchronize(s.done);
+    s.pending = false;
+  }
+  cudaStreamSynchronize(put_stream);
+  aput.clear();
+  open_slot = -1;
+  inflight_blocks = 0;
+  placed_unsettled = false;
+  cudaGetLastError();
+}
+
+// Batches still queued are dropped (their outputs are never written).
+void Store::pipeline_release() {
+  for (HashSlot &h : hslots) {
+    if (h.stream) {
+      cudaStreamSynchronize(h.stream);
+      cudaStreamDestroy(h.stream);
+    }
+    if (h.done) cudaEventDestroy(h.done);
+    h.h.release();
+    h.d.release();
+    h = HashSlot{};
+  }
+  for (ScratchSlot &s : sslots) {
+    if (s.done) {
+      cudaEventSynchronize(s.done);
+      cudaEventDestroy(s.done);
+    }
+    s.h.release();
+    s.d.release();
+    s = ScratchSlot{};
+  }
+  if (put_stream) {
+    cudaStreamSynchronize(put_stream);
+    cudaStreamDestroy(put_stream);
+    put_stream = nullptr;
+  }
+  if (ev_submit) cudaEventDestroy(ev_submit);
+  ev_submit = nullptr;
+  if (d_err_get) cudaFree(d_err_get);
+  d_err_get = nullptr;
+  aput.clear();
+  open_slot = -1;
+  pipeline_ready = false;
+}
+
+Store::ScratchSlot *Store::take_scratch(size_t bytes, int &rc) {
+  ScratchSlot &s = sslots[sslot_next];
+  sslot_next = (sslot_next + 1) % kScratchSlots;
+  rc = CB_OK;
+  if (s.pending) {  // its previous kernels must be done reading it
+    cudaError_t e = cudaEventSynchronize(s.done);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "stream-ordered kernel");
+      return nullptr;
+    }
+    s.pending = false;
+  }
+  cudaError_t e = s.h.ensure(bytes);
+  if (e == cudaSuccess) e = s.d.ensure(bytes);
+  if (e != cudaSuccess) {
+    rc = cuda_fail(e, "scratch");
+    return nullptr;
+  }
+  return &s;
+}
+
+int Store::fence_reads(cudaStream_t st) {
+  if (!pipeline_ready) return CB_OK;
+  for (ScratchSlot &s : sslots)
+    if (s.pending) CB_TRY_CUDA(cudaStreamWaitEvent(st, s.done, 0), "fence");
+  return CB_OK;
+}
+
+// ------------------------------------------------------------------ put
+
+int Store::launch_open_slot() {
+  if (open_slot < 0) return CB_OK;
+  HashSlot &h = hslots[open_slot];
+  open_slot = -1;
+  const size_t o_dig = digest_offset(h.cap);
+  uint8_t *hp = static_cast<uint8_t *>(h.h.ptr);
+  uint8_t *dp = static_cast<uint8_t *>(h.d.ptr);
+  uint64_t bytes = 0;
+  const HashJob *jobs = reinterpret_cast<const HashJob *>(hp);
+  for (int i = 0; i < h.n; ++i) bytes += jobs[i].size;
+  CB_TRY_CUDA(cudaMemcpyAsync(dp, hp, sizeof(HashJob) * h.n, cudaMemcpyHostToDevice, h.stream), "H2D jobs");
+  CB_TRY_CUDA(timed(0, bytes, h.stream,
+                    [&] {
+                      return launch_sha256_batch(reinterpret_cast<const HashJob *>(dp), h.n,
+                                                 reinterpret_cast<uint32_t *>(dp + o_dig), hash_lanes, d_err,
+                                                 h.stream);
+                    }),
+              "sha256 launch");
+  CB_TRY_CUDA(cudaMemcpyAsync(hp + o_dig, dp + o_dig, 32ull * h.n, cudaMemcpyDeviceToHost, h.stream), "D2H digests");
+  CB_TRY_CUDA(cudaEventRecord(h.done, h.stream), "event");
+  h.launched = true;
+  return CB_OK;
+}
+
+int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix, const uint8_t *keys_in,
+                     int n, uint8_t *keys_out, uint8_t *status_out, uint64_t *ticket, cudaStream_t st) {
+  int rc = pipeline_init();
+  if (rc) return rc;
+  AsyncPut b;
+  b.ticket = next_ticket;
+  b.ptrs.assign(ptrs, ptrs + n);
+  b.sizes.assign(sizes, sizes + n);
+  if (is_prefix) b.prefix.assign(is_prefix, is_prefix + n);
+  if (keys_in) b.keys_in.assign(keys_in, keys_in + 16ull * n);
+  b.keys_out = keys_out;
+  b.status_out = status_out;
+  if (!keys_in && n > 0) {
+    // A DHT member gives every batch its own launch, so that slot reuse
+    // (and the placements it may force) happens at the same call on every
+    // rank; one GPU queues small batches into a shared launch.
+    if (open_slot >= 0 && (dht || hslots[open_slot].n + n > hslots[open_slot].cap)) {
+      rc = launch_open_slot();
+      if (rc) return rc;
+    }
+    if (open_slot < 0) {
+      const int s = hslot_next;
+      while (hslots[s].users > 0) {  // its batches are the oldest in flight: place them
+        rc = place_oldest();
+        if (rc) return rc;
+      }
+      HashSlot &h = hslots[s];
+      const int cap = std::max(n, kLaunchBlocks);
+      const size_t bytes = digest_offset(cap) + 32ull * cap;
+      CB_TRY_CUDA(h.h.ensure(bytes), "pinned hash slot");
+      CB_TRY_CUDA(h.d.ensure(bytes), "device hash slot");
+      h.cap = cap;
+      h.n = 0;
+      h.users = 0;
+      h.launched = false;
+      open_slot = s;
+      hslot_next = (s + 1) % kHashSlots;
+    }
+    HashSlot &h = hslots[open_slot];
+    HashJob *jobs = static_cast<HashJob *>(h.h.ptr) + h.n;
+    for (int i = 0; i < n; ++i) jobs[i] = HashJob{ptrs[i], sizes[i]};
+    b.slot = open_slot;
+    b.off = h.n;
+    h.n += n;
+    h.users++;
+    // the hash reads the blocks after the caller's earlier work on st
+    CB_TRY_CUDA(cudaEventRecord(ev_submit, st), "event");
+    CB_TRY_CUDA(cudaStreamWaitEvent(h.stream, ev_submit, 0), "wait");
+    if (dht || h.n >= kLaunchBlocks) {
+      rc = launch_open_slot();
+      if (rc) return rc;
+    }
+  }
+  next_ticket++;
+  *ticket = b.ticket;
+  inflight_blocks += (uint64_t)n;
+  aput.push_back(std::move(b));
+  if (dht) {
+    while (aput.size() > kDhtPending) {
+      rc = place_oldest();
+      if (rc) return rc;
+    }
+    return CB_OK;
+  }
+  const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultPipelineBlocks;
+  while (!aput.empty() && inflight_blocks > limit) {
+    rc = place_oldest();
+    if (rc) return rc;
+  }
+  // place whatever is ready, so placements keep pace with the hashes
+  while (!aput.empty()) {
+    const AsyncPut &f = aput.front();
+    if (f.slot >= 0) {
+      const HashSlot &h = hslots[f.slot];
+      if (!h.launched) break;
+      const cudaError_t q = cudaEventQuery(h.done);
+      if (q == cudaErrorNotReady) break;
+      if (q != cudaSuccess) return cuda_fail(q, "hash");
+    }
+    rc = place_oldest();
+    if (rc) return rc;
+  }
+  return CB_OK;
+}
+
+// Places the oldest submitted batch (waiting for its digests if need be).
+int Store::place_oldest() {
+  AsyncPut &b = aput.front();
+  const int n = (int)b.sizes.size();
+  std::vector<HKey> keys(n);
+  int rc = CB_OK;
+  if (b.slot >= 0) {
+    HashSlot &h = hslots[b.slot];
+    if (!h.launched) {
+      rc = launch_open_slot();  // b is among the open slot's batches
+      if (rc) return rc;
+    }
+    CB_TRY_CUDA(cudaEventSynchronize(h.done), "pipelined hash");
+    const uint8_t *dig = static_cast<const uint8_t *>(h.h.ptr) + digest_offset(h.cap) + 32ull * b.off;
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32ull * i);
+  } else {
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(b.keys_in.data() + 16ull * i);
+  }
+  if (dht) {
+    std::vector<uint8_t> k16(16ull * n);
+    for (int i = 0; i < n; ++i) {
+      memcpy(k16.data() + 16ull * i, &keys[i].lo, 8);
+      memcpy(k16.data() + 16ull * i + 8, &keys[i].hi, 8);
+    }
+    rc = dht_put(reinterpret_cast<const void *const *>(b.ptrs.data()), b.sizes.data(),
+                 b.prefix.empty() ? nullptr : b.prefix.data(), k16.data(), n, CB_MEM_DEVICE, b.keys_out, b.status_out,
+                 put_stream);
+  } else {
+    rc = n ? place_batch(keys, b) : CB_OK;
+  }
+  if (rc) return rc;
+  if (b.slot >= 0) hslots[b.slot].users--;
+  inflight_blocks -= (uint64_t)n;
+  placed_ticket = b.ticket;
+  aput.pop_front();
+  return CB_OK;
+}
+
+// 1 GPU: the synchronous put's plan and scatter, stream-ordered on
+// put_stream with descriptors in a scratch slot; nothing waits here.
+int Store::place_batch(const std::vector<HKey> &keys, AsyncPut &b) {
+  Trace tr("cb.place");
+  const int n = (int)keys.size();
+  int rc = reserve_index((uint64_t)n, put_stream);
+  if (rc) return rc;
+  PutPlan &plan = put_plan;
+  policy.plan_put(keys.data(), b.sizes.data(), b.prefix.empty() ? nullptr : b.prefix.data(), n,
+                  cfg.dedup_enabled != 0, plan);
+  plan_open = true;
+  rc = fence_reads(put_stream);  // extents a stream-ordered gather still reads
+  if (rc) return rc;
+  rc = run_moves(plan.moves, plan.dropped, put_stream);
+  if (rc) return rc;
+  if (!plan.places.empty()) {
+    ScratchSlot *sl = take_scratch(4096, rc);
+    if (!sl) return rc;
+    rc = enqueue_places(plan, b.ptrs.data(), put_stream, sl->h, sl->d, 2, kScatterLsuCtasPerSm);
+    if (rc) return rc;
+    CB_TRY_CUDA(cudaEventRecord(sl->done, put_stream), "event");
+    sl->pending = true;
+  }
+  policy.commit();
+  plan_open = false;
+  placed_unsettled = true;
+  for (int i = 0; i < n; ++i) {
+    if (b.keys_out) {
+      memcpy(b.keys_out + 16ull * i, &keys[i].lo, 8);
+      memcpy(b.keys_out + 16ull * i + 8, &keys[i].hi, 8);
+    }
+    if (b.status_out) b.status_out[i] = plan.status[i];
+  }
+  return CB_OK;
+}
+
+int Store::place_until(uint64_t ticket) {
+  while (!aput.empty() && aput.front().ticket <= ticket) {
+    const int rc = place_oldest();
+    if (rc) return rc;
+  }
+  return CB_OK;
+}
+
+// Device work of the placements made so far is complete; a device-side
+// error of one of them is returned (and, since the host metadata already
+// records those placements, leaves the store refusing data calls).
+int Store::finish_placements() {
+  if (!placed_unsettled) return CB_OK;
+  CB_TRY_CUDA(cudaStreamSynchronize(put_stream), "placements");
+  placed_unsettled = false;
+  const int rc = read_error_word(d_err, put_stream);
+  if (rc) plan_open = true;
+  return rc;
+}
+
+// Places every batch up to `ticket` (they need not be hashed yet) and
+// waits for their device work; later batches keep hashing.
+int Store::put_wait(uint64_t ticket) {
+  int rc = place_until(ticket);
+  if (rc) return rc;
+  return finish_placements();
+}
+
+int Store::settle() {
+  if (!pipeline_ready) return CB_OK;
+  if (!lost.empty()) {  // nothing more is placed on a store that lost its state
+    drop_pipeline();
+    return CB_OK;
+  }
+  int rc = place_until(UINT64_MAX);
+  if (rc) return rc;
+  bool gathers = false;
+  for (ScratchSlot &s : sslots) {
+    if (!s.pending) continue;
+    CB_TRY_CUDA(cudaEventSynchronize(s.done), "stream-ordered kernel");
+    s.pending = false;
+    gathers = true;
+  }
+  rc = finish_placements();
+  if (rc) return rc;
+  // an error of a stream-ordered get changed nothing in the store: report it
+  return gathers ? read_error_word(d_err_get, put_stream) : CB_OK;
+}
+
+// ------------------------------------------------------------------ get
+
+int Store::get_async(const uint8_t *keys, int n, const uint64_t *outs, const uint64_t *caps, uint64_t *sizes_out,
+                     uint8_t *found_out, cudaStream_t st) {
+  int rc = pipeline_init();
+  if (rc) return rc;
+  // every put submitted earlier is visible to this get
+  if (!aput.empty()) {
+    rc = place_until(UINT64_MAX);
+    if (rc) return rc;
+  }
+  std::vector<const BlockMeta *> meta(n);
+  for (int i = 0; i < n; ++i) {
+    meta[i] = policy.find(to_hkey(keys + 16ull * i));
+    if (meta[i] && meta[i]->tier != kTierHbm && meta[i]->size <= caps[i]) {
+      // a DRAM-tier block (and its promotion) takes the synchronous path
+      rc = settle();
+      if (rc) return rc;
+      return get_device(keys, n, outs, caps, sizes_out, found_out, st);
+    }
+  }
+  if (placed_unsettled) {  // the gather reads what the pipelined scatters wrote
+    CB_TRY_CUDA(cudaEventRecord(ev_submit, put_stream), "event");
+    CB_TRY_CUDA(cudaStreamWaitEvent(st, ev_submit, 0), "wait");
+  }
+  const bool inject = inject_get_error;
+  inject_get_error = false;
+  const int nd = n + (inject ? 1 : 0);
+  const size_t o_us = align_up(sizeof(CopyDesc) * nd, 256);
+  const size_t bytes = o_us + 4ull * (nd + 1);
+  ScratchSlot *sl = take_scratch(bytes, rc);
+  if (!sl) return rc;
+  uint8_t *h = static_cast<uint8_t *>(sl->h.ptr);
+  CopyDesc *desc = reinterpret_cast<CopyDesc *>(h);
+  uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
+  uint32_t total = 0;
+  uint64_t moved = 0;
+  for (int i = 0; i < n; ++i) {
+    const BlockMeta *m = meta[i];
+    us[i] = total;
+    if (!m) {
+      desc[i] = CopyDesc{0, 0, 0, 0};
+      sizes_out[i] = 0;
+      found_out[i] = CB_FOUND_MISS;
+      misses++;
+      continue;
+    }
+    local_gpu_hits++;
+    sizes_out[i] = m->size;
+    if (m->size > caps[i]) {
+      desc[i] = CopyDesc{0, 0, 0, 0};
+      found_out[i] = CB_FOUND_LOCAL_HBM | CB_FOUND_NOT_COPIED;
+      continue;
+    }
+    found_out[i] = CB_FOUND_LOCAL_HBM;
+    desc[i] = CopyDesc{(uint64_t)pool + m->off, outs[i], m->size, 0};
+    total += (uint32_t)((m->size + kCopyUnit - 1) / kCopyUnit);
+    moved += m->size;
+  }
+  if (inject) {  // self-test: one descriptor whose kernel reports an error
+    us[n] = total;
+    desc[n] = CopyDesc{0, 0, 16, kCopyFault};
+    total += 1;
+  }
+  us[nd] = total;
+  // LRU order: CascadeStore::get touches on hit (src/cascade_core.cpp:1281)
+  for (int i = 0; i < n; ++i)
+    if (meta[i]) policy.touch(to_hkey(keys + 16ull * i));
+  if (total) {
+    uint8_t *d = static_cast<uint8_t *>(sl->d.ptr);
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st), "H2D gather");
+    CB_TRY_CUDA(timed(2, moved, st,
+                      [&] {
+                        return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d),
+                                                 reinterpret_cast<const uint32_t *>(d + o_us), nd, total, copy_engine,
+                                                 d_err_get, num_sms, st);
+                      }),
+                "gather");
+    CB_TRY_CUDA(cudaEventRecord(sl->done, st), "event");
+    sl->pending = true;
+  }
+  return CB_OK;
+}
+
+}  // namespace cb

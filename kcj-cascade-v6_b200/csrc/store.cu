@@ -176,6 +176,7 @@ int Store::init() {
 Store::~Store() {
   if (device >= 0) cudaSetDevice(device);
   if (own_stream) cudaStreamSynchronize(own_stream);
+  pipeline_release();
   dht_detach();
   if (pool) cudaFree(pool);
   if (table) cudaFree(table);
@@ -276,36 +277,52 @@ int Store::reserve_index(uint64_t incoming, cudaStream_t st) {
 }
 
 cudaError_t Store::prof_event(cudaEvent_t &e) {
-  if (prof_events_used == prof_events.size()) {
+  if (prof_free.empty()) {
     cudaEvent_t ne;
     cudaError_t r = cudaEventCreate(&ne);
     if (r != cudaSuccess) return r;
     prof_events.push_back(ne);
+    e = ne;
+    return cudaSuccess;
   }
-  e = prof_events[prof_events_used++];
+  e = prof_free.back();
+  prof_free.pop_back();
   return cudaSuccess;
 }
 
-void Store::resolve_prof() {
-  for (const ProfRec &r : prof_pending) {
+// Launches still running on other streams (pipelined hashes) keep their
+// records pending unless `wait` is set.
+void Store::resolve_prof(bool wait) {
+  size_t keep = 0;
+  for (size_t k = 0; k < prof_pending.size(); ++k) {
+    const ProfRec r = prof_pending[k];
+    if (!wait && cudaEventQuery(r.b) == cudaErrorNotReady) {
+      prof_pending[keep++] = r;
+      continue;
+    }
     float ms = 0.f;
-    if (cudaEventSynchronize(r.b) != cudaSuccess || cudaEventElapsedTime(&ms, r.a, r.b) != cudaSuccess) continue;
-    prof_ns[r.kind] += (uint64_t)(ms * 1.0e6);
-    prof_bytes[r.kind] += r.bytes;
-    prof_launches[r.kind]++;
+    if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+      prof_ns[r.kind] += (uint64_t)(ms * 1.0e6);
+      prof_bytes[r.kind] += r.bytes;
+      prof_launches[r.kind]++;
+    }
+    prof_free.push_back(r.a);
+    prof_free.push_back(r.b);
   }
-  prof_pending.clear();
-  prof_events_used = 0;
+  prof_pending.resize(keep);
+  cudaGetLastError();  // a not-ready query leaves nothing sticky, but be sure
 }
 
 // Reads and clears the device error word (after a stream sync).
-int Store::check_device_error(cudaStream_t st) {
-  CB_TRY(cudaMemcpyAsync(h_err.ptr, d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "D2H err");
+int Store::check_device_error(cudaStream_t st) { return read_error_word(d_err, st); }
+
+int Store::read_error_word(unsigned *word, cudaStream_t st) {
+  CB_TRY(cudaMemcpyAsync(h_err.ptr, word, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "D2H err");
   CB_TRY(cudaStreamSynchronize(st), "stream sync");
   resolve_prof();
   const unsigned e = *static_cast<unsigned *>(h_err.ptr);
   if (!e) return CB_OK;
-  CB_TRY(cudaMemsetAsync(d_err, 0, sizeof(unsigned), st), "clear err");
+  CB_TRY(cudaMemsetAsync(word, 0, sizeof(unsigned), st), "clear err");
   CB_TRY(cudaStreamSynchronize(st), "stream sync");
   if (e & kErrTimeout) return fail(CB_ERR_TIMEOUT, "device wait timed out (error bits 0x%x)", e);
   return fail(CB_ERR_DEVICE, "device-side check failed (error bits 0x%x)", e);
@@ -594,30 +611,15 @@ int Store::hash_device(const uint64_t *ptrs, const uint64_t *sizes, int n, cudaS
 
 // ---------------------------------------------------------------- put
 
-int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
-                      const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
-                      cudaStream_t st, const HashProgress *pg, cudaEvent_t copies_done) {
-  Trace tr("cb.put");
-  std::vector<HKey> keys(n);
-  if (keys_in) {
-    if (copies_done) CB_TRY(cudaStreamWaitEvent(st, copies_done, 0), "wait copies");
-    for (int i = 0; i < n; ++i) keys[i] = to_hkey(keys_in + 16 * i);
-  } else {
-    int rc = hash_device(ptrs, sizes, n, st, pg, copies_done);
-    if (rc) return rc;
-    const uint8_t *dig = static_cast<const uint8_t *>(h_out.ptr);
-    for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32 * i);
-  }
-  int rc = reserve_index((uint64_t)n, st);
-  if (rc) return rc;
-  PutPlan &plan = put_plan;
-  policy.plan_put(keys.data(), sizes, is_prefix, n, cfg.dedup_enabled != 0, plan);
-  plan_open = true;
-  rc = run_moves(plan.moves, plan.dropped, st);
-  if (rc) return rc;
-
+// Scatter of a planned put into its tiers, stream-ordered on st: plain
+// copies (HBM, or DRAM without packing), blocks packed to INT8 straight into
+// the DRAM tier, then the index insert. Descriptors go through (hbuf, dbuf),
+// which must stay untouched until the kernels have run.
+int Store::enqueue_places(const PutPlan &plan, const uint64_t *ptrs, cudaStream_t st, PinnedBuf &hbuf,
+                          DevBuf &dbuf, int engine, int lsu_ctas_per_sm) {
   const int np = (int)plan.places.size();
-  if (np) {
+  if (!np) return CB_OK;
+  {
     bool need_dram = false;
     for (const auto &p : plan.places) need_dram |= p.tier == kTierDram;
     if (need_dram) {
@@ -635,9 +637,9 @@ int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t
     const size_t o_pus = L.add(sizeof(uint32_t) * (npk + 1));
     const size_t o_mm = L.add(sizeof(int) * 2 * npk);
     const size_t o_ins = L.add(sizeof(IndexRec) * np);
-    CB_TRY(h_scratch.ensure(L.off), "pinned scratch");
-    CB_TRY(d_scratch.ensure(L.off), "device scratch");
-    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    CB_TRY(hbuf.ensure(L.off), "pinned scratch");
+    CB_TRY(dbuf.ensure(L.off), "device scratch");
+    uint8_t *h = static_cast<uint8_t *>(hbuf.ptr);
     CopyDesc *desc = reinterpret_cast<CopyDesc *>(h + o_desc);
     uint32_t *us = reinterpret_cast<uint32_t *>(h + o_us);
     uint32_t *pus = reinterpret_cast<uint32_t *>(h + o_pus);
@@ -670,14 +672,14 @@ int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t
     }
     us[ncp] = total;
     pus[npk] = ptotal;
-    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    uint8_t *d = static_cast<uint8_t *>(dbuf.ptr);
     CB_TRY(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D scatter");
     if (ncp) {
       CB_TRY(timed(1, bytes, st,
                    [&] {
                      return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_desc),
                                               reinterpret_cast<const uint32_t *>(d + o_us), ncp, total,
-                                              copy_engine, d_err, num_sms, st);
+                                              engine, d_err, num_sms, st, lsu_ctas_per_sm);
                    }),
              "scatter");
     }
@@ -697,6 +699,33 @@ int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t
     launches++;
     table_used += np;
   }
+  return CB_OK;
+}
+
+int Store::put_device(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                      const uint8_t *keys_in, int n, uint8_t *keys_out, uint8_t *status_out,
+                      cudaStream_t st, const HashProgress *pg, cudaEvent_t copies_done) {
+  Trace tr("cb.put");
+  std::vector<HKey> keys(n);
+  if (keys_in) {
+    if (copies_done) CB_TRY(cudaStreamWaitEvent(st, copies_done, 0), "wait copies");
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(keys_in + 16 * i);
+  } else {
+    int rc = hash_device(ptrs, sizes, n, st, pg, copies_done);
+    if (rc) return rc;
+    const uint8_t *dig = static_cast<const uint8_t *>(h_out.ptr);
+    for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32 * i);
+  }
+  int rc = reserve_index((uint64_t)n, st);
+  if (rc) return rc;
+  PutPlan &plan = put_plan;
+  policy.plan_put(keys.data(), sizes, is_prefix, n, cfg.dedup_enabled != 0, plan);
+  plan_open = true;
+  rc = run_moves(plan.moves, plan.dropped, st);
+  if (rc) return rc;
+
+  rc = enqueue_places(plan, ptrs, st, h_scratch, d_scratch, copy_engine, 8);
+  if (rc) return rc;
   rc = check_device_error(st);  // also the final sync of the batch
   policy.commit();
   if (rc) return rc;
@@ -1104,6 +1133,10 @@ int Store::selftest(int which, cudaStream_t st) {
     fake_move_failures = 1;
     return CB_OK;
   }
+  if (which == CB_SELFTEST_GET_ERROR) {
+    inject_get_error = true;
+    return CB_OK;
+  }
   if (which != CB_SELFTEST_HASH_WAIT) return fail(CB_ERR_ARG, "unknown self-test %d", which);
   constexpr uint64_t kBytes = 1 << 20;
   CB_TRY(cudaStreamSynchronize(copy_stream), "copy stream");
@@ -1265,6 +1298,11 @@ int Store::clear(cudaStream_t st) {
   if (policy.pinned_blocks())  // a view would point at memory the store hands out again
     return fail(CB_ERR_STATE, "%llu block(s) have outstanding zero-copy views",
                 (unsigned long long)policy.pinned_blocks());
+  // Pipelined work first: batches submitted before the clear are placed
+  // (and then cleared) like synchronous puts would have been; after a
+  // failure the rest of them are dropped.
+  if (settle() != CB_OK) drop_pipeline();
+  plan_open = false;
   CB_TRY(cudaStreamSynchronize(st), "sync");
   if (dht) {  // collective, like DistributedStore::clear (barrier before and after)
     int rc = dht_barrier();
@@ -1346,22 +1384,32 @@ cudaStream_t pick_stream(Store *s, void *stream) {
 }
 
 // kData calls read or change stored blocks: they are refused once a call
-// failed after planning (Store::lost) until clear(). kAny calls (hashing,
-// statistics, clear, releases, barriers) run in that state too.
-enum Access { kData, kAny };
+// failed after planning (Store::lost) until clear(), and they first settle
+// the stream-ordered work (pipelined puts are placed, stream-ordered gets
+// waited for; an error of that work is the call's result). kAsync calls
+// (the stream-ordered put and get) are refused in that state too but do not
+// settle. kAny calls (statistics, barriers, syncs) run in that state and
+// settle; kFree calls (hashing, KV compression, view releases, clear, which
+// settles by itself) neither.
+enum Access { kData, kAsync, kAny, kFree };
 
 template <class F>
 int guarded(cb_store *h, F f, Access access = kData) {
   if (!h || !h->s) return CB_ERR_ARG;
   Store *s = h->s;
   std::lock_guard<std::mutex> g(s->mu);
-  if (access == kData && !s->lost.empty())
+  if ((access == kData || access == kAsync) && !s->lost.empty())
     return s->fail(CB_ERR_STATE, "store state lost after a failed call (%s); clear() resets it", s->lost.c_str());
   s->plan_open = false;
   int rc;
   try {
     cudaError_t e = cudaSetDevice(s->device);
-    rc = e != cudaSuccess ? s->cuda_fail(e, "cudaSetDevice") : f(s);
+    if (e != cudaSuccess) {
+      rc = s->cuda_fail(e, "cudaSetDevice");
+    } else {
+      rc = (access == kData || access == kAny) ? s->settle() : CB_OK;
+      if (rc == CB_OK) rc = f(s);
+    }
   } catch (const std::bad_alloc &) {
     rc = s->fail(CB_ERR_NOSPACE, "host allocation failed");
   } catch (const std::exception &ex) {
@@ -1434,6 +1482,64 @@ int cb_selftest(cb_store *h, int32_t which) {
   return guarded(h, [&](Store *s) -> int { return s->selftest(which, s->own_stream); }, kAny);
 }
 
+int cb_put_batch_async(cb_store *h, const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
+                       const uint8_t *keys_in, int32_t n, int32_t mem_kind, uint8_t *keys_out, uint8_t *status_out,
+                       uint64_t *ticket_out, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!ptrs || !sizes)) || !ticket_out) return s->fail(CB_ERR_ARG, "bad arguments");
+    if (mem_kind != CB_MEM_DEVICE && mem_kind != CB_MEM_HOST) return s->fail(CB_ERR_ARG, "unknown mem_kind %d", mem_kind);
+    for (int i = 0; i < n; ++i)
+      if (sizes[i] > cb::kSizeMask) return s->fail(CB_ERR_ARG, "block %d too large", i);
+    cudaStream_t st = pick_stream(s, stream);
+    if (mem_kind == CB_MEM_HOST) {
+      // host blocks are staged and placed at once, after every earlier batch
+      int rc = s->settle();
+      if (rc) return rc;
+      *ticket_out = s->next_ticket++;
+      s->placed_ticket = *ticket_out;
+      if (s->world > 1)
+        return s->dht_put(ptrs, sizes, is_prefix, keys_in, n, mem_kind, keys_out, status_out, st);
+      return n ? s->put_host(ptrs, sizes, is_prefix, keys_in, n, keys_out, status_out, st) : CB_OK;
+    }
+    std::vector<uint64_t> p(n);
+    for (int i = 0; i < n; ++i) p[i] = (uint64_t)ptrs[i];
+    return s->put_async(p.data(), sizes, is_prefix, keys_in, n, keys_out, status_out, ticket_out, st);
+  }, kAsync);
+}
+
+int cb_put_wait(cb_store *h, uint64_t ticket, uint64_t *placed_out) {
+  return guarded(h, [&](Store *s) -> int {
+    const int rc = s->put_wait(ticket ? ticket : UINT64_MAX);
+    if (placed_out) *placed_out = s->placed_ticket;
+    return rc;
+  }, kAsync);
+}
+
+int cb_put_placed(cb_store *h, uint64_t *placed_out) {
+  if (!h || !h->s || !placed_out) return CB_ERR_ARG;
+  std::lock_guard<std::mutex> g(h->s->mu);
+  *placed_out = h->s->placed_ticket;
+  return CB_OK;
+}
+
+int cb_get_batch_async(cb_store *h, const uint8_t *keys, int32_t n, void *const *outs, const uint64_t *out_caps,
+                       uint64_t *sizes_out, uint8_t *found_out, void *stream) {
+  return guarded(h, [&](Store *s) -> int {
+    if (n < 0 || (n > 0 && (!keys || !outs || !out_caps || !sizes_out || !found_out)))
+      return s->fail(CB_ERR_ARG, "bad arguments");
+    cudaStream_t st = pick_stream(s, stream);
+    if (s->world > 1) {  // DHT gets are collective and synchronous
+      int rc = s->settle();
+      if (rc) return rc;
+      return s->dht_get(keys, n, outs, out_caps, CB_MEM_DEVICE, sizes_out, found_out, st);
+    }
+    if (n == 0) return CB_OK;
+    std::vector<uint64_t> o(n);
+    for (int i = 0; i < n; ++i) o[i] = (uint64_t)outs[i];
+    return s->get_async(keys, n, o.data(), out_caps, sizes_out, found_out, st);
+  }, kAsync);
+}
+
 int cb_get_views(cb_store *h, const uint8_t *keys, int32_t n, uint64_t *addrs_out, uint64_t *sizes_out,
                  uint8_t *found_out, void *stream) {
   return guarded(h, [&](Store *s) -> int {
@@ -1448,7 +1554,7 @@ int cb_release_views(cb_store *h, const uint8_t *keys, int32_t n) {
   return guarded(h, [&](Store *s) -> int {
     if (n < 0 || (n > 0 && !keys)) return s->fail(CB_ERR_ARG, "bad arguments");
     return s->release_views(keys, n);
-  }, kAny);
+  }, kFree);
 }
 
 int cb_kv_compress_batch(cb_store *h, const void *const *srcs, const uint64_t *sizes, void *const *dsts,
@@ -1462,7 +1568,7 @@ int cb_kv_compress_batch(cb_store *h, const void *const *srcs, const uint64_t *s
       dst[i] = (uint64_t)dsts[i];
     }
     return s->kv_compress(src.data(), sizes, dst.data(), n, pick_stream(s, stream));
-  }, kAny);
+  }, kFree);
 }
 
 int cb_kv_decompress_batch(cb_store *h, const void *const *srcs, const uint64_t *comp_sizes,
@@ -1477,7 +1583,7 @@ int cb_kv_decompress_batch(cb_store *h, const void *const *srcs, const uint64_t 
       dst[i] = (uint64_t)dsts[i];
     }
     return s->kv_decompress(src.data(), comp_sizes, orig_sizes, dst.data(), n, ok_out, pick_stream(s, stream));
-  }, kAny);
+  }, kFree);
 }
 
 int cb_hash_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, int32_t n,
@@ -1521,7 +1627,7 @@ int cb_hash_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, i
       i = j;
     }
     return CB_OK;
-  }, kAny);
+  }, kFree);
 }
 
 int cb_put_batch(cb_store *h, const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
@@ -1593,7 +1699,7 @@ int cb_evict(cb_store *h, uint64_t bytes, uint64_t *evicted_bytes) {
 int cb_get_stats(cb_store *h, cb_stats *out) {
   return guarded(h, [&](Store *s) -> int {
     if (!out) return s->fail(CB_ERR_ARG, "bad arguments");
-    s->resolve_prof();  // records of batches that ended without a store-side sync
+    s->resolve_prof(true);  // records of batches that ended without a store-side sync
     s->fill_stats(out);
     if (s->world > 1) return s->dht_cluster_usage(out);
     return CB_OK;
@@ -1601,7 +1707,7 @@ int cb_get_stats(cb_store *h, cb_stats *out) {
 }
 
 int cb_clear(cb_store *h) {
-  return guarded(h, [&](Store *s) -> int { return s->clear(s->own_stream); }, kAny);
+  return guarded(h, [&](Store *s) -> int { return s->clear(s->own_stream); }, kFree);
 }
 
 int cb_sync(cb_store *h) {

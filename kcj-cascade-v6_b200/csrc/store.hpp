@@ -3,6 +3,7 @@
 
 #include <cuda_runtime.h>
 
+#include <deque>
 #include <functional>
 #include <mutex>
 #include <string>
@@ -106,11 +107,12 @@ struct Store {
     uint64_t bytes;
     cudaEvent_t a, b;
   };
-  std::vector<cudaEvent_t> prof_events;
-  size_t prof_events_used = 0;
+  std::vector<cudaEvent_t> prof_events;  // every event created (destroyed with the store)
   std::vector<ProfRec> prof_pending;
   cudaError_t prof_event(cudaEvent_t &e);
-  void resolve_prof();  // after every stream with pending records is idle
+  std::vector<cudaEvent_t> prof_free;  // created, not in use
+  // Reads the timing of finished launches; with `wait`, waits for all.
+  void resolve_prof(bool wait = false);
 
   // Runs `launch` (one or two kernels on stream st) and, when profiling,
   // brackets it with events. `bytes` = payload bytes it processes.
@@ -185,6 +187,82 @@ struct Store {
   void fill_stats(cb_stats *o) const;
   uint64_t staging_capacity() const;
 
+  // pipeline.cu — stream-ordered (pipelined) puts and gets.
+  //
+  // Pipelined put: a batch's SHA-256 is launched at submission on one of
+  // kHashSlots side streams (several queued small batches share one launch),
+  // so many batches hash concurrently; batches are then placed (dedup plan,
+  // tier moves, scatter, index insert) strictly in submission order, which
+  // keeps the sequential dedup rule of put_batch exactly.
+  struct HashSlot {
+    PinnedBuf h;  // [HashJob x n][digests n x 32]
+    DevBuf d;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;  // digests are in h
+    int n = 0;                   // blocks of the launch
+    int cap = 0;                 // blocks the slot's buffers hold
+    int users = 0;               // batches of the launch not placed yet
+    bool launched = false;
+  };
+  struct AsyncPut {
+    uint64_t ticket = 0;
+    std::vector<uint64_t> ptrs, sizes;
+    std::vector<uint8_t> prefix, keys_in;  // empty: none given
+    uint8_t *keys_out = nullptr, *status_out = nullptr;
+    int slot = -1, off = 0;  // its digests: slot's launch, from block `off`
+  };
+  // Ring of scratch buffers for stream-ordered kernels whose descriptors must
+  // outlive the call (pipelined scatters, stream-ordered gathers).
+  struct ScratchSlot {
+    PinnedBuf h;
+    DevBuf d;
+    cudaEvent_t done = nullptr;
+    bool pending = false;  // done is recorded and not yet waited for by the host
+  };
+  static constexpr int kHashSlots = 16;
+  static constexpr int kScratchSlots = 16;
+  HashSlot hslots[kHashSlots];
+  int hslot_next = 0;
+  std::deque<AsyncPut> aput;         // submitted, not placed (submission order)
+  int open_slot = -1;                // slot collecting batches not launched yet
+  uint64_t next_ticket = 1, placed_ticket = 0;
+  uint64_t inflight_blocks = 0;      // blocks submitted and not placed
+  cudaStream_t put_stream = nullptr; // placements of pipelined puts
+  ScratchSlot sslots[kScratchSlots];
+  int sslot_next = 0;
+  bool pipeline_ready = false;
+  int pipeline_init();
+  void pipeline_release();
+  int put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix, const uint8_t *keys_in,
+                int n, uint8_t *keys_out, uint8_t *status_out, uint64_t *ticket, cudaStream_t st);
+  int put_wait(uint64_t ticket);
+  int place_until(uint64_t ticket);
+  int launch_open_slot();
+  int place_oldest();
+  int place_batch(const std::vector<HKey> &keys, AsyncPut &b);
+  // Scatter + INT8 packing + index insert of a plan's placements on st, with
+  // descriptors in (h, d). Returns without waiting.
+  int enqueue_places(const PutPlan &plan, const uint64_t *ptrs, cudaStream_t st, PinnedBuf &h, DevBuf &d,
+                     int engine, int lsu_ctas_per_sm);
+  ScratchSlot *take_scratch(size_t bytes, int &rc);
+  // Every pool extent a stream-ordered gather may still read is released
+  // only after it: work that may write the pool waits for them first.
+  int fence_reads(cudaStream_t st);
+  // Settles everything stream-ordered: places every pipelined put, waits for
+  // every stream-ordered gather, and reports a device error any of them
+  // raised (CB_ERR_DEVICE / CB_ERR_TIMEOUT) before the caller goes on.
+  int settle();
+  int finish_placements();
+  void drop_pipeline();
+  unsigned *d_err_get = nullptr;  // device errors of stream-ordered gathers
+  // Reads and clears a device error word (st is synchronised first).
+  int read_error_word(unsigned *word, cudaStream_t st);
+  int get_async(const uint8_t *keys, int n, const uint64_t *outs, const uint64_t *caps, uint64_t *sizes_out,
+                uint8_t *found_out, cudaStream_t st);
+  bool inject_get_error = false;  // CB_SELFTEST_GET_ERROR: host-side injection
+  bool placed_unsettled = false;  // a pipelined batch was placed since the last settle()
+  cudaEvent_t ev_submit = nullptr;
+
   // dht.cu
   int dht_attach(int rank, int world, const uint8_t *uid);
   void dht_detach();
@@ -211,6 +289,12 @@ struct Store {
 };
 
 inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+// dht.cu: the DHT's host-side routing and owner planning (also exported for
+// host-only use through cb_dht_route / cb_dht_plan_put).
+void dht_route(const HKey *keys, int n, int W, int *owner, int *order, uint32_t *scount);
+void dht_owner_plan(Policy &policy, const HKey *keys, const uint64_t *sizes, const uint8_t *prefix, uint32_t n,
+                    bool dedup, PutPlan &plan, uint32_t *status, uint64_t *loc);
 
 // The address range one copy starting at p may cover: the CUDA allocation
 // that contains p (device, pinned or managed), or everything when p is memory

@@ -163,3 +163,29 @@ int main(void) {
                     f"-L{libdir}", "-l:" + os.path.basename(L.LIB_PATH), f"-Wl,-rpath,{libdir}"], check=True)
     r = subprocess.run([str(exe)], capture_output=True, text=True)
     assert r.returncode == 0 and r.stdout.strip() == "ok", (r.returncode, r.stdout, r.stderr)
+
+
+def test_dht_route_and_owner_plan_without_a_gpu(lib):
+    # the DHT's host-side routing and owner planning run without a GPU
+    import numpy as np
+    import cascade_cpp
+    rng = np.random.default_rng(2)
+    keys = rng.integers(0, 256, (50, 16), dtype=np.uint8)
+    keys[10] = keys[3]  # a repeat inside the batch
+    owner, order, counts = cascade_cpp.dht_route(keys, 3)
+    want_owner = [int.from_bytes(k[:8].tobytes(), "big") % 3 for k in keys]
+    assert owner.tolist() == want_owner
+    assert counts.tolist() == [want_owner.count(r) for r in range(3)]
+    assert order.tolist() == sorted(range(50), key=lambda i: (want_owner[i], i))
+    p = cascade_cpp.DhtPlanner(1 << 20)
+    status, loc = p.plan_put(keys, np.full(50, 4096, np.uint64), np.zeros(50, np.uint8))
+    assert status.tolist() == [1 if i == 10 else 0 for i in range(50)]
+    stored = loc[status == 0]
+    assert len(set(stored.tolist())) == 49 and all(x % 256 == 0 for x in stored.tolist())
+    # a second step: everything already held is a dedup hit; no room is a failure
+    status2, _ = p.plan_put(keys[:5], np.full(5, 4096, np.uint64))
+    assert status2.tolist() == [1] * 5
+    big = rng.integers(0, 256, (1, 16), dtype=np.uint8)
+    status3, _ = p.plan_put(big, np.array([2 << 20], np.uint64))
+    assert status3.tolist() == [2]
+    p.close()

@@ -1,7 +1,10 @@
-"""N>1 host-side logic on CPU: 2 and 4 gloo ranks run the DHT routing protocol
-(owner = cb_owner_rank, per-owner buckets in batch order, counts all-gather,
-all-to-all of requests, owner-side sequential dedup in (source rank, index)
-order) and must reach exactly the sequential DhtOracle's decisions."""
+"""N>1 host-side logic on CPU: 2 and 4 gloo ranks run the DHT put protocol
+with the library's own host functions - writer-side routing
+(cb_dht_route: owner per key, per-owner buckets in batch order, counts) and
+owner-side planning (cb_dht_plan_put: sequential dedup in (source rank,
+index) order), the functions cb_put_batch runs on a DHT member - with gloo
+collectives in place of NCCL, and must reach exactly the sequential
+DhtOracle's decisions."""
 import os
 import socket
 
@@ -58,35 +61,41 @@ def _worker(rank, world, port, out):
 
     pool, items = _batches(world)
     mine = [(O.block_id(pool[s]), pool[s], pf) for s, pf in items[rank]]
-    # routing: owner per block (the C ABI's rule) in batch order
-    owners = [cascade_cpp.owner_rank(b, world) for b, _, _ in mine]
-    assert owners == [oracle_owner(b, world) for b, _, _ in mine]
-    buckets = [[i for i, o in enumerate(owners) if o == r] for r in range(world)]
-    counts = torch.tensor([len(b) for b in buckets], dtype=torch.int64)
+    keys = np.frombuffer(b"".join(bytes.fromhex(b) for b, _, _ in mine), np.uint8).reshape(-1, 16)
+    # writer side: the library's routing
+    owners, order, counts = cascade_cpp.dht_route(keys, world)
+    assert owners.tolist() == [oracle_owner(b, world) for b, _, _ in mine]
     allc = [torch.zeros(world, dtype=torch.int64) for _ in range(world)]
-    dist.all_gather(allc, counts)
+    dist.all_gather(allc, torch.from_numpy(counts.astype(np.int64)))
     rcount = [int(allc[r][rank]) for r in range(world)]
-    # requests: (index, id bytes, size) records, all-to-all
-    send = [torch.tensor([[i] + list(bytes.fromhex(mine[i][0])) for i in b], dtype=torch.int64).reshape(-1, 17)
-            for b in buckets]
-    recv = [torch.zeros((rcount[r], 17), dtype=torch.int64) for r in range(world)]
+    # requests (key bytes, size, prefix) in send order, all-to-all
+    rows = [list(keys[i]) + [len(mine[i][1]), int(mine[i][2])] for i in order.tolist()]
+    send, o = [], 0
+    for r in range(world):
+        send.append(torch.tensor(rows[o:o + int(counts[r])], dtype=torch.int64).reshape(-1, 18))
+        o += int(counts[r])
+    recv = [torch.zeros((rcount[r], 18), dtype=torch.int64) for r in range(world)]
     _alltoallv(recv, send, rank, world)
-    # owner: sequential dedup in (source rank, index) order
-    shard = O.SequentialStore()
-    replies = []
+    # owner side: the library's planning over (source rank, index) order
+    req = torch.cat(recv).numpy()
+    planner = cascade_cpp.DhtPlanner(1 << 30)
+    status, loc = planner.plan_put(req[:, :16].astype(np.uint8), req[:, 16].astype(np.uint64),
+                                   req[:, 17].astype(np.uint8))
+    # every stored block got a distinct pool extent
+    stored = [int(x) for x, st in zip(loc, status) if st == 0]
+    assert len(set(stored)) == len(stored)
+    replies, o = [], 0
     for r in range(world):
-        rep = []
-        for row in recv[r].tolist():
-            bid = bytes(row[1:]).hex()
-            rep.append([row[0], shard.put(bid, b"x")[1]])
-        replies.append(torch.tensor(rep, dtype=torch.int64).reshape(-1, 2))
-    back = [torch.zeros((len(buckets[r]), 2), dtype=torch.int64) for r in range(world)]
+        replies.append(torch.from_numpy(status[o:o + rcount[r]].astype(np.int64)).reshape(-1, 1))
+        o += rcount[r]
+    back = [torch.zeros((int(counts[r]), 1), dtype=torch.int64) for r in range(world)]
     _alltoallv(back, replies, rank, world)
-    status = [None] * len(mine)
-    for r in range(world):
-        for idx, st in back[r].tolist():
-            status[idx] = st
-    out[rank] = status
+    flat = torch.cat(back).reshape(-1).tolist()
+    status_mine = [None] * len(mine)
+    for j, i in enumerate(order.tolist()):
+        status_mine[i] = flat[j]
+    out[rank] = status_mine
+    planner.close()
     dist.destroy_process_group()
 
 
