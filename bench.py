@@ -182,18 +182,43 @@ def make_store(args, device_index, capacity, dht=False):
     return cascade_cpp.DistributedStore(cfg)
 
 
+def plan_gets(keys_all, rng_seed):
+    """The get side of a step: every distinct stored key once, in a uniformly
+    shuffled order. Prepared from the IDs the puts returned, outside the
+    timed region (the IDs are the same every step)."""
+    uk = np.unique(keys_all.view(np.dtype((np.void, 16))).reshape(-1))
+    order = np.random.default_rng(rng_seed).permutation(len(uk))
+    return np.ascontiguousarray(uk[order].view(np.uint8).reshape(-1, 16))
+
+
+def n_get_calls(keys, batch):
+    """Get calls of a step; in a DHT the largest over ranks (every get is
+    collective, so ranks with fewer keys join the last calls with empty
+    batches)."""
+    import torch
+    n_get = (len(keys) + batch - 1) // batch
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        t = torch.tensor([n_get], dtype=torch.int64, device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        n_get = int(t.item())
+    return n_get
+
+
 def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_memory=True, pipelined=True,
-             keys_all=None):
+             keys_all=None, gets=None):
     """One step: put everything in batches, then get every stored key in a
     shuffled order into out_buf (one batch at a time). Device blocks go
     through the pipelined put (each batch's SHA-256 launched at submission,
     batches placed in order; one wait at the end) and the stream-ordered get;
-    host blocks through the synchronous calls. Returns (put_s, get_s,
-    put_bytes, get_bytes) measured with CUDA events on the current stream
-    (the put phase ends with a host wait for every placement)."""
+    host blocks through the synchronous calls. `gets` = (keys in get order,
+    number of get calls) prepared beforehand (plan_gets); without it they
+    are prepared from this pass's IDs between the two phases, outside both
+    phase timings. Returns (put_s, get_s, put_bytes, get_bytes) measured
+    with CUDA events on the current stream (the put phase ends with a host
+    wait for every placement)."""
     import torch
     n = len(ptrs)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     if keys_all is None:
         keys_all = np.empty((n, 16), np.uint8)
     ev[0].record()
@@ -210,20 +235,15 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
     if device_memory and pipelined:
         store.wait_puts()
     ev[1].record()
-    uk = np.unique(keys_all.view(np.dtype((np.void, 16))).reshape(-1))
-    order = np.random.default_rng(rng_seed).permutation(len(uk))
-    keys = uk[order].view(np.uint8).reshape(-1, 16)
+    if gets is None:
+        keys = plan_gets(keys_all, rng_seed)
+        gets = (keys, n_get_calls(keys, batch))
+    keys, n_get = gets
     base = out_buf.data_ptr() if hasattr(out_buf, "data_ptr") else out_buf.ctypes.data
     outs_b = np.uint64(base) + np.arange(batch, dtype=np.uint64) * np.uint64(size)
-    got = 0
-    # In a DHT every get is collective: ranks whose streams hold fewer unique
-    # blocks join the remaining calls with empty batches.
-    n_get = (len(keys) + batch - 1) // batch
-    if torch.distributed.is_available() and torch.distributed.is_initialized():
-        t = torch.tensor([n_get], dtype=torch.int64, device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        n_get = int(t.item())
     caps = np.full(batch, size, np.uint64)
+    got = 0
+    ev[2].record()
     for j in range(n_get):
         i = j * batch
         if _TRACE["on"] and j % 16 == 0:
@@ -236,10 +256,10 @@ def run_pass(store, ptrs, sizes, prefix, batch, out_buf, size, rng_seed, device_
             s, f = store.get_ptrs(kk, outs_b[:m], caps[:m], device_memory)
         ok = (f & 0x0F) != 0
         got += int(s[ok].sum())
-    ev[2].record()
-    ev[2].synchronize()
+    ev[3].record()
+    ev[3].synchronize()
     put_s = ev[0].elapsed_time(ev[1]) / 1e3
-    get_s = ev[1].elapsed_time(ev[2]) / 1e3
+    get_s = ev[2].elapsed_time(ev[3]) / 1e3
     return put_s, get_s, int(sizes.sum()), got
 
 
@@ -406,10 +426,19 @@ def main():
         if world > 1:
             torch.distributed.barrier()
 
-    for w in range(args.warmup):
+    keys_ref = np.empty((len(ptrs), 16), np.uint8)
+    for w in range(max(args.warmup, 1)):  # (at least one: the IDs the timed steps get come from it)
         trace(args, f"warm-up pass {w}")
         store.clear()
-        run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, w)
+        run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, w, keys_all=keys_ref)
+    # the get side of every timed step: all distinct IDs in a fresh shuffled
+    # order per step (the IDs themselves are the same every step; each
+    # step's are checked against them after the timed region)
+    step_gets = []
+    for s in range(args.steps):
+        keys = plan_gets(keys_ref, 100 + s)
+        step_gets.append((keys, n_get_calls(keys, args.batch)))
+    step_keys = [np.empty_like(keys_ref) for _ in range(args.steps)]
     trace(args, "timed passes")
     st0 = store._n.stats()
     sync_all()
@@ -421,13 +450,16 @@ def main():
         t_ev0.record()
         for s in range(args.steps):
             store.clear()
-            ps, gs, pb, gb = run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, 100 + s)
+            ps, gs, pb, gb = run_pass(store, ptrs, sizes, prefix, args.batch, out_buf, size, 100 + s,
+                                      keys_all=step_keys[s], gets=step_gets[s])
             put_t += ps
             get_t += gs
             put_b += pb
             get_b += gb
         t_ev1.record()
         sync_all()
+    if not all(np.array_equal(k, keys_ref) for k in step_keys):
+        raise SystemExit("block IDs of a timed step differ from the warm-up's")
     elapsed = t_ev0.elapsed_time(t_ev1) / 1e3
     st1 = store._n.stats()
     remote_b = st1.peer_bytes_read - st0.peer_bytes_read  # crossed NVLink
@@ -926,13 +958,18 @@ def e2e_run(args, rank, world, device, store):
     prefix = is_prefix.astype(np.uint8)
     out = torch.empty(args.batch * size, dtype=torch.uint8, pin_memory=True)
     store.clear()
-    run_pass(store, ptrs, sizes, prefix, args.batch, out, size, 1, device_memory=False)
+    keys_ref = np.empty((n, 16), np.uint8)
+    run_pass(store, ptrs, sizes, prefix, args.batch, out, size, 1, device_memory=False, keys_all=keys_ref)
+    keys_step = np.empty_like(keys_ref)
     times, pb, gb = [], 0, 0
     for s in range(max(args.steps, 2)):
         store.clear()
+        gk = plan_gets(keys_ref, 2 + s)
+        gets = (gk, n_get_calls(gk, args.batch))
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        ps, gs, pb, gb = run_pass(store, ptrs, sizes, prefix, args.batch, out, size, 2 + s, device_memory=False)
+        ps, gs, pb, gb = run_pass(store, ptrs, sizes, prefix, args.batch, out, size, 2 + s, device_memory=False,
+                                  keys_all=keys_step, gets=gets)
         torch.cuda.synchronize()
         times.append(time.perf_counter() - t0)
     el = reduce_max(float(np.median(times)), world)

@@ -406,11 +406,16 @@ int Store::get_async(const uint8_t *keys, int n, const uint64_t *outs, const uin
     rc = place_until(UINT64_MAX);
     if (rc) return rc;
   }
+  // One lookup per key, which also marks the hit most recently used
+  // (CascadeStore::get touches on hit, src/cascade_core.cpp:1281). A batch
+  // that reads the DRAM tier (and may promote) takes the synchronous path
+  // instead, which touches every key in batch order itself; the keys this
+  // loop touched before the first DRAM hit are then touched again in the
+  // same order, which leaves the LRU order of a single pass.
   std::vector<const BlockMeta *> meta(n);
   for (int i = 0; i < n; ++i) {
-    meta[i] = policy.find(to_hkey(keys + 16ull * i));
+    meta[i] = policy.find_touch(to_hkey(keys + 16ull * i));
     if (meta[i] && meta[i]->tier != kTierHbm && meta[i]->size <= caps[i]) {
-      // a DRAM-tier block (and its promotion) takes the synchronous path
       rc = settle();
       if (rc) return rc;
       return get_device(keys, n, outs, caps, sizes_out, found_out, st);
@@ -460,9 +465,6 @@ int Store::get_async(const uint8_t *keys, int n, const uint64_t *outs, const uin
     total += 1;
   }
   us[nd] = total;
-  // LRU order: CascadeStore::get touches on hit (src/cascade_core.cpp:1281)
-  for (int i = 0; i < n; ++i)
-    if (meta[i]) policy.touch(to_hkey(keys + 16ull * i));
   if (total) {
     uint8_t *d = static_cast<uint8_t *>(sl->d.ptr);
     CB_TRY_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st), "H2D gather");

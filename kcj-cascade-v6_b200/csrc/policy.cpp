@@ -78,13 +78,16 @@ const BlockMeta *Policy::find(const HKey &k) const {
   return it == map_.end() ? nullptr : &it->second;
 }
 
-void Policy::touch(const HKey &k) {
+void Policy::touch(const HKey &k) { find_touch(k); }
+
+const BlockMeta *Policy::find_touch(const HKey &k) {
   auto it = map_.find(k);
-  if (it == map_.end()) return;
+  if (it == map_.end()) return nullptr;
   BlockMeta &m = it->second;
   auto &lst = lru_[m.tier][m.prefix];
   lst.splice(lst.begin(), lst, m.lru);
   m.stamp = ++clock_;
+  return &m;
 }
 
 bool Policy::pin(const HKey &k) {

@@ -174,6 +174,8 @@ class Policy {
 
   const BlockMeta *find(const HKey &k) const;
   void touch(const HKey &k);  // mark most recently used
+  // find + touch with one lookup (a get's hit)
+  const BlockMeta *find_touch(const HKey &k);
   // Keep a block out of every victim choice until commit() (a get is still
   // reading it while this plan's moves run).
   void protect(const HKey &k);

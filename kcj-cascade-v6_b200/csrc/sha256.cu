@@ -318,6 +318,11 @@ __global__ void __launch_bounds__(64) sha256_pc_kernel(const HashJob *__restrict
 }
 
 }  // namespace
+}  // namespace cb
+
+#include "sha256_fused.cuh"
+
+namespace cb {
 
 cudaError_t prepare_sha256_kernel() {
   cudaFuncAttributes a;
