@@ -460,6 +460,7 @@ def main():
         sync_all()
     if not all(np.array_equal(k, keys_ref) for k in step_keys):
         raise SystemExit("block IDs of a timed step differ from the warm-up's")
+    dedup_step = reduce_sum((store._n.stats().dedup_hits - st0.dedup_hits) / max(args.steps, 1), world)
     elapsed = t_ev0.elapsed_time(t_ev1) / 1e3
     st1 = store._n.stats()
     remote_b = st1.peer_bytes_read - st0.peer_bytes_read  # crossed NVLink
@@ -534,6 +535,8 @@ def main():
                                    "remote_fraction": round(remote_b / max(1, get_b), 4)}
         line["config"]["parallelism"] = f"hash-sharded DHT over {world} GPUs (owner = ID mod {world})"
     line["clocks"] = clk.summary()
+    trace(args, "verification")
+    line["verified"] = verify_run(store, ptrs, sizes, keys_ref, dedup_step, out_buf, size, local, world)
 
     if not args.no_sweep:
         trace(args, "batch sweep")
@@ -560,6 +563,56 @@ def main():
     store.close()
     if world > 1:
         torch.distributed.destroy_process_group()
+    if not line["verified"]["ok"]:
+        sys.exit(3)
+
+
+def verify_run(store, ptrs, sizes, keys_ref, dedup_step, out_buf, size, local, world, sample=256):
+    """Checks of the run's results, on every rank (collective in a DHT):
+    * IDs: a seeded sample of put positions re-hashed from their source
+      blocks by the store-less hashing call equals the IDs the puts returned;
+    * dedup: dedup hits per step, summed over ranks, equal the blocks put
+      minus the distinct IDs over all ranks (every distinct block is stored
+      exactly once cluster-wide, every other put is a hit);
+    * read-back: a seeded sample of this rank's distinct IDs fetched again
+      through the store re-hashes on the GPU to the requested IDs.
+    Returns {"ok": bool, ...}; the caller exits non-zero when ok is false."""
+    import torch
+    import cascade_cpp
+    from cascade_cpp import _lib as L
+    rank = int(os.environ.get("RANK", "0"))
+    rng = np.random.default_rng(4242 + rank)
+    hasher = cascade_cpp._hasher(local)
+    sel = np.sort(rng.choice(len(ptrs), min(sample, len(ptrs)), replace=False))
+    dig = hasher.hash(np.ascontiguousarray(ptrs[sel]), np.ascontiguousarray(sizes[sel]), L.CB_MEM_DEVICE)
+    ids_ok = bool(np.array_equal(dig[:, :16], keys_ref[sel]))
+    all_keys = keys_ref
+    if world > 1:
+        kt = torch.from_numpy(keys_ref).cuda()
+        parts = [torch.empty_like(kt) for _ in range(world)]
+        torch.distributed.all_gather(parts, kt)
+        all_keys = torch.cat(parts).cpu().numpy()
+    distinct = len(np.unique(all_keys.view(np.dtype((np.void, 16))).reshape(-1)))
+    dedup_want = len(all_keys) - distinct
+    dedup_ok = abs(dedup_step - dedup_want) < 0.5
+    uk = plan_gets(keys_ref, 777 + rank)[:min(sample, len(keys_ref), out_buf.numel() // size)]
+    m = len(uk)
+    outs = (np.uint64(out_buf.data_ptr()) + np.arange(m, dtype=np.uint64) * np.uint64(size)).astype(np.uint64)
+    s, f = store.get_ptrs(uk, outs, np.full(m, size, np.uint64), True)
+    found_ok = bool(((f & 0x0F) != 0).all() and (s == size).all())
+    torch.cuda.synchronize()
+    back = hasher.hash(outs, np.full(m, size, np.uint64), L.CB_MEM_DEVICE)
+    read_ok = found_ok and bool(np.array_equal(back[:, :16], uk))
+    oks = [ids_ok, dedup_ok, read_ok]
+    if world > 1:
+        t = torch.tensor([0 if x else 1 for x in oks], dtype=torch.int64, device="cuda")
+        torch.distributed.all_reduce(t)
+        oks = [int(v) == 0 for v in t.tolist()]
+    return {"ok": all(oks), "ids": oks[0], "dedup": oks[1], "read_back": oks[2], "sample": int(len(sel)),
+            "dedup_hits_per_step": round(dedup_step, 1), "expected_dedup_hits": int(dedup_want),
+            "how": "IDs of a seeded sample re-hashed from the source blocks (store-less hashing call); dedup hits "
+                   "per step summed over ranks = blocks put - distinct IDs over all ranks; a seeded sample of "
+                   "distinct IDs fetched again and re-hashed on the GPU (all ranks must pass)"}
 
 
 def zipf_main(args, rank, world, local, device):

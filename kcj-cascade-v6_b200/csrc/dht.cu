@@ -27,6 +27,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <climits>
 #include <chrono>
 #include <thread>
 #include <unordered_set>
@@ -48,10 +49,21 @@ struct PutRep {
   uint32_t pad;
 };
 struct Export {
-  cudaIpcMemHandle_t pool, table;
-  uint64_t pool_bytes, table_slots;
+  cudaIpcMemHandle_t pool, table, outbox;
+  uint64_t pool_bytes, table_slots, outbox_bytes;
   int32_t device, pad;
 };
+
+// A location word with this bit names a byte offset in the owner's outbox:
+// HBM through which blocks of the owner's DRAM tier reach peers (peers map
+// only each other's HBM, not pinned host memory).
+constexpr uint64_t kLocOutbox = 1ull << 62;
+constexpr uint64_t kLocOutboxOff = ~(kLocDram | kLocOutbox);
+
+// Index meta word of a block (occupied, packed, prefix, size).
+inline uint64_t meta_of(const BlockMeta &m) {
+  return kMetaOccupied | (m.size & kSizeMask) | (m.prefix ? kMetaPrefix : 0) | (m.packed ? kMetaPacked : 0);
+}
 
 inline uint64_t be_owner(const HKey &k, int world) {
   return (uint64_t)owner_of(Key{k.lo, k.hi}, world);
@@ -93,6 +105,13 @@ struct DhtState {
   ncclComm_t comm = nullptr;
   int W = 1, me = 0;
   std::vector<uint64_t> pool, pool_bytes, table, slots;
+  // Outbox (HBM, exported like the pool): a get stages the DRAM-tier blocks
+  // that other ranks requested here, a put receives here the new blocks
+  // this owner places straight into its DRAM tier. Reused every step; the
+  // closing all-reduce of each step keeps it until every peer is done.
+  uint8_t *outbox = nullptr;
+  uint64_t outbox_bytes = 0;
+  std::vector<uint64_t> peer_outbox, peer_outbox_bytes;
   std::vector<int> device;
   std::vector<void *> opened;
   DevBuf d_send, d_recv, d_misc;
@@ -319,6 +338,17 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   memset(&ex, 0, sizeof ex);
   CB_TRY_CUDA(cudaIpcGetMemHandle(&ex.pool, pool), "cudaIpcGetMemHandle(pool)");
   CB_TRY_CUDA(cudaIpcGetMemHandle(&ex.table, table), "cudaIpcGetMemHandle(index)");
+  if (policy.dram_capacity() > 0) {  // a DRAM tier: peers reach it through the outbox
+    // an eighth of the pool (at least 64 MiB), at most 2 GiB or the DRAM tier
+    const uint64_t want = std::max<uint64_t>(pool_bytes / 8, 64ull << 20);
+    const uint64_t ob = std::min<uint64_t>(std::min<uint64_t>(want, 2ull << 30), policy.dram_capacity()) / 256 * 256;
+    if (ob) {
+      CB_TRY_CUDA(cudaMalloc(&dht->outbox, ob), "outbox");
+      dht->outbox_bytes = ob;
+      CB_TRY_CUDA(cudaIpcGetMemHandle(&ex.outbox, dht->outbox), "cudaIpcGetMemHandle(outbox)");
+      ex.outbox_bytes = ob;
+    }
+  }
   ex.pool_bytes = pool_bytes;
   ex.table_slots = table_slots;
   ex.device = device;
@@ -341,16 +371,26 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   dht->table.assign(W, 0);
   dht->slots.assign(W, 0);
   dht->device.assign(W, -1);
+  dht->peer_outbox.assign(W, 0);
+  dht->peer_outbox_bytes.assign(W, 0);
   for (int p = 0; p < W; ++p) {
     Export e;
     memcpy(&e, h + sizeof(Export) * (p + 1), sizeof e);
     dht->pool_bytes[p] = e.pool_bytes;
     dht->slots[p] = e.table_slots;
     dht->device[p] = e.device;
+    dht->peer_outbox_bytes[p] = e.outbox_bytes;
     if (p == r) {
       dht->pool[p] = (uint64_t)pool;
       dht->table[p] = (uint64_t)table;
+      dht->peer_outbox[p] = (uint64_t)dht->outbox;
       continue;
+    }
+    if (e.outbox_bytes) {
+      void *po = nullptr;
+      CB_TRY_CUDA(cudaIpcOpenMemHandle(&po, e.outbox, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(outbox)");
+      dht->opened.push_back(po);
+      dht->peer_outbox[p] = (uint64_t)po;
     }
     void *pp = nullptr, *pt = nullptr;
     CB_TRY_CUDA(cudaIpcOpenMemHandle(&pp, e.pool, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle(pool)");
@@ -362,7 +402,9 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   }
   rank = r;
   world = W;
-  policy.set_direct_dram_placement(false);
+  // a new block an owner places straight into its DRAM tier arrives through
+  // its outbox: at most the outbox's bytes per put step
+  policy.set_direct_dram_budget(dht->outbox_bytes);
   if (cfg.locality_aware || cfg.prefix_replication) {
     // one replica region serves hot-block replicas and prefix replicas
     uint64_t rb = cfg.replica_bytes ? cfg.replica_bytes : std::min<uint64_t>(pool_bytes / 32, 4ull << 30);
@@ -387,6 +429,7 @@ void Store::dht_detach() {
   }
   for (void *p : dht->opened) cudaIpcCloseMemHandle(p);
   if (dht->rbase) cudaFree(dht->rbase);
+  if (dht->outbox) cudaFree(dht->outbox);
   dht->d_send.release();
   dht->d_recv.release();
   dht->d_misc.release();
@@ -492,10 +535,24 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   }
   std::vector<PutRep> reps(nrecv);
   for (uint32_t j = 0; j < nrecv; ++j) reps[j] = PutRep{oloc[j], ostatus[j], 0};
+  // A new block this owner places straight into its DRAM tier (no HBM room
+  // even after demotions) is handed over through the outbox: the writer
+  // stores it there, the owner moves it to DRAM once the step's writes are
+  // done (below). The index records the final DRAM location.
+  std::vector<std::pair<const Placement *, uint64_t>> inbox;  // placement, outbox offset
+  uint64_t ib = 0;
   std::vector<IndexRec> ins;
   ins.reserve(plan.places.size());
-  for (const Placement &p : plan.places)
-    ins.push_back(IndexRec{p.key.lo, p.key.hi, oloc[p.idx], (p.size & kSizeMask) | (p.prefix ? kMetaPrefix : 0)});
+  for (const Placement &p : plan.places) {
+    if (p.tier == kTierDram) {
+      inbox.emplace_back(&p, ib);
+      reps[p.idx].loc = ib | kLocOutbox;
+      ib += align_up(p.size, 256);
+    }
+    ins.push_back(IndexRec{p.key.lo, p.key.hi, oloc[p.idx],
+                           ((p.packed ? (p.size & ~1ull) : p.size) & kSizeMask) | (p.prefix ? kMetaPrefix : 0) |
+                               (p.packed ? kMetaPacked : 0)});
+  }
   policy.commit();
   // replies reuse the request buffers (PutRep <= PutReq)
   memcpy(dht->h_recv.ptr, reps.data(), sizeof(PutRep) * nrecv);
@@ -537,11 +594,12 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
       remote_dedup_bytes += cfg.dedup_enabled ? sizes[i] : 0;
     }
     if (mine[j].status != CB_PUT_STORED || !sizes[i]) continue;
-    if (mine[j].loc & kLocDram) {  // only owner-local DRAM placements are reachable
-      status[i] = CB_PUT_FAILED;
-      continue;
+    uint64_t dst;
+    if (mine[j].loc & kLocOutbox) {  // bound for the owner's DRAM tier, through its outbox
+      dst = dht->peer_outbox[owner] + (mine[j].loc & kLocOutboxOff);
+    } else {
+      dst = dht->pool[owner] + (mine[j].loc & kLocOffMask);
     }
-    const uint64_t dst = dht->pool[owner] + (mine[j].loc & kLocOffMask);
     if (owner != me) peer_bytes_written += sizes[i];
     us.push_back(total);
     desc.push_back(CopyDesc{dptr[i], dst, sizes[i], owner == me ? 0u : 1u});
@@ -579,6 +637,10 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   if (rc) return rc;
   rc = check_device_error(st);
   if (rc) return rc;
+  if (!inbox.empty()) {
+    rc = dht_drain_inbox(inbox, st);
+    if (rc) return rc;
+  }
   for (int i = 0; i < n; ++i) {
     if (keys_out) memcpy(keys_out + 16 * i, &keys[i], 16);
     if (status_out) status_out[i] = status[i];
@@ -587,6 +649,53 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
     if (status[i] == CB_PUT_STORED && is_prefix && is_prefix[i]) dht->registry.insert(keys[i]);
   }
   return CB_OK;
+}
+
+// Owner side, after a put step's writes: the blocks writers stored in this
+// owner's outbox go to their DRAM-tier extents - plain ones by the D2H copy
+// engine, INT8-packed ones (kv_compression) by the pack kernels writing the
+// mapped arena.
+int Store::dht_drain_inbox(const std::vector<std::pair<const Placement *, uint64_t>> &inbox, cudaStream_t st) {
+  CB_TRY_CUDA(ensure_dram(), "pinned DRAM arena cudaHostAlloc");
+  std::vector<CopyDesc> desc;
+  std::vector<uint32_t> us;
+  uint32_t total = 0;
+  for (const auto &pe : inbox) {
+    const Placement &p = *pe.first;
+    const uint8_t *src = dht->outbox + pe.second;
+    if (!p.size) continue;
+    if (!p.packed) {
+      CB_TRY_CUDA(cudaMemcpyAsync(dram_host + p.off, src, p.size, cudaMemcpyDeviceToHost, st), "inbox to DRAM");
+      continue;
+    }
+    us.push_back(total);
+    desc.push_back(CopyDesc{(uint64_t)src, (uint64_t)dram_dev + p.off, p.size, kCopyHost});
+    total += (uint32_t)((p.size + kCopyUnit - 1) / kCopyUnit);
+  }
+  if (!desc.empty()) {
+    const int nd = (int)desc.size();
+    us.push_back(total);
+    const size_t o_us = align_up(sizeof(CopyDesc) * nd, 256);
+    const size_t o_mm = align_up(o_us + 4 * us.size(), 256);
+    const size_t need = o_mm + sizeof(int) * 2 * nd;
+    CB_TRY_CUDA(h_scratch.ensure(need), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(need), "device");
+    uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+    memcpy(h, desc.data(), sizeof(CopyDesc) * nd);
+    memcpy(h + o_us, us.data(), 4 * us.size());
+    int *mm = reinterpret_cast<int *>(h + o_mm);
+    for (int j = 0; j < nd; ++j) {
+      mm[2 * j] = INT_MAX;
+      mm[2 * j + 1] = INT_MIN;
+    }
+    uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, need, cudaMemcpyHostToDevice, st), "H2D pack");
+    CB_TRY_CUDA(launch_kv_pack(reinterpret_cast<const CopyDesc *>(d), reinterpret_cast<const uint32_t *>(d + o_us), nd,
+                               total, reinterpret_cast<int *>(d + o_mm), num_sms, st),
+                "inbox pack");
+    launches += 2;
+  }
+  return check_device_error(st);  // syncs
 }
 
 // ------------------------------------------------------------ prefix sync
@@ -756,9 +865,14 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
   uint64_t *rr = reinterpret_cast<uint64_t *>(rk + 16 * rmax);  // replies
   rc = dht_alltoallv(dht->d_send.ptr, scount.data(), rk, rcount.data(), 16, st);
   if (rc) return rc;
-  CB_TRY_CUDA(launch_index_serve(table, table_slots - 1, reinterpret_cast<const Key *>(rk), (int)nrecv, rr, st),
-              "index serve");
-  launches++;
+  if (dht->outbox && policy.dram_used() > 0) {
+    rc = dht_serve_host(rk, nrecv, rcount.data(), rr, st);
+    if (rc) return rc;
+  } else {
+    CB_TRY_CUDA(launch_index_serve(table, table_slots - 1, reinterpret_cast<const Key *>(rk), (int)nrecv, rr, st),
+                "index serve");
+    launches++;
+  }
   // keys this owner served, for its LRU order (read after the sync below)
   CB_TRY_CUDA(cudaMemcpyAsync(dht->h_recv.ptr, rk, 16ull * nrecv, cudaMemcpyDeviceToHost, st), "D2H served keys");
   rc = dht_alltoallv(rr, rcount.data(), dht->d_send.ptr, scount.data(), 16, st);
@@ -774,6 +888,60 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
     reps[2ull * order[j]] = hr[2ull * j];
     reps[2ull * order[j] + 1] = hr[2ull * j + 1];
   }
+  return CB_OK;
+}
+
+// Owner side of a lookup with a non-empty DRAM tier. The host metadata is
+// authoritative for the blocks this rank owns, so the replies are built from
+// it; a DRAM-tier block another rank asked for is copied by the H2D copy
+// engine from the pinned arena into the outbox (as it sits there: INT8-packed
+// blocks stay packed, the requester's gather unpacks them) and the reply
+// names its outbox offset. The reference serves such reads from the owner's
+// DRAM shadow through MPI_Get (src/distributed_backend.cpp:729-767,
+// :210-219); it leaves the owner's tiers as they are, and so does this.
+// Requests of this rank for its own DRAM blocks are read from the mapped
+// arena directly. Blocks beyond the outbox's room are reported as found in
+// remote DRAM and not copied.
+int Store::dht_serve_host(const uint8_t *d_keys, uint32_t nrecv, const uint32_t *rcount, uint64_t *d_reps,
+                          cudaStream_t st) {
+  const int W = dht->W, me = dht->me;
+  const size_t o_rep = align_up(16ull * nrecv, 256);
+  CB_TRY_CUDA(h_scratch.ensure(o_rep + 16ull * std::max<uint32_t>(nrecv, 1)), "pinned");
+  uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
+  if (nrecv) CB_TRY_CUDA(cudaMemcpyAsync(h, d_keys, 16ull * nrecv, cudaMemcpyDeviceToHost, st), "D2H keys");
+  int rc = dht_sync(st);
+  if (rc) return rc;
+  uint64_t *reps = reinterpret_cast<uint64_t *>(h + o_rep);
+  uint64_t ob = 0;
+  uint32_t j = 0;
+  for (int r = 0; r < W; ++r) {
+    for (uint32_t t = 0; t < rcount[r]; ++t, ++j) {
+      const BlockMeta *m = policy.find(to_hkey(h + 16ull * j));
+      uint64_t loc = 0, meta = 0;
+      if (m) {
+        meta = meta_of(*m);
+        loc = Policy::data_offset(*m);
+        if (m->tier == kTierDram) {
+          loc |= kLocDram;
+          const uint64_t foot = Policy::footprint(*m);
+          const uint64_t lead = m->packed ? kPackLead : 0;  // keeps a packed payload 16-byte aligned
+          const uint64_t slot = align_up(lead + foot, 256);
+          if (r != me && ob + slot <= dht->outbox_bytes) {
+            if (foot)
+              CB_TRY_CUDA(cudaMemcpyAsync(dht->outbox + ob + lead, dram_host + Policy::data_offset(*m), foot,
+                                          cudaMemcpyHostToDevice, st),
+                          "DRAM block to outbox");
+            loc = (ob + lead) | kLocOutbox;
+            ob += slot;
+          }
+        }
+      }
+      reps[2ull * j] = loc;
+      reps[2ull * j + 1] = meta;
+    }
+  }
+  if (nrecv)
+    CB_TRY_CUDA(cudaMemcpyAsync(d_reps, reps, 16ull * nrecv, cudaMemcpyHostToDevice, st), "H2D replies");
   return CB_OK;
 }
 
@@ -852,7 +1020,9 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
     const uint64_t meta = reps[2ull * i + 1], loc = reps[2ull * i];
     const uint64_t sz = meta & kSizeMask;
     const bool replica = rep_off[i] >= 0;
-    const bool dram = !replica && (loc & kLocDram) != 0;
+    const bool staged = !replica && (loc & kLocOutbox) != 0;  // a DRAM-tier block, in the owner's outbox
+    const bool dram = !replica && !staged && (loc & kLocDram) != 0;
+    const bool in_dram = dram || staged;
     const bool local = owner[i] == me;
     sizes_out[i] = 0;
     if (!(meta & kMetaOccupied)) {
@@ -861,12 +1031,12 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
       continue;
     }
     sizes_out[i] = sz;
-    found_out[i] = dram ? (local ? CB_FOUND_LOCAL_DRAM : CB_FOUND_REMOTE_DRAM)
-                        : (local ? CB_FOUND_LOCAL_HBM : CB_FOUND_REMOTE_HBM);
-    if (local && !dram) local_gpu_hits++;
-    if (local && dram) local_dram_hits++;
-    if (!local && !dram) remote_gpu_hits++;
-    if (!local && dram) remote_dram_hits++;
+    found_out[i] = in_dram ? (local ? CB_FOUND_LOCAL_DRAM : CB_FOUND_REMOTE_DRAM)
+                           : (local ? CB_FOUND_LOCAL_HBM : CB_FOUND_REMOTE_HBM);
+    if (local && !in_dram) local_gpu_hits++;
+    if (local && in_dram) local_dram_hits++;
+    if (!local && !in_dram) remote_gpu_hits++;
+    if (!local && in_dram) remote_dram_hits++;
     if (dht->locality) dht->record_access(to_hkey(keys + 16 * i), !local);
     if (sz > caps[i] || (dram && !local)) {  // too small, or a peer's pinned DRAM (not mapped here)
       found_out[i] |= CB_FOUND_NOT_COPIED;
@@ -880,11 +1050,16 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
     } else {
       if (leader[uidx[i]] >= 0) continue;  // a repeat: filled from the leader below
       leader[uidx[i]] = i;
-      if (!local) peer_bytes_read += sz;
-      const uint64_t off = loc & kLocOffMask;
-      src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
-      flags = (dram || !local) ? kCopyHost : 0;  // peer and pinned-host sources: plain loads
-      if (dram && (meta & kMetaPacked)) flags |= kCopyUnpack;
+      const bool packed = in_dram && (meta & kMetaPacked);
+      if (!local) peer_bytes_read += packed ? packed_bytes(sz) : sz;
+      if (staged) {
+        src = dht->peer_outbox[owner[i]] + (loc & kLocOutboxOff);
+      } else {
+        const uint64_t off = loc & kLocOffMask;
+        src = dram ? (uint64_t)dram_dev + off : dht->pool[owner[i]] + off;
+      }
+      flags = (in_dram || !local) ? kCopyHost : 0;  // peer and pinned-host sources: plain loads
+      if (packed) flags |= kCopyUnpack;
     }
     us.push_back(total);
     desc.push_back(CopyDesc{src, dst[i], sz, flags});
@@ -912,7 +1087,11 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
   if (dht->locality) {
     for (int u = 0; u < m; ++u) {
       const int l = leader[u];
-      if (l < 0 || (found_out[l] & 0x0f) != CB_FOUND_REMOTE_HBM) continue;
+      if (l < 0) continue;
+      const uint32_t code = found_out[l];
+      if ((code & CB_FOUND_NOT_COPIED) ||
+          ((code & 0x0f) != CB_FOUND_REMOTE_HBM && (code & 0x0f) != CB_FOUND_REMOTE_DRAM))
+        continue;
       const HKey k = to_hkey(ukeys.data() + 16 * u);
       if (dht->rmap.count(k) || !dht->should_promote(k)) continue;
       const uint64_t sz = sizes_out[l];
@@ -1069,7 +1248,7 @@ struct cb_planner {
   bool dedup;
   cb::PutPlan plan;
   cb_planner(uint64_t hbm, uint64_t dram, bool semantic, bool dd) : policy(hbm, dram, semantic), dedup(dd) {
-    policy.set_direct_dram_placement(false);  // as a DHT owner (cb_dht_attach)
+    policy.set_direct_dram_budget(0);  // as a DHT owner without an outbox (cb_dht_attach)
   }
 };
 

@@ -243,6 +243,7 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
                       bool dedup_enabled, PutPlan &plan) {
   plan.clear();
   plan.status.assign(n, 0);
+  uint64_t direct_left = direct_dram_budget_;
   for (int i = 0; i < n; ++i) {
     const HKey &k = keys[i];
     const uint64_t size = sizes[i];
@@ -264,7 +265,8 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
       off = hbm_.alloc(size);
     }
     bool pack = false;
-    if (off == UINT64_MAX && direct_dram_) {
+    const uint64_t staged = (size + 255) / 256 * 256;
+    if (off == UINT64_MAX && staged <= direct_left) {
       // Larger than the whole HBM pool (or every HBM block pending): the
       // reference's put still succeeds through its DRAM copy
       // (distributed_backend.cpp:643-652), compressed when kv_compression is
@@ -275,6 +277,7 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
       if (make_dram_room(dbytes, dext, plan.dropped)) {
         off = dram_.alloc(dext);
         tier = kTierDram;
+        if (direct_left != UINT64_MAX) direct_left -= staged;
       }
     }
     if (off == UINT64_MAX) {

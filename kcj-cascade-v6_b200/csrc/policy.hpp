@@ -194,9 +194,11 @@ class Policy {
   const PolicyCounters &counters() const { return ctr_; }
   void reset_counters() { ctr_ = PolicyCounters{}; }
   const ExtentAllocator &hbm_alloc() const { return hbm_; }
-  // When false, a new block that cannot get HBM fails instead of landing in
-  // the DRAM tier (DHT mode: remote writers can only reach HBM pools).
-  void set_direct_dram_placement(bool on) { direct_dram_ = on; }
+  // Bytes of new blocks one plan_put may place straight into the DRAM tier
+  // (counted as 256-byte-rounded block sizes); a new block that cannot get
+  // HBM beyond that fails. Unlimited on one GPU; on a DHT owner the size of
+  // its inbox, through which remote writers hand such blocks over.
+  void set_direct_dram_budget(uint64_t bytes) { direct_dram_budget_ = bytes; }
   // INT8 packing of DRAM-tier blocks >= kPackMinBytes (kv_compression).
   void set_compression(bool on) { compress_ = on; }
   bool compression() const { return compress_; }
@@ -221,7 +223,7 @@ class Policy {
 
   uint64_t hbm_cap_, dram_cap_;
   bool semantic_;
-  bool direct_dram_ = true;
+  uint64_t direct_dram_budget_ = UINT64_MAX;
   bool compress_ = false;
   ExtentAllocator hbm_, dram_;
   uint64_t hbm_used_ = 0, dram_used_ = 0;  // logical bytes (reference used_)

@@ -284,6 +284,12 @@ struct Store {
   int dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st);
   int dht_cluster_usage(cb_stats *o);
   int dht_sync_prefixes(cudaStream_t st);
+  int dht_drain_inbox(const std::vector<std::pair<const Placement *, uint64_t>> &inbox, cudaStream_t st);
+  // Owner side of a get step when this rank's DRAM tier holds blocks: the
+  // replies come from the host metadata, and DRAM-tier blocks other ranks
+  // asked for are staged into the outbox for their peer loads.
+  int dht_serve_host(const uint8_t *d_keys, uint32_t nrecv, const uint32_t *rcount, uint64_t *d_reps,
+                     cudaStream_t st);
   uint64_t dht_registry_size() const;
   uint64_t dht_prefix_replicas() const;
 };

@@ -140,6 +140,28 @@ def main():
 
     store.clear()
     assert not store.contains(uniq[0])
+
+    # pipelined puts: four steps of 16 blocks per rank submitted before any
+    # wait, each placed in submission order by the collective DHT put; the
+    # statuses equal the oracle's four sequential steps
+    ora2 = DhtOracle(world)
+    futs = []
+    for j in range(4):
+        part = items[rank][16 * j:16 * (j + 1)]
+        futs.append(store.batch_put_async([torch.from_numpy(pool[s].copy()).to(dev) for s, _ in part],
+                                          is_prefix=[pf for _, pf in part]))
+    want2 = [ora2.put_step([[(ids_all[r][16 * j + i], pool[s].tobytes(), pf)
+                             for i, (s, pf) in enumerate(items[r][16 * j:16 * (j + 1)])] for r in range(world)])
+             for j in range(4)]
+    for j, f in enumerate(futs):
+        got_ids, got_st = f.result(return_status=True)
+        assert got_ids == ids_all[rank][16 * j:16 * (j + 1)], ("pipelined ids", j)
+        assert got_st == want2[j][rank], ("pipelined status", j, got_st, want2[j][rank])
+    assert store.get_stats().dedup_hits == ora2.dedup_hits[rank], "pipelined dedup"
+    outs = [torch.empty(len(by_id[b]), dtype=torch.uint8, device=dev) for b in req]
+    found, sizes = store.batch_get(req, outs)
+    assert all(found) and all(np.array_equal(o.cpu().numpy(), by_id[b]) for o, b in zip(outs, req)), "pipelined bytes"
+    store.clear()
     store.barrier()
     store.close()
     dist.destroy_process_group()

@@ -42,3 +42,18 @@ def test_dht_rank_leaving_is_detected():
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
     assert "collective failed" in r.stdout, r.stdout[-2000:]
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["plain", "compress"])
+def test_dht_dram_tier_through_the_outbox(mode):
+    """Owners with small HBM pools and a DRAM tier: pipelined puts whose
+    blocks land in the owners' DRAM tiers (demoted, or placed there through
+    the outbox) and every block read back by every rank
+    (tests/dht_dram_worker.py)."""
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", os.path.join(HERE, "dht_dram_worker.py"), mode]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-4000:]
+    assert r.stdout.count("DHT DRAM parity ok") == 2
