@@ -18,8 +18,9 @@
 //             index, reply {status, offset} -> writers copy new blocks into
 //             the owners' pools -> closing all-reduce (barrier).
 // batch_get : keys to owners -> owner index lookup kernel -> replies
-//             {location, meta} -> gather kernel reading the owners' pools ->
-//             closing all-reduce.
+//             {location, meta} -> gather kernel reading the owners' pools
+//             (the next step's counts all-gather keeps owners from reusing
+//             extents before the readers are done).
 // Every collective call is made by all ranks in the same order. Waits are
 // bounded: a collective that does not finish within the timeout aborts the
 // communicator and returns CB_ERR_TIMEOUT.
@@ -107,8 +108,9 @@ struct DhtState {
   std::vector<uint64_t> pool, pool_bytes, table, slots;
   // Outbox (HBM, exported like the pool): a get stages the DRAM-tier blocks
   // that other ranks requested here, a put receives here the new blocks
-  // this owner places straight into its DRAM tier. Reused every step; the
-  // closing all-reduce of each step keeps it until every peer is done.
+  // this owner places straight into its DRAM tier. Reused every step: a
+  // put's closing all-reduce, and a get's successor step's opening counts
+  // all-gather, keep its contents until every peer is done with them.
   uint8_t *outbox = nullptr;
   uint64_t outbox_bytes = 0;
   std::vector<uint64_t> peer_outbox, peer_outbox_bytes;
@@ -839,7 +841,7 @@ uint64_t Store::dht_prefix_replicas() const { return dht ? dht->prefix_replicas 
 // Sends keys to their owners, runs the owner lookup kernel, returns for each
 // key (in the caller's order) {location, meta} in reps (host) and the owner.
 int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, std::vector<int> &owner,
-                      cudaStream_t st) {
+                      cudaStream_t st, bool stage) {
   const int W = dht->W;
   std::vector<uint32_t> scount(W, 0), rcount(W, 0);
   std::vector<int> order(n);
@@ -866,7 +868,7 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
   rc = dht_alltoallv(dht->d_send.ptr, scount.data(), rk, rcount.data(), 16, st);
   if (rc) return rc;
   if (dht->outbox && policy.dram_used() > 0) {
-    rc = dht_serve_host(rk, nrecv, rcount.data(), rr, st);
+    rc = dht_serve_host(rk, nrecv, rcount.data(), rr, st, stage);
     if (rc) return rc;
   } else {
     CB_TRY_CUDA(launch_index_serve(table, table_slots - 1, reinterpret_cast<const Key *>(rk), (int)nrecv, rr, st),
@@ -903,7 +905,7 @@ int Store::dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, s
 // arena directly. Blocks beyond the outbox's room are reported as found in
 // remote DRAM and not copied.
 int Store::dht_serve_host(const uint8_t *d_keys, uint32_t nrecv, const uint32_t *rcount, uint64_t *d_reps,
-                          cudaStream_t st) {
+                          cudaStream_t st, bool stage) {
   const int W = dht->W, me = dht->me;
   const size_t o_rep = align_up(16ull * nrecv, 256);
   CB_TRY_CUDA(h_scratch.ensure(o_rep + 16ull * std::max<uint32_t>(nrecv, 1)), "pinned");
@@ -926,7 +928,7 @@ int Store::dht_serve_host(const uint8_t *d_keys, uint32_t nrecv, const uint32_t 
           const uint64_t foot = Policy::footprint(*m);
           const uint64_t lead = m->packed ? kPackLead : 0;  // keeps a packed payload 16-byte aligned
           const uint64_t slot = align_up(lead + foot, 256);
-          if (r != me && ob + slot <= dht->outbox_bytes) {
+          if (stage && r != me && ob + slot <= dht->outbox_bytes) {
             if (foot)
               CB_TRY_CUDA(cudaMemcpyAsync(dht->outbox + ob + lead, dram_host + Policy::data_offset(*m), foot,
                                           cudaMemcpyHostToDevice, st),
@@ -1143,11 +1145,12 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
                 "repeat copies");
     launches++;
   }
-  // owners must not reuse pool extents before every reader is done
-  CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
-  rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
-                "ncclAllReduce(get barrier)");
-  if (rc) return rc;
+  // No closing barrier: an owner rewrites its pool or outbox only in a later
+  // collective step (a put's scatter into extents it plans then, the staging
+  // of a later get), and every step opens with the counts all-gather, which
+  // completes on the owner only after every reader enqueued its part of it -
+  // behind this gather on the reader's stream (and this call waits for the
+  // gather before it returns anyway).
   if (mem_kind == CB_MEM_HOST) {
     // one D2H per run of blocks contiguous both in staging and in the
     // caller's memory (a caller's [n, block] buffer is one copy)
@@ -1182,7 +1185,7 @@ int Store::dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStre
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   std::vector<uint64_t> reps;
   std::vector<int> owner;
-  int rc = dht_lookup(keys, n, reps, owner, st);
+  int rc = dht_lookup(keys, n, reps, owner, st, false);
   if (rc) return rc;
   for (int i = 0; i < n; ++i) found_out[i] = (reps[2ull * i + 1] & kMetaOccupied) ? 1 : 0;
   return CB_OK;

@@ -272,8 +272,10 @@ struct Store {
   int dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st);
   int dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount, size_t rec,
                     cudaStream_t st);
+  // stage: DRAM-tier blocks other ranks ask for go to the outbox (a get);
+  // without it the replies only say where each block is (contains).
   int dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, std::vector<int> &owner,
-                 cudaStream_t st);
+                 cudaStream_t st, bool stage = true);
   int dht_locate(const uint8_t *key, cb_location *out, int32_t *found);
   void dht_clear_replicas();
   int dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
@@ -289,7 +291,7 @@ struct Store {
   // replies come from the host metadata, and DRAM-tier blocks other ranks
   // asked for are staged into the outbox for their peer loads.
   int dht_serve_host(const uint8_t *d_keys, uint32_t nrecv, const uint32_t *rcount, uint64_t *d_reps,
-                     cudaStream_t st);
+                     cudaStream_t st, bool stage);
   uint64_t dht_registry_size() const;
   uint64_t dht_prefix_replicas() const;
 };
