@@ -460,7 +460,8 @@ def main():
         sync_all()
     if not all(np.array_equal(k, keys_ref) for k in step_keys):
         raise SystemExit("block IDs of a timed step differ from the warm-up's")
-    dedup_step = reduce_sum((store._n.stats().dedup_hits - st0.dedup_hits) / max(args.steps, 1), world)
+    # clear() resets the counters: what they hold now is the last step's
+    dedup_step = reduce_sum(store._n.stats().dedup_hits, world)
     elapsed = t_ev0.elapsed_time(t_ev1) / 1e3
     st1 = store._n.stats()
     remote_b = st1.peer_bytes_read - st0.peer_bytes_read  # crossed NVLink

@@ -21,9 +21,13 @@ struct HashProgress {
 };
 
 // sha256.cu — digests: n * 8 words holding the 32 digest bytes in order.
-// One CTA (producer + consumer warp) per 32 blocks. progress may be null.
+// progress may be null. many_chains = false: one CTA (producer + consumer
+// warp) per 32 blocks, the fastest chains when few run; true: the fused
+// kernel (one warp per 32 blocks, half the issue resources per chain), the
+// higher throughput when many chains run at once (pipelined puts).
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
-                                unsigned *d_err, cudaStream_t stream, const HashProgress *progress = nullptr);
+                                unsigned *d_err, cudaStream_t stream, const HashProgress *progress = nullptr,
+                                bool many_chains = false);
 // Loads the SHA-256 kernel's module on the current device now (with lazy
 // module loading it would otherwise load, and allocate, at its first launch).
 cudaError_t prepare_sha256_kernel();

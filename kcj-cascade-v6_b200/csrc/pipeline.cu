@@ -11,10 +11,9 @@
 //    kHashSlots side streams (small batches queued back to back share one
 //    launch of up to kLaunchBlocks blocks) and returns a ticket;
 //  * batches are placed - sequential dedup plan, tier moves, scatter into the
-//    pool, index insert - strictly in ticket order, each as soon as its
-//    digests are back and, at the latest, when more than `pipeline_blocks`
-//    blocks are waiting, or when cb_put_wait / any other data call needs
-//    them. Placement in ticket order keeps the sequential dedup rule of
+//    pool, index insert - strictly in ticket order, when more than
+//    `pipeline_blocks` blocks are waiting, or when cb_put_wait / any other
+//    data call needs them. Placement in ticket order keeps the sequential dedup rule of
 //    DistributedStore::put_batch (src/distributed_backend.cpp:813-841)
 //    exactly: a block is a dedup hit iff its key was stored before it.
 //
@@ -52,7 +51,7 @@ namespace {
 constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
 constexpr uint64_t kDefaultPipelineBlocks = 16384;  // blocks hashing ahead of placement (1 GPU)
 constexpr size_t kDhtPending = 8;                // DHT: batches submitted and not placed (every rank alike)
-constexpr int kScatterLsuCtasPerSm = 4;          // pipelined scatters share the SMs with the hashes
+constexpr int kScatterLsuCtasPerSm = 4;          // LSU engine (copy_engine = 2): CTAs per SM beside the hashes
 
 inline size_t digest_offset(int cap) { return align_up(sizeof(HashJob) * (size_t)cap, 256); }
 
@@ -178,7 +177,7 @@ int Store::launch_open_slot() {
                     [&] {
                       return launch_sha256_batch(reinterpret_cast<const HashJob *>(dp), h.n,
                                                  reinterpret_cast<uint32_t *>(dp + o_dig), hash_lanes, d_err,
-                                                 h.stream);
+                                                 h.stream, nullptr, /*many_chains=*/true);
                     }),
               "sha256 launch");
   CB_TRY_CUDA(cudaMemcpyAsync(hp + o_dig, dp + o_dig, 32ull * h.n, cudaMemcpyDeviceToHost, h.stream), "D2H digests");
@@ -251,21 +250,11 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
     }
     return CB_OK;
   }
+  // Place only as much as keeps `limit` blocks hashing: concurrent launches
+  // tend to finish together, and placing every finished batch at once would
+  // leave the GPU without new launches while the host plans them.
   const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultPipelineBlocks;
   while (!aput.empty() && inflight_blocks > limit) {
-    rc = place_oldest();
-    if (rc) return rc;
-  }
-  // place whatever is ready, so placements keep pace with the hashes
-  while (!aput.empty()) {
-    const AsyncPut &f = aput.front();
-    if (f.slot >= 0) {
-      const HashSlot &h = hslots[f.slot];
-      if (!h.launched) break;
-      const cudaError_t q = cudaEventQuery(h.done);
-      if (q == cudaErrorNotReady) break;
-      if (q != cudaSuccess) return cuda_fail(q, "hash");
-    }
     rc = place_oldest();
     if (rc) return rc;
   }
@@ -328,7 +317,9 @@ int Store::place_batch(const std::vector<HKey> &keys, AsyncPut &b) {
   if (!plan.places.empty()) {
     ScratchSlot *sl = take_scratch(4096, rc);
     if (!sl) return rc;
-    rc = enqueue_places(plan, b.ptrs.data(), put_stream, sl->h, sl->d, 2, kScatterLsuCtasPerSm);
+    // the TMA engine: one lane per SM issues the bulk copies, so the scatter
+    // takes next to no issue slots from the hash warps beside it
+    rc = enqueue_places(plan, b.ptrs.data(), put_stream, sl->h, sl->d, copy_engine, kScatterLsuCtasPerSm);
     if (rc) return rc;
     CB_TRY_CUDA(cudaEventRecord(sl->done, put_stream), "event");
     sl->pending = true;

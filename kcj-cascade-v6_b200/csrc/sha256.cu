@@ -326,15 +326,22 @@ namespace cb {
 
 cudaError_t prepare_sha256_kernel() {
   cudaFuncAttributes a;
-  return cudaFuncGetAttributes(&a, sha256_pc_kernel);
+  return cudaFuncGetAttributes(&a, sha256_pc_kernel);  // loads this file's module (both kernels)
 }
 
 cudaError_t launch_sha256_batch(const HashJob *d_jobs, int n, uint32_t *d_digests, int lanes,
-                                unsigned *d_err, cudaStream_t stream, const HashProgress *progress) {
+                                unsigned *d_err, cudaStream_t stream, const HashProgress *progress,
+                                bool many_chains) {
   (void)lanes;
   if (n <= 0) return cudaSuccess;
   const HashProgress pg = progress ? *progress : HashProgress{nullptr, 1, 0, 0};
-  sha256_pc_kernel<<<(n + 31) / 32, 64, 0, stream>>>(d_jobs, n, d_digests, d_err, 1u, pg);
+  if (many_chains) {
+    constexpr int kThreads = 32 * kFusedWarps;
+    sha256_fused_kernel<<<(n + kThreads - 1) / kThreads, kThreads, 0, stream>>>(d_jobs, n, d_digests, d_err, 1u,
+                                                                               pg);
+  } else {
+    sha256_pc_kernel<<<(n + 31) / 32, 64, 0, stream>>>(d_jobs, n, d_digests, d_err, 1u, pg);
+  }
   return cudaGetLastError();
 }
 

@@ -1,17 +1,25 @@
-// Fused SHA-256 kernel: one warp per 32 blocks, included by sha256.cu (it
-// uses that file's load, padding and progress-wait helpers).
+// Fused SHA-256 kernel for many chains in flight (pipelined puts): one warp
+// per 32 blocks, included by sha256.cu (it uses that file's load, padding and
+// progress-wait helpers).
 //
-// Each lane runs its block's message schedule and rounds itself, with no
-// shared-memory hand-off, and every addition is issued as IMAD on the FMA
-// pipe. The half-rate integer ALU pipe then carries only the rotates,
-// shifts and 3-input logic: 10 instructions per round (Sigma0, Sigma1: 3
-// SHF + LOP3 each; Ch, Maj: one LOP3) and 8 per schedule word (sigma0,
-// sigma1: 2 SHF + SHR + LOP3 each), i.e. 1040 ALU instructions per 64-byte
-// chunk with the byte swaps, while 7 + 3 IMAD go to the FMA pipe beside
-// them. The independent schedule words fill the gaps of the two round
-// recurrences, so one such warp keeps its sub-partition's ALU pipe busy: a
-// GPU full of them hashes at the ALU-pipe rate, where the producer/consumer
-// pair spends a second sub-partition on the schedule of the same 32 chains.
+// Each lane runs its block's whole compression - message schedule and
+// rounds - with no shared-memory hand-off, and every addition is issued as
+// IMAD on the FMA pipe, so the half-rate integer ALU pipe carries only the
+// rotates, shifts and 3-input logic: 10 instructions per round (Sigma0,
+// Sigma1: 3 SHF + LOP3 each; Ch, Maj: one LOP3) and 8 per schedule word
+// (sigma0, sigma1: 2 SHF + SHR + LOP3 each). The schedule words of each
+// 16-round block are expanded together before its rounds: two independent
+// recurrences (W[t] on W[t-2]) that issue back to back, where interleaving
+// one word per round stalled the in-order issue on each word's latency.
+//
+// Measured on B200 (917,504-byte blocks, digests equal to the
+// producer/consumer kernel's): one warp per sub-partition runs ~46 cycles
+// per round (the producer/consumer pair ~31, but it occupies two
+// sub-partitions per 32 chains), so with 16,384 chains in flight (16
+// concurrent 1024-block launches) this kernel hashes 693 GB/s against 555,
+// and 904 against 667 GB/s at 37,888 chains; at 1024 chains alone the pair
+// is faster (63.5 against 43.8 GB/s), which is why the synchronous put keeps
+// it.
 #pragma once
 
 namespace cb {
@@ -19,25 +27,24 @@ namespace {
 
 constexpr int kFusedWarps = 4;  // warps (of 32 chains) per CTA
 
-// Rounds T0..T0+15 of one chunk; for T0 >= 16 the window w is extended by
-// the message schedule in place. kk: the 16 round constants of this block
-// (shared memory) when T0 >= 16.
-template <int T0>
+// The next 16 schedule words, in place: w[j] = W[t0 + j] from the previous
+// 16 (FIPS 180-4 6.2.2 step 1).
+CB_D void expand16(uint32_t w[16], uint32_t one) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    w[j] = madd(madd(w[j], small_sigma0(w[(j + 1) & 15]), one),
+                madd(w[(j + 9) & 15], small_sigma1(w[(j + 14) & 15]), one), one);
+}
+
+// 16 rounds with the schedule words w[0..15] and round constants k(0..15).
+template <class K>
 CB_D void rounds16(uint32_t &a, uint32_t &b, uint32_t &c, uint32_t &d, uint32_t &e, uint32_t &f, uint32_t &g,
-                   uint32_t &h, uint32_t w[16], const uint32_t *kk, uint32_t one) {
+                   uint32_t &h, const uint32_t w[16], K k, uint32_t one) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
-    uint32_t wt;
-    if (T0 == 0) {
-      wt = w[j];
-    } else {
-      const uint32_t x15 = w[(j + 1) & 15], x2 = w[(j + 14) & 15];
-      wt = madd(madd(w[j], small_sigma0(x15), one), madd(w[(j + 9) & 15], small_sigma1(x2), one), one);
-      w[j] = wt;
-    }
     // T1 = h + K + W + Ch(e,f,g) + Sigma1(e); e' = d + T1;
-    // a' = T1 + Sigma0(a) + Maj(a,b,c): every add on the FMA pipe
-    const uint32_t hkw = madd(madd(wt, T0 == 0 ? kSha256K[j] : kk[j], one), h, one);
+    // a' = T1 + Sigma0(a) + Maj(a,b,c)
+    const uint32_t hkw = madd(madd(w[j], k(j), one), h, one);
     const uint32_t t1 = madd(madd(hkw, sha_ch(e, f, g), one), big_sigma1(e), one);
     const uint32_t t2 = madd(big_sigma0(a), sha_maj(a, b, c), one);
     h = g;
@@ -55,7 +62,7 @@ __global__ void __launch_bounds__(32 * kFusedWarps) sha256_fused_kernel(const Ha
                                                                           uint32_t *__restrict__ digests,
                                                                           unsigned *err, uint32_t one,
                                                                           HashProgress pg) {
-  // round constants for the runtime-indexed 16-round loop (warp-uniform
+  // round constants of the runtime-indexed rounds 16..63 (warp-uniform
   // shared-memory reads are broadcasts)
   __shared__ uint32_t kk[64];
   for (int t = threadIdx.x; t < 64; t += blockDim.x) kk[t] = kSha256K[t];
@@ -116,11 +123,15 @@ __global__ void __launch_bounds__(32 * kFusedWarps) sha256_fused_kernel(const Ha
     }
     uint32_t a = st[0], b = st[1], cc = st[2], d = st[3];
     uint32_t e = st[4], f = st[5], g = st[6], h = st[7];
-    rounds16<0>(a, b, cc, d, e, f, g, h, w, kk, one);
+    rounds16(a, b, cc, d, e, f, g, h, w, [](int j) { return kSha256K[j]; }, one);
     // rounds 16..63: one 16-round body (instruction-cache sized) run three
-    // times, the round constants from shared memory
+    // times, after the expansion of its schedule words
 #pragma unroll 1
-    for (int it = 1; it < 4; ++it) rounds16<16>(a, b, cc, d, e, f, g, h, w, kk + 16 * it, one);
+    for (int it = 1; it < 4; ++it) {
+      expand16(w, one);
+      const uint32_t *kb = kk + 16 * it;
+      rounds16(a, b, cc, d, e, f, g, h, w, [kb](int j) { return kb[j]; }, one);
+    }
     if (c < nchunks) {
       st[0] += a;
       st[1] += b;

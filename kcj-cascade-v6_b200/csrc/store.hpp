@@ -219,7 +219,7 @@ struct Store {
     cudaEvent_t done = nullptr;
     bool pending = false;  // done is recorded and not yet waited for by the host
   };
-  static constexpr int kHashSlots = 16;
+  static constexpr int kHashSlots = 32;
   static constexpr int kScratchSlots = 16;
   HashSlot hslots[kHashSlots];
   int hslot_next = 0;

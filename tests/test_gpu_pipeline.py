@@ -264,3 +264,26 @@ def test_clear_places_then_drops_pipelined_batches():
     assert store.get_stats().total_blocks == 0
     assert all(f.done() for f in fs)
     assert store.batch_put(blocks[:1], return_status=True)[1] == [0]
+
+
+def test_pipelined_ids_match_the_golden_vectors():
+    """The pipelined put hashes with the many-chain kernel: its IDs of every
+    golden vector (FIPS examples, every padding edge 0..129 B, KV pages,
+    1 MB of 'a') equal the reference's, in one launch and spread over
+    launches of different sizes; unaligned sources too."""
+    from helpers import gen
+    vec = load("sha256_vectors.json")["vectors"]
+    blocks = [np.ascontiguousarray(gen(v["gen"], v["seed"], v["size"])) for v in vec]
+    for shift in (0, 3):
+        arrays = [np.concatenate([np.zeros(shift, np.uint8), b]) for b in blocks]
+        buf, ptrs, sizes = dev_blocks(arrays)
+        ptrs = (ptrs + np.uint64(shift)).astype(np.uint64)
+        sizes = (sizes - np.uint64(shift)).astype(np.uint64)
+        for batch in (len(vec), 5):
+            store = make_store(dedup_enabled=False)
+            keys = np.zeros((len(vec), 16), np.uint8)
+            for i in range(0, len(vec), batch):
+                store.put_ptrs_async(ptrs[i:i + batch], sizes[i:i + batch], keys_out=keys[i:i + batch])
+            store.wait_puts()
+            assert [k.tobytes().hex() for k in keys] == [v["block_id"] for v in vec], (shift, batch)
+            store.close()
