@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 METRIC = "aggregate batch_put (incl. SHA256) + batch_get GB/s"
 GB = 1e9
 SHA_TRAFFIC_PER_1024_LAUNCH = 711_190_272  # bytes, ncu capture (see roofline note)
+SHA_ALU_INSTR_PER_CHUNK = 64 * 10 + 48 * 8 + 16  # integer-ALU lane-instructions per 64-byte chunk
 NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool (nominal 900)
 
 
@@ -58,6 +59,10 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="cpu_baseline: repeat passes over the sample until this much put + get time is timed")
     p.add_argument("--copy-engine", type=int, default=0)
+    p.add_argument("--no-profile", action="store_true",
+                   help="no per-launch CUDA events in the store (roofline fields then come out empty)")
+    p.add_argument("--pipeline-blocks", type=int, default=0,
+                   help="pipelined puts: blocks hashing at once (0 = the library default, 32768)")
     p.add_argument("--hash-lanes", type=int, default=32, help="reserved; the SHA-256 kernel runs 32 chains per warp")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -177,7 +182,8 @@ def make_store(args, device_index, capacity, dht=False):
     cfg.copy_engine = args.copy_engine
     cfg.index_log2 = 18 if not dht else 20
     cfg.hash_lanes = args.hash_lanes
-    cfg.profile = True   # per-kernel CUDA-event timing for the roofline fields
+    cfg.pipeline_blocks = args.pipeline_blocks
+    cfg.profile = not getattr(args, "no_profile", False)  # per-kernel CUDA-event timing for the roofline fields
     cfg.dht = dht        # N>1: one hash-sharded store over all ranks
     return cascade_cpp.DistributedStore(cfg)
 
@@ -481,9 +487,20 @@ def main():
     def d(f):
         return getattr(st1, f) - getattr(st0, f)
 
-    sha_s = d("sha_ns") / 1e9
+    # Pipelined puts keep many SHA-256 launches in flight at once (bytes and
+    # launch counts come from the store; the launches overlap, so their
+    # aggregate rate is the bytes hashed over the put phases' CUDA-event time
+    # on this stream - a lower bound, the phases also hold the last
+    # placements)
     sha_bytes_launch = d("sha_bytes") / max(d("sha_launches"), 1)
-    sha_achieved = d("sha_bytes") / sha_s / GB if sha_s else 0.0
+    sha_achieved = d("sha_bytes") / put_t / GB if put_t else 0.0
+    clk_sum = clk.summary()
+    sm_mhz = clk_sum.get("sm_mhz") or 1965.0
+    n_sms = torch.cuda.get_device_properties(device).multi_processor_count
+    # the integer ALU pipe: 16 lanes per cycle per sub-partition (4 per SM);
+    # SHA-256 needs >= 1040 ALU lane-instructions per 64-byte chunk (64 rounds
+    # x 10 rotates/LOP3, 48 schedule words x 8, 16 byte swaps)
+    alu_peak = n_sms * 4 * 16 * sm_mhz * 1e6 * 64 / SHA_ALU_INSTR_PER_CHUNK / GB
     gather_s = d("gather_ns") / 1e9
     gather_alg = 2 * d("gather_bytes")
     gather_achieved = gather_alg / gather_s / GB if gather_s else 0.0
@@ -500,18 +517,22 @@ def main():
         "config": config_dict(args),
         "batch_put_gbs": round(put_gbs, 3), "batch_get_gbs": round(get_gbs, 3),
         "roofline": {
-            "kernel": "sha256_pc_kernel", "bound": "hbm", "achieved": round(sha_achieved, 2),
+            "kernel": "sha256_fused_kernel", "bound": "hbm", "achieved": round(sha_achieved, 2),
             "peak": hbm_peak, "unit": "GB/s", "frac": round(sha_achieved / hbm_peak, 5),
             "peak_source": peak_src,
             # dram__bytes_read.sum + dram__bytes_write.sum of one 1024-block
-            # launch from an ncu capture of this workload (704.9 MB + 6.3 MB;
-            # the 25 % copies are read from L2, not DRAM)
+            # launch from an ncu capture of this workload (the 25 % copies are
+            # read from L2, not DRAM)
             "traffic": SHA_TRAFFIC_PER_1024_LAUNCH if args.batch == 1024 else None,
             "bytes_per_launch": int(sha_bytes_launch),
-            "note": "bytes = block bytes read once per launch; binding limit is the SHA-256 chain latency "
-                    "(one serial chain per block, chains = batch size)",
-            "chain_bound": {"chains_per_launch": args.batch,
-                            "per_chain_MBps": round(sha_achieved * 1e3 / max(args.batch, 1), 2)},
+            "launches": int(d("sha_launches")),
+            "achieved_is": "block bytes hashed / put-phase time (CUDA events on the caller's stream); up to "
+                           f"{args.pipeline_blocks or 32768} blocks hash at once in overlapping launches",
+            "binding": {"pipe": "integer ALU (rotates, shifts, 3-input logic of SHA-256)",
+                        "peak_gbs": round(alu_peak, 1), "frac": round(sha_achieved / alu_peak, 4),
+                        "sm_mhz": sm_mhz, "sms": n_sms,
+                        "peak_is": f"{n_sms} SMs x 4 x 16 lanes/cycle x clock x 64 B / "
+                                   f"{SHA_ALU_INSTR_PER_CHUNK} ALU lane-instructions per chunk"},
         },
         "roofline_get": {
             "kernel": "copy (gather)", "bound": "hbm", "achieved": round(gather_achieved, 2), "peak": hbm_peak,
@@ -531,11 +552,12 @@ def main():
                                    "achieved_per_gpu_min": round(nv_min, 2), "achieved_rank0": round(nv, 2),
                                    "peak": NVLINK_PEER_GBS, "unit": "GB/s",
                                    "frac": round(nv_min / NVLINK_PEER_GBS, 4),
+                                   "frac_of_nominal_900": round(nv_min / 900.0, 4),
                                    "note": "remote bytes received per GPU / gather kernel time (the gather also "
                                            "moves the local 1/W from HBM)",
                                    "remote_fraction": round(remote_b / max(1, get_b), 4)}
         line["config"]["parallelism"] = f"hash-sharded DHT over {world} GPUs (owner = ID mod {world})"
-    line["clocks"] = clk.summary()
+    line["clocks"] = clk_sum
     trace(args, "verification")
     line["verified"] = verify_run(store, ptrs, sizes, keys_ref, dedup_step, out_buf, size, local, world)
 
@@ -700,7 +722,8 @@ def zipf_main(args, rank, world, local, device):
         "roofline": {"kernel": "copy_lsu (peer-load gather)", "bound": "nvlink" if world > 1 else "hbm",
                      "achieved": round(nv_min if world > 1 else 2 * d["gather_bytes"] / gather_s / GB, 2),
                      "peak": NVLINK_PEER_GBS if world > 1 else None, "unit": "GB/s",
-                     "frac": round(nv_min / NVLINK_PEER_GBS, 4) if world > 1 else None},
+                     "frac": round(nv_min / NVLINK_PEER_GBS, 4) if world > 1 else None,
+                     "frac_of_nominal_900": round(nv_min / 900.0, 4) if world > 1 else None},
         "gpu_launches": int(d["kernel_launches"]), "clocks": clk.summary(),
     }
     if rank == 0:
@@ -966,6 +989,9 @@ def config_dict(args):
                         f"byte-identical copies of 64 prefix blocks; step = clear + batch_put all (batch "
                         f"{args.batch}) + batch_get all unique in uniform random order",
             "blocks": args.blocks, "block_bytes": args.block_bytes, "batch": args.batch,
+            "put": "pipelined batch_put (cb_put_batch_async): each batch's SHA-256 launched at submission, up to "
+                   f"{args.pipeline_blocks or 32768} blocks hashing at once, batches placed in submission order",
+            "get": "stream-ordered batch_get (cb_get_batch_async)",
             "l2": "inputs ~60 GB resident in HBM, >> 126 MB L2 (no flush needed)",
             "copy_engine": {0: "tma", 1: "tma", 2: "lsu"}[args.copy_engine]}
 

@@ -83,7 +83,7 @@ typedef struct cb_config {
                                    moves back to HBM: CB_PROMOTE_*          */
   int32_t reserved32;
   uint64_t pipeline_blocks;     /* cb_put_batch_async: blocks whose SHA-256
-                                   may run ahead of placement (0 = 16384)   */
+                                   runs at once (0 = 32768)                 */
 } cb_config;
 
 /* cb_config.promotion_rule. CB_PROMOTE_EVERY_HIT: every DRAM-tier hit of a
@@ -271,7 +271,7 @@ int cb_selftest(cb_store *s, int32_t which);
  * batch is placed: at the latest when cb_put_wait covers its ticket, or when
  * any other data call of the store runs; they must stay valid until then,
  * and the blocks must stay unchanged until then. Up to
- * cb_config.pipeline_blocks blocks hash ahead of placement. CB_MEM_HOST
+ * cb_config.pipeline_blocks blocks hash at once. CB_MEM_HOST
  * blocks are placed before the call returns. On a DHT member every rank
  * must submit the same number of batches (n may be 0) and wait on the same
  * tickets: placement there is collective. */

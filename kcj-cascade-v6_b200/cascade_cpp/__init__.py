@@ -470,6 +470,7 @@ class DistributedConfig:
         self.profile = False          # time every kernel with CUDA events (stats *_ns)
         self.hash_lanes = 32          # reserved (the SHA-256 kernel runs 32 chains per warp)
         self.collective_timeout_ms = 0  # DHT: abort a collective after this long (0 = 600 s)
+        self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 32768)
 
 
 class CascadeConfig:
@@ -499,6 +500,7 @@ class CascadeConfig:
         self.copy_engine = 0
         self.index_log2 = 16
         self.staging_bytes = 1 << 30
+        self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 32768)
 
 
 class _Record:
@@ -861,6 +863,7 @@ class DistributedStore(_StoreBase):
         c.kv_compression = 1 if cfg.kv_compression else 0
         c.prefix_replication = 1 if cfg.prefix_replication else 0
         c.collective_timeout_ms = int(cfg.collective_timeout_ms)
+        c.pipeline_blocks = int(cfg.pipeline_blocks)
         self._init_native(c)
         self._rank, self._world = 0, 1
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -945,6 +948,7 @@ class CascadeStore(_StoreBase):
         c.copy_engine = int(cfg.copy_engine)
         c.staging_bytes = int(cfg.staging_bytes)
         c.kv_compression = 1 if cfg.kv_compression else 0
+        c.pipeline_blocks = int(cfg.pipeline_blocks)
         self._init_native(c)
 
     def get_stats(self) -> CascadeStats:

@@ -11,9 +11,10 @@
 //    kHashSlots side streams (small batches queued back to back share one
 //    launch of up to kLaunchBlocks blocks) and returns a ticket;
 //  * batches are placed - sequential dedup plan, tier moves, scatter into the
-//    pool, index insert - strictly in ticket order, when more than
-//    `pipeline_blocks` blocks are waiting, or when cb_put_wait / any other
-//    data call needs them. Placement in ticket order keeps the sequential dedup rule of
+//    pool, index insert - strictly in ticket order: while more than
+//    `pipeline_blocks` blocks are hashing (the host plans finished batches
+//    while the GPU hashes), when a hash slot is needed again, or when
+//    cb_put_wait / any other data call needs them. Placement in ticket order keeps the sequential dedup rule of
 //    DistributedStore::put_batch (src/distributed_backend.cpp:813-841)
 //    exactly: a block is a dedup hit iff its key was stored before it.
 //
@@ -49,7 +50,7 @@ namespace cb {
 namespace {
 
 constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
-constexpr uint64_t kDefaultPipelineBlocks = 16384;  // blocks hashing ahead of placement (1 GPU)
+constexpr uint64_t kDefaultPipelineBlocks = 32768;  // blocks hashing at once (1 GPU)
 constexpr size_t kDhtPending = 8;                // DHT: batches submitted and not placed (every rank alike)
 constexpr int kScatterLsuCtasPerSm = 4;          // LSU engine (copy_engine = 2): CTAs per SM beside the hashes
 
@@ -84,7 +85,9 @@ void Store::drop_pipeline() {
     h.users = 0;
     h.n = 0;
     h.launched = false;
+    h.finished = false;
   }
+  hashing_blocks = 0;
   for (ScratchSlot &s : sslots) {
     if (s.pending) cudaEventSynchronize(s.done);
     s.pending = false;
@@ -173,17 +176,38 @@ int Store::launch_open_slot() {
   const HashJob *jobs = reinterpret_cast<const HashJob *>(hp);
   for (int i = 0; i < h.n; ++i) bytes += jobs[i].size;
   CB_TRY_CUDA(cudaMemcpyAsync(dp, hp, sizeof(HashJob) * h.n, cudaMemcpyHostToDevice, h.stream), "H2D jobs");
-  CB_TRY_CUDA(timed(0, bytes, h.stream,
-                    [&] {
-                      return launch_sha256_batch(reinterpret_cast<const HashJob *>(dp), h.n,
-                                                 reinterpret_cast<uint32_t *>(dp + o_dig), hash_lanes, d_err,
-                                                 h.stream, nullptr, /*many_chains=*/true);
-                    }),
+  // Not bracketed by timing events even when profiling: timing events around
+  // dozens of concurrent launches on their own streams halved the hashing
+  // throughput on B200. Their bytes and count are kept; a caller times the
+  // hashing as a whole (the put phase) on its own stream.
+  CB_TRY_CUDA(launch_sha256_batch(reinterpret_cast<const HashJob *>(dp), h.n,
+                                  reinterpret_cast<uint32_t *>(dp + o_dig), hash_lanes, d_err, h.stream, nullptr,
+                                  /*many_chains=*/true),
               "sha256 launch");
+  launches++;
+  prof_bytes[0] += bytes;
+  prof_launches[0]++;
   CB_TRY_CUDA(cudaMemcpyAsync(hp + o_dig, dp + o_dig, 32ull * h.n, cudaMemcpyDeviceToHost, h.stream), "D2H digests");
   CB_TRY_CUDA(cudaEventRecord(h.done, h.stream), "event");
   h.launched = true;
+  h.finished = false;
+  hashing_blocks += (uint64_t)h.n;
   return CB_OK;
+}
+
+void Store::refresh_hashing() {
+  for (HashSlot &h : hslots) {
+    if (!h.launched || h.finished) continue;
+    if (cudaEventQuery(h.done) != cudaSuccess) continue;  // not ready (or an error the wait reports)
+    h.finished = true;
+    hashing_blocks -= (uint64_t)h.n;
+  }
+}
+
+bool Store::front_ready() const {
+  if (aput.empty()) return false;
+  const AsyncPut &f = aput.front();
+  return f.slot < 0 || hslots[f.slot].finished;
 }
 
 int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t *is_prefix, const uint8_t *keys_in,
@@ -221,6 +245,7 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
       h.n = 0;
       h.users = 0;
       h.launched = false;
+      h.finished = false;
       open_slot = s;
       hslot_next = (s + 1) % kHashSlots;
     }
@@ -250,13 +275,30 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
     }
     return CB_OK;
   }
-  // Place only as much as keeps `limit` blocks hashing: concurrent launches
-  // tend to finish together, and placing every finished batch at once would
-  // leave the GPU without new launches while the host plans them.
+  // At most `limit` blocks hash at once. Beyond that the host places batches
+  // whose digests are back (host planning and the scatter overlap the
+  // hashes still running) and waits for the oldest launch only when nothing
+  // is ready. Finished batches otherwise stay unplaced until their hash slot
+  // is needed again: concurrent launches of equal blocks finish together,
+  // and launching the next ones must not wait for their placements.
   const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultPipelineBlocks;
-  while (!aput.empty() && inflight_blocks > limit) {
-    rc = place_oldest();
-    if (rc) return rc;
+  for (;;) {
+    refresh_hashing();
+    if (hashing_blocks <= limit) break;
+    if (front_ready()) {
+      rc = place_oldest();
+      if (rc) return rc;
+      continue;
+    }
+    HashSlot *oldest = nullptr;  // the launch of the oldest batch still hashing
+    for (const AsyncPut &b : aput) {
+      if (b.slot >= 0 && hslots[b.slot].launched && !hslots[b.slot].finished) {
+        oldest = &hslots[b.slot];
+        break;
+      }
+    }
+    if (!oldest) break;
+    CB_TRY_CUDA(cudaEventSynchronize(oldest->done), "pipelined hash");
   }
   return CB_OK;
 }
@@ -274,6 +316,10 @@ int Store::place_oldest() {
       if (rc) return rc;
     }
     CB_TRY_CUDA(cudaEventSynchronize(h.done), "pipelined hash");
+    if (!h.finished) {
+      h.finished = true;
+      hashing_blocks -= (uint64_t)h.n;
+    }
     const uint8_t *dig = static_cast<const uint8_t *>(h.h.ptr) + digest_offset(h.cap) + 32ull * b.off;
     for (int i = 0; i < n; ++i) keys[i] = to_hkey(dig + 32ull * i);
   } else {

@@ -203,6 +203,7 @@ struct Store {
     int cap = 0;                 // blocks the slot's buffers hold
     int users = 0;               // batches of the launch not placed yet
     bool launched = false;
+    bool finished = false;       // launched and its digests are back
   };
   struct AsyncPut {
     uint64_t ticket = 0;
@@ -227,6 +228,9 @@ struct Store {
   int open_slot = -1;                // slot collecting batches not launched yet
   uint64_t next_ticket = 1, placed_ticket = 0;
   uint64_t inflight_blocks = 0;      // blocks submitted and not placed
+  uint64_t hashing_blocks = 0;       // blocks of launches whose digests are not back yet
+  void refresh_hashing();            // notes launches that finished (does not wait)
+  bool front_ready() const;          // the oldest batch can be placed without waiting
   cudaStream_t put_stream = nullptr; // placements of pipelined puts
   ScratchSlot sslots[kScratchSlots];
   int sslot_next = 0;
