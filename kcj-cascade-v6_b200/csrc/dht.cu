@@ -28,6 +28,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <numeric>
 #include <climits>
 #include <chrono>
 #include <thread>
@@ -244,6 +245,17 @@ int Store::dht_sync(cudaStream_t st) {
   return CB_OK;
 }
 
+// End of a collective step: the device error word comes back with the
+// stream's last copy, so one bounded wait covers both.
+int Store::dht_finish(cudaStream_t st) {
+  CB_TRY_CUDA(cudaMemcpyAsync(h_err.ptr, d_err, sizeof(unsigned), cudaMemcpyDeviceToHost, st), "D2H err");
+  int rc = dht_sync(st);
+  if (rc) return rc;
+  resolve_prof();
+  if (*static_cast<unsigned *>(h_err.ptr) == 0) return CB_OK;
+  return check_device_error(st);  // reads it again, clears it and reports
+}
+
 // All-gather of the per-destination counts: on return rcount[r] = number of
 // records rank r sends to this rank.
 int Store::dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st) {
@@ -446,7 +458,7 @@ void Store::dht_detach() {
 
 int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
                    const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out, uint8_t *status_out,
-                   cudaStream_t st) {
+                   cudaStream_t st, const uint16_t *step) {
   Trace tr("cb.dht_put");
   if (!dht || !dht->comm) return fail(CB_ERR_STATE, "DHT not attached (or its communicator was aborted after a failure)");
   const int W = dht->W, me = dht->me;
@@ -503,7 +515,8 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   PutReq *sreq = static_cast<PutReq *>(dht->h_send.ptr);
   for (int j = 0; j < n; ++j) {
     const int i = order[j];
-    sreq[j] = PutReq{keys[i].lo, keys[i].hi, sizes[i], (is_prefix && is_prefix[i]) ? 1ull : 0ull};
+    const uint64_t flags = ((is_prefix && is_prefix[i]) ? 1ull : 0ull) | ((step ? (uint64_t)step[i] : 0ull) << 8);
+    sreq[j] = PutReq{keys[i].lo, keys[i].hi, sizes[i], flags};
   }
   CB_TRY_CUDA(cudaMemcpyAsync(dht->d_send.ptr, sreq, sizeof(PutReq) * n, cudaMemcpyHostToDevice, st), "H2D req");
   rc = dht_alltoallv(dht->d_send.ptr, scount.data(), dht->d_recv.ptr, rcount.data(), sizeof(PutReq), st);
@@ -512,20 +525,30 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
               "D2H req");
   rc = dht_sync(st);
   if (rc) return rc;
-  // 4. owner: sequential dedup + placement in (source rank, index) order
+  // 4. owner: sequential dedup + placement in (step, source rank, index)
+  // order. The requests arrive grouped by source rank, each rank's in batch
+  // order; a step tag (bits 8.. of flags) names the batch of a group of
+  // pipelined batches placed together, so a stable sort by step restores the
+  // order of placing those batches one collective step at a time.
   const PutReq *rreq = static_cast<const PutReq *>(dht->h_recv.ptr);
+  std::vector<uint32_t> perm(nrecv);
+  for (uint32_t j = 0; j < nrecv; ++j) perm[j] = j;
+  if (step)
+    std::stable_sort(perm.begin(), perm.end(),
+                     [rreq](uint32_t x, uint32_t y) { return (rreq[x].flags >> 8) < (rreq[y].flags >> 8); });
   std::vector<HKey> okeys(nrecv);
   std::vector<uint64_t> osizes(nrecv);
   std::vector<uint8_t> oprefix(nrecv);
   for (uint32_t j = 0; j < nrecv; ++j) {
-    okeys[j] = HKey{rreq[j].klo, rreq[j].khi};
-    osizes[j] = rreq[j].size;
-    oprefix[j] = (uint8_t)(rreq[j].flags & 1);
+    const PutReq &q = rreq[perm[j]];
+    okeys[j] = HKey{q.klo, q.khi};
+    osizes[j] = q.size;
+    oprefix[j] = (uint8_t)(q.flags & 1);
   }
   rc = reserve_index(nrecv, st);
   if (rc) return rc;
   PutPlan &plan = put_plan;
-  std::vector<uint32_t> ostatus(nrecv);
+  std::vector<uint32_t> ostatus(nrecv);  // in planning order (perm)
   std::vector<uint64_t> oloc(nrecv);
   dht_owner_plan(policy, okeys.data(), osizes.data(), oprefix.data(), nrecv, cfg.dedup_enabled != 0, plan,
                  ostatus.data(), oloc.data());
@@ -535,8 +558,8 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
     policy.commit();
     return rc;
   }
-  std::vector<PutRep> reps(nrecv);
-  for (uint32_t j = 0; j < nrecv; ++j) reps[j] = PutRep{oloc[j], ostatus[j], 0};
+  std::vector<PutRep> reps(nrecv);  // in received order
+  for (uint32_t j = 0; j < nrecv; ++j) reps[perm[j]] = PutRep{oloc[j], ostatus[j], 0};
   // A new block this owner places straight into its DRAM tier (no HBM room
   // even after demotions) is handed over through the outbox: the writer
   // stores it there, the owner moves it to DRAM once the step's writes are
@@ -548,7 +571,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   for (const Placement &p : plan.places) {
     if (p.tier == kTierDram) {
       inbox.emplace_back(&p, ib);
-      reps[p.idx].loc = ib | kLocOutbox;
+      reps[perm[p.idx]].loc = ib | kLocOutbox;
       ib += align_up(p.size, 256);
     }
     ins.push_back(IndexRec{p.key.lo, p.key.hi, oloc[p.idx],
@@ -635,9 +658,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
                 "ncclAllReduce(put barrier)");
   if (rc) return rc;
-  rc = dht_sync(st);
-  if (rc) return rc;
-  rc = check_device_error(st);
+  rc = dht_finish(st);
   if (rc) return rc;
   if (!inbox.empty()) {
     rc = dht_drain_inbox(inbox, st);
@@ -828,9 +849,7 @@ int Store::dht_sync_prefixes(cudaStream_t st) {
   rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
                 "ncclAllReduce(prefix sync barrier)");
   if (rc) return rc;
-  rc = dht_sync(st);
-  if (rc) return rc;
-  return check_device_error(st);
+  return dht_finish(st);
 }
 
 uint64_t Store::dht_registry_size() const { return dht ? dht->registry.size() : 0; }
@@ -1176,9 +1195,7 @@ int Store::dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t
       i = e;
     }
   }
-  rc = dht_sync(st);
-  if (rc) return rc;
-  return check_device_error(st);
+  return dht_finish(st);
 }
 
 int Store::dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st) {

@@ -21,8 +21,9 @@
 // On a DHT member the placement of a batch is the collective DHT put with
 // the digests as keys. Every rank must make the same sequence of calls, so
 // placement there is driven by batch counts alone (never by timing or block
-// counts, which differ between ranks): a batch is placed once kDhtPending
-// later batches were submitted, or at a wait.
+// counts, which differ between ranks): once more than kDhtPending batches
+// are pending the oldest kDhtGroup are placed together in one collective
+// step (owners keep the batch order), and a wait places the rest in groups.
 //
 // cb_get_batch_async serves the common case of a 1-GPU get without a device
 // round trip: when every requested block is in the HBM tier (or missing),
@@ -51,7 +52,8 @@ namespace {
 
 constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
 constexpr uint64_t kDefaultPipelineBlocks = 32768;  // blocks hashing at once (1 GPU)
-constexpr size_t kDhtPending = 8;                // DHT: batches submitted and not placed (every rank alike)
+constexpr size_t kDhtPending = 16;               // DHT: batches submitted and not placed (every rank alike)
+constexpr size_t kDhtGroup = 8;                  // DHT: batches placed together in one collective step
 constexpr int kScatterLsuCtasPerSm = 4;          // LSU engine (copy_engine = 2): CTAs per SM beside the hashes
 
 inline size_t digest_offset(int cap) { return align_up(sizeof(HashJob) * (size_t)cap, 256); }
@@ -268,9 +270,9 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
   *ticket = b.ticket;
   inflight_blocks += (uint64_t)n;
   aput.push_back(std::move(b));
-  if (dht) {
-    while (aput.size() > kDhtPending) {
-      rc = place_oldest();
+  if (dht) {  // counts only: every rank places the same groups at the same call
+    if (aput.size() > kDhtPending) {
+      rc = place_dht_group(kDhtGroup);
       if (rc) return rc;
     }
     return CB_OK;
@@ -303,8 +305,71 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
   return CB_OK;
 }
 
+// DHT member: the `count` oldest batches in one collective put. Their
+// blocks go out as one request batch, each tagged with its batch's position
+// in the group; owners apply them in (batch, source rank, index) order, so
+// statuses and dedup decisions equal those of one collective step per
+// batch, for a fraction of the exchanges and synchronisations.
+int Store::place_dht_group(size_t count) {
+  count = std::min(count, aput.size());
+  size_t total = 0;
+  for (size_t j = 0; j < count; ++j) total += aput[j].sizes.size();
+  std::vector<uint64_t> ptrs, sizes;
+  std::vector<uint8_t> prefix, keys16;
+  std::vector<uint16_t> step;
+  ptrs.reserve(total);
+  sizes.reserve(total);
+  prefix.reserve(total);
+  step.reserve(total);
+  keys16.reserve(16 * total);
+  for (size_t j = 0; j < count; ++j) {
+    AsyncPut &b = aput[j];
+    const size_t n = b.sizes.size();
+    const uint8_t *dig = nullptr;
+    if (b.slot >= 0) {
+      HashSlot &h = hslots[b.slot];
+      if (!h.launched) {
+        const int rc = launch_open_slot();
+        if (rc) return rc;
+      }
+      CB_TRY_CUDA(cudaEventSynchronize(h.done), "pipelined hash");
+      if (!h.finished) {
+        h.finished = true;
+        hashing_blocks -= (uint64_t)h.n;
+      }
+      dig = static_cast<const uint8_t *>(h.h.ptr) + digest_offset(h.cap) + 32ull * b.off;
+    }
+    for (size_t i = 0; i < n; ++i) {
+      ptrs.push_back(b.ptrs[i]);
+      sizes.push_back(b.sizes[i]);
+      prefix.push_back(b.prefix.empty() ? 0 : b.prefix[i]);
+      step.push_back((uint16_t)j);
+      const uint8_t *k = dig ? dig + 32 * i : b.keys_in.data() + 16 * i;
+      keys16.insert(keys16.end(), k, k + 16);
+    }
+  }
+  std::vector<uint8_t> kout(16 * std::max<size_t>(total, 1)), sout(std::max<size_t>(total, 1));
+  const int rc = dht_put(reinterpret_cast<const void *const *>(ptrs.data()), sizes.data(), prefix.data(),
+                         keys16.data(), (int)total, CB_MEM_DEVICE, kout.data(), sout.data(), put_stream, step.data());
+  if (rc) return rc;
+  size_t off = 0;
+  for (size_t j = 0; j < count; ++j) {
+    AsyncPut &b = aput.front();
+    const size_t n = b.sizes.size();
+    if (b.keys_out) memcpy(b.keys_out, kout.data() + 16 * off, 16 * n);
+    if (b.status_out) memcpy(b.status_out, sout.data() + off, n);
+    off += n;
+    if (b.slot >= 0) hslots[b.slot].users--;
+    inflight_blocks -= (uint64_t)n;
+    placed_ticket = b.ticket;
+    aput.pop_front();
+  }
+  return CB_OK;
+}
+
 // Places the oldest submitted batch (waiting for its digests if need be).
 int Store::place_oldest() {
+  if (dht) return place_dht_group(1);
   AsyncPut &b = aput.front();
   const int n = (int)b.sizes.size();
   std::vector<HKey> keys(n);
@@ -325,18 +390,7 @@ int Store::place_oldest() {
   } else {
     for (int i = 0; i < n; ++i) keys[i] = to_hkey(b.keys_in.data() + 16ull * i);
   }
-  if (dht) {
-    std::vector<uint8_t> k16(16ull * n);
-    for (int i = 0; i < n; ++i) {
-      memcpy(k16.data() + 16ull * i, &keys[i].lo, 8);
-      memcpy(k16.data() + 16ull * i + 8, &keys[i].hi, 8);
-    }
-    rc = dht_put(reinterpret_cast<const void *const *>(b.ptrs.data()), b.sizes.data(),
-                 b.prefix.empty() ? nullptr : b.prefix.data(), k16.data(), n, CB_MEM_DEVICE, b.keys_out, b.status_out,
-                 put_stream);
-  } else {
-    rc = n ? place_batch(keys, b) : CB_OK;
-  }
+  rc = n ? place_batch(keys, b) : CB_OK;
   if (rc) return rc;
   if (b.slot >= 0) hslots[b.slot].users--;
   inflight_blocks -= (uint64_t)n;
@@ -385,7 +439,14 @@ int Store::place_batch(const std::vector<HKey> &keys, AsyncPut &b) {
 
 int Store::place_until(uint64_t ticket) {
   while (!aput.empty() && aput.front().ticket <= ticket) {
-    const int rc = place_oldest();
+    int rc;
+    if (dht) {  // groups of up to kDhtGroup batches, the same on every rank
+      size_t cnt = 0;
+      while (cnt < aput.size() && cnt < kDhtGroup && aput[cnt].ticket <= ticket) ++cnt;
+      rc = place_dht_group(cnt);
+    } else {
+      rc = place_oldest();
+    }
     if (rc) return rc;
   }
   return CB_OK;

@@ -220,7 +220,7 @@ struct Store {
     cudaEvent_t done = nullptr;
     bool pending = false;  // done is recorded and not yet waited for by the host
   };
-  static constexpr int kHashSlots = 32;
+  static constexpr int kHashSlots = 64;
   static constexpr int kScratchSlots = 16;
   HashSlot hslots[kHashSlots];
   int hslot_next = 0;
@@ -273,6 +273,7 @@ struct Store {
   int dht_barrier();
   int dht_nccl(int nccl_result, const char *what);
   int dht_sync(cudaStream_t st);
+  int dht_finish(cudaStream_t st);
   int dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st);
   int dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount, size_t rec,
                     cudaStream_t st);
@@ -282,9 +283,12 @@ struct Store {
                  cudaStream_t st, bool stage = true);
   int dht_locate(const uint8_t *key, cb_location *out, int32_t *found);
   void dht_clear_replicas();
+  // step (may be null): per block, the index of its batch within a group of
+  // pipelined batches placed in one collective step (non-decreasing).
   int dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
               const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out,
-              uint8_t *status_out, cudaStream_t st);
+              uint8_t *status_out, cudaStream_t st, const uint16_t *step = nullptr);
+  int place_dht_group(size_t count);
   int dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps, int mem_kind,
               uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
   int dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st);

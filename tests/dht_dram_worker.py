@@ -59,6 +59,7 @@ def main():
         blocks = [torch.from_numpy(pool[s].copy()).to(dev) for s in st[rank]]
         results.append((store.batch_put_async(blocks), blocks))
         tickets.append(ora.put_step([[(ids[s], pool[s].tobytes(), False) for s in st[r]] for r in range(world)]))
+    store.wait_puts()  # the three steps placed as one group (batch order kept by the owners)
     for (fut, _), want in zip(results, tickets):
         got_ids, got_status = fut.result(return_status=True)
         assert got_status == want[rank], ("status", got_status, want[rank])

@@ -153,6 +153,7 @@ def main():
     want2 = [ora2.put_step([[(ids_all[r][16 * j + i], pool[s].tobytes(), pf)
                              for i, (s, pf) in enumerate(items[r][16 * j:16 * (j + 1)])] for r in range(world)])
              for j in range(4)]
+    store.wait_puts()  # all four placed in one grouped collective step
     for j, f in enumerate(futs):
         got_ids, got_st = f.result(return_status=True)
         assert got_ids == ids_all[rank][16 * j:16 * (j + 1)], ("pipelined ids", j)
