@@ -556,10 +556,20 @@ def main():
                                    "note": "remote bytes received per GPU / gather kernel time (the gather also "
                                            "moves the local 1/W from HBM)",
                                    "remote_fraction": round(remote_b / max(1, get_b), 4)}
+        # every DHT collective step (count all-gathers, key/reply
+        # all-to-alls, put barriers), CUDA events on the store's stream: the
+        # time includes waiting for the slowest peer
+        coll_ms = reduce_max(d("coll_ns") / 1e6 / args.steps, world)
+        line["collectives"] = {"calls_per_step": round(d("coll_calls") / args.steps, 1),
+                               "ms_per_step_max_rank": round(coll_ms, 3),
+                               "share_of_step": round(coll_ms / (elapsed_max / args.steps * 1e3), 4),
+                               "bytes_sent_per_step_rank0": int(d("coll_bytes") / args.steps)}
         line["config"]["parallelism"] = f"hash-sharded DHT over {world} GPUs (owner = ID mod {world})"
     line["clocks"] = clk_sum
     trace(args, "verification")
     line["verified"] = verify_run(store, ptrs, sizes, keys_ref, dedup_step, out_buf, size, local, world)
+    line["roofline"]["chain_bound"] = chain_rates(store, ptrs, sizes, size, sm_mhz, n_sms, put_t,
+                                                  d("sha_bytes"))
 
     if not args.no_sweep:
         trace(args, "batch sweep")
@@ -588,6 +598,35 @@ def main():
         torch.distributed.destroy_process_group()
     if not line["verified"]["ok"]:
         sys.exit(3)
+
+
+def chain_rates(store, ptrs, sizes, size, sm_mhz, n_sms, put_t, sha_bytes):
+    """Cycles per SHA-256 round, from CUDA-event times x the median SM clock
+    sampled during the timed region:
+    * one chain: a synchronous 1024-block hashing call on the store (one
+      producer/consumer launch, every chain alone on its two sub-partitions)
+      = launch time x clock / (64-byte chunks per block x 64 rounds);
+    * pipelined put: sub-partition cycles spent per 32-chain round during the
+      timed put phases = put time x clock x sub-partitions / (chunks hashed /
+      32 x 64); the integer ALU pipe needs 32.5 (1040 lane-instructions per
+      chunk at 16 lanes per cycle, per 64 rounds)."""
+    from cascade_cpp import _lib as L
+    nch = (size + 9 + 63) // 64
+    n = min(1024, len(ptrs))
+    st0 = store._n.stats()
+    store._n.hash(np.ascontiguousarray(ptrs[:n]), np.ascontiguousarray(sizes[:n]), L.CB_MEM_DEVICE)
+    st1 = store._n.stats()
+    if st1.sha_launches == st0.sha_launches:  # profiling off
+        return None
+    t_ns = (st1.sha_ns - st0.sha_ns) / (st1.sha_launches - st0.sha_launches)
+    one = t_ns * 1e-9 * sm_mhz * 1e6 / (nch * 64)
+    chunks = sha_bytes / size * nch
+    piped = put_t * sm_mhz * 1e6 * n_sms * 4 / (chunks / 32 * 64) if chunks else None
+    return {"one_chain_cycles_per_round": round(one, 2), "one_chain_design_floor": 20,
+            "one_chain_launch_ms": round(t_ns / 1e6, 3), "one_chain_blocks": n,
+            "pipelined_smsp_cycles_per_warp_round": round(piped, 2) if piped else None,
+            "pipelined_alu_floor": SHA_ALU_INSTR_PER_CHUNK * 2 / 64,
+            "how": "CUDA-event launch times x median SM MHz of the timed region"}
 
 
 def verify_run(store, ptrs, sizes, keys_ref, dedup_step, out_buf, size, local, world, sample=256):

@@ -124,6 +124,11 @@ typedef struct cb_stats {
   /* DHT: prefix blocks of other ranks held in this rank's HBM (replicated by
    * cb_sync_metadata)                                                       */
   uint64_t prefix_replicated_blocks;
+  /* DHT collective steps (cb_config.profile = 1): CUDA-event time on the
+   * store's stream of each count all-gather, key/reply all-to-all and put
+   * barrier (waiting for the slowest peer included), payload bytes this rank
+   * sent in them, and their number                                          */
+  uint64_t coll_ns, coll_bytes, coll_calls;
 } cb_stats;
 
 /* Mirrors BlockLocation (include/cascade_distributed.hpp:62-80). */

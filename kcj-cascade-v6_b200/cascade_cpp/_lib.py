@@ -79,6 +79,7 @@ STATS_FIELDS = [
     "sha_ns", "sha_bytes", "sha_launches", "scatter_ns", "scatter_bytes", "scatter_launches",
     "gather_ns", "gather_bytes", "gather_launches", "tier_ns", "tier_bytes", "tier_launches",
     "peer_bytes_read", "peer_bytes_written", "prefix_replicated_blocks",
+    "coll_ns", "coll_bytes", "coll_calls",
 ]
 
 

@@ -266,7 +266,9 @@ int Store::dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st)
   uint32_t *d = static_cast<uint32_t *>(dht->d_misc.ptr);
   memcpy(h, scount, 4ull * W);
   CB_TRY_CUDA(cudaMemcpyAsync(d, h, 4ull * W, cudaMemcpyHostToDevice, st), "H2D counts");
-  int rc = dht_nccl(ncclAllGather(d, d + W, (size_t)W, ncclUint32, dht->comm, st), "ncclAllGather(counts)");
+  int rc = timed_coll(4ull * W, st, [&] {
+    return dht_nccl(ncclAllGather(d, d + W, (size_t)W, ncclUint32, dht->comm, st), "ncclAllGather(counts)");
+  });
   if (rc) return rc;
   CB_TRY_CUDA(cudaMemcpyAsync(h + W, d + W, 4ull * W * W, cudaMemcpyDeviceToHost, st), "D2H counts");
   rc = dht_sync(st);
@@ -278,6 +280,13 @@ int Store::dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st)
 // Variable all-to-all of fixed-size records (grouped ncclSend/ncclRecv).
 int Store::dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount,
                          size_t rec, cudaStream_t st) {
+  uint64_t sent = 0;
+  for (int r = 0; r < dht->W; ++r) sent += scount[r] * rec;
+  return timed_coll(sent, st, [&] { return dht_alltoallv_group(d_send, scount, d_recv, rcount, rec, st); });
+}
+
+int Store::dht_alltoallv_group(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount,
+                               size_t rec, cudaStream_t st) {
   const int W = dht->W;
   int rc = dht_nccl(ncclGroupStart(), "ncclGroupStart");
   if (rc) return rc;
@@ -655,8 +664,10 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   }
   // 7. closing barrier: every writer's copies precede every later op
   CB_TRY_CUDA(dht->d_misc.ensure(256), "device");
-  rc = dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
-                "ncclAllReduce(put barrier)");
+  rc = timed_coll(4, st, [&] {
+    return dht_nccl(ncclAllReduce(dht->d_misc.ptr, dht->d_misc.ptr, 1, ncclInt32, ncclSum, dht->comm, st),
+                    "ncclAllReduce(put barrier)");
+  });
   if (rc) return rc;
   rc = dht_finish(st);
   if (rc) return rc;

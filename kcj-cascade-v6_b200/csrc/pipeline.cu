@@ -308,8 +308,12 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
 // DHT member: the `count` oldest batches in one collective put. Their
 // blocks go out as one request batch, each tagged with its batch's position
 // in the group; owners apply them in (batch, source rank, index) order, so
-// statuses and dedup decisions equal those of one collective step per
-// batch, for a fraction of the exchanges and synchronisations.
+// dedup decisions and statuses equal those of one collective step per batch,
+// for a fraction of the exchanges and synchronisations. One difference under
+// capacity pressure: the group is one owner plan, and a plan never demotes
+// the blocks it places itself, so a new block that finds no HBM room goes to
+// the owner's DRAM tier (through the outbox) where a per-batch step could
+// have demoted an earlier batch's block of the same group instead.
 int Store::place_dht_group(size_t count) {
   count = std::min(count, aput.size());
   size_t total = 0;

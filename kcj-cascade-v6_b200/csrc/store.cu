@@ -1361,6 +1361,9 @@ void Store::fill_stats(cb_stats *o) const {
     p[3 * k + 1] = prof_bytes[k];
     p[3 * k + 2] = prof_launches[k];
   }
+  o->coll_ns = prof_ns[4];
+  o->coll_bytes = prof_bytes[4];
+  o->coll_calls = prof_launches[4];
 }
 
 uint64_t Store::staging_capacity() const {

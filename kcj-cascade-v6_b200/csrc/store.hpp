@@ -95,13 +95,15 @@ struct Store {
   int rank = 0, world = 1;
   DhtState *dht = nullptr;
 
-  // Kernel accounting. kinds: 0 SHA-256, 1 scatter, 2 gather, 3 tier move.
+  // Kernel accounting. kinds: 0 SHA-256, 1 scatter, 2 gather, 3 tier move,
+  // 4 DHT collective (NCCL; not counted as a kernel launch of this store).
   // With profiling on, every launch is bracketed by two CUDA events on its
   // stream; the pairs are read after the batch's final synchronisation
   // (resolve_prof), so profiling does not serialise streams.
   bool profile = false;
   uint64_t launches = 0;
-  uint64_t prof_ns[4] = {0, 0, 0, 0}, prof_bytes[4] = {0, 0, 0, 0}, prof_launches[4] = {0, 0, 0, 0};
+  static constexpr int kProfKinds = 5;
+  uint64_t prof_ns[kProfKinds] = {}, prof_bytes[kProfKinds] = {}, prof_launches[kProfKinds] = {};
   struct ProfRec {
     int kind;
     uint64_t bytes;
@@ -130,6 +132,24 @@ struct Store {
     e = cudaEventRecord(b, st);
     if (e == cudaSuccess) prof_pending.push_back(ProfRec{kind, bytes, a, b});
     return e;
+  }
+
+  // The same bracketing for a DHT collective step (`call` returns a CB_*
+  // code); `bytes` = payload bytes this rank sends in it.
+  template <class F>
+  int timed_coll(uint64_t bytes, cudaStream_t st, F call) {
+    if (!profile) return call();
+    cudaEvent_t a, b;
+    cudaError_t e = prof_event(a);
+    if (e == cudaSuccess) e = prof_event(b);
+    if (e == cudaSuccess) e = cudaEventRecord(a, st);
+    if (e != cudaSuccess) return cuda_fail(e, "collective timing event");
+    const int rc = call();
+    if (rc) return rc;
+    e = cudaEventRecord(b, st);
+    if (e != cudaSuccess) return cuda_fail(e, "collective timing event");
+    prof_pending.push_back(ProfRec{4, bytes, a, b});
+    return 0;
   }
 
   int fail(int code, const char *fmt, ...);
@@ -277,6 +297,8 @@ struct Store {
   int dht_counts(const uint32_t *scount, uint32_t *rcount, cudaStream_t st);
   int dht_alltoallv(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount, size_t rec,
                     cudaStream_t st);
+  int dht_alltoallv_group(const void *d_send, const uint32_t *scount, void *d_recv, const uint32_t *rcount,
+                          size_t rec, cudaStream_t st);
   // stage: DRAM-tier blocks other ranks ask for go to the outbox (a get);
   // without it the replies only say where each block is (contains).
   int dht_lookup(const uint8_t *keys, int n, std::vector<uint64_t> &reps, std::vector<int> &owner,
