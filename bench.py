@@ -40,7 +40,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "aggregate batch_put (incl. SHA256) + batch_get GB/s"
 GB = 1e9
-SHA_TRAFFIC_PER_1024_LAUNCH = 711_190_272  # bytes, ncu capture (see roofline note)
+SHA_TRAFFIC_PER_1024_LAUNCH = 740_662_528  # bytes, ncu capture of one sha256_fused_kernel launch (roofline note)
 SHA_ALU_INSTR_PER_CHUNK = 64 * 10 + 48 * 8 + 16  # integer-ALU lane-instructions per 64-byte chunk
 NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool (nominal 900)
 
@@ -521,7 +521,8 @@ def main():
             "peak": hbm_peak, "unit": "GB/s", "frac": round(sha_achieved / hbm_peak, 5),
             "peak_source": peak_src,
             # dram__bytes_read.sum + dram__bytes_write.sum of one 1024-block
-            # launch from an ncu capture of this workload (the 25 % copies are
+            # sha256_fused_kernel launch from an ncu capture of this workload
+            # (736.6 MB read + 4.1 MB written; most of the 25 % copies are
             # read from L2, not DRAM)
             "traffic": SHA_TRAFFIC_PER_1024_LAUNCH if args.batch == 1024 else None,
             "bytes_per_launch": int(sha_bytes_launch),

@@ -52,7 +52,7 @@ namespace {
 
 constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
 constexpr uint64_t kDefaultPipelineBlocks = 32768;  // blocks hashing at once (1 GPU)
-constexpr size_t kDhtPending = 16;               // DHT: batches submitted and not placed (every rank alike)
+constexpr size_t kDhtPending = 40;               // DHT: batches submitted and not placed (every rank alike)
 constexpr size_t kDhtGroup = 8;                  // DHT: batches placed together in one collective step
 constexpr int kScatterLsuCtasPerSm = 4;          // LSU engine (copy_engine = 2): CTAs per SM beside the hashes
 
@@ -156,6 +156,12 @@ Store::ScratchSlot *Store::take_scratch(size_t bytes, int &rc) {
     return nullptr;
   }
   return &s;
+}
+
+bool Store::scratch_free() const {
+  const ScratchSlot &s = sslots[sslot_next];
+  // an error is reported by the take_scratch that waits for it
+  return !s.pending || cudaEventQuery(s.done) != cudaErrorNotReady;
 }
 
 int Store::fence_reads(cudaStream_t st) {
@@ -277,21 +283,21 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
     }
     return CB_OK;
   }
-  // At most `limit` blocks hash at once. Beyond that the host places batches
-  // whose digests are back (host planning and the scatter overlap the
-  // hashes still running) and waits for the oldest launch only when nothing
-  // is ready. Finished batches otherwise stay unplaced until their hash slot
-  // is needed again: concurrent launches of equal blocks finish together,
-  // and launching the next ones must not wait for their placements.
+  // Batches whose digests are back are placed (host planning; the scatter
+  // overlaps the hashes still running) as long as their scatter can be
+  // queued without waiting for an earlier one to finish: the scatter runs
+  // at a fraction of HBM speed beside dozens of hash launches, and a host
+  // blocked on it would delay the caller's next submission - the launch of
+  // the next hash. At most `limit` blocks hash at once; beyond that the host
+  // waits for the oldest launch.
   const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultPipelineBlocks;
   for (;;) {
     refresh_hashing();
-    if (hashing_blocks <= limit) break;
-    if (front_ready()) {
+    while (front_ready() && scratch_free()) {
       rc = place_oldest();
       if (rc) return rc;
-      continue;
     }
+    if (hashing_blocks <= limit) break;
     HashSlot *oldest = nullptr;  // the launch of the oldest batch still hashing
     for (const AsyncPut &b : aput) {
       if (b.slot >= 0 && hslots[b.slot].launched && !hslots[b.slot].finished) {

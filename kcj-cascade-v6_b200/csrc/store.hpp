@@ -269,6 +269,8 @@ struct Store {
   int enqueue_places(const PutPlan &plan, const uint64_t *ptrs, cudaStream_t st, PinnedBuf &h, DevBuf &d,
                      int engine, int lsu_ctas_per_sm);
   ScratchSlot *take_scratch(size_t bytes, int &rc);
+  // The next take_scratch would not wait.
+  bool scratch_free() const;
   // Every pool extent a stream-ordered gather may still read is released
   // only after it: work that may write the pool waits for them first.
   int fence_reads(cudaStream_t st);
