@@ -1032,7 +1032,7 @@ def config_dict(args):
             "put": "pipelined batch_put (cb_put_batch_async): each batch's SHA-256 launched at submission, up to "
                    f"{args.pipeline_blocks or 32768} blocks hashing at once, batches placed in submission order",
             "get": "stream-ordered batch_get (cb_get_batch_async)",
-            "l2": "inputs ~60 GB resident in HBM, >> 126 MB L2 (no flush needed)",
+            "l2": "inputs (the distinct blocks, ~45 GB) resident in HBM, >> 126 MB L2 (no flush needed)",
             "copy_engine": {0: "tma", 1: "tma", 2: "lsu"}[args.copy_engine]}
 
 

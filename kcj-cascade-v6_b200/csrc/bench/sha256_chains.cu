@@ -1,16 +1,17 @@
 // Throughput of the two SHA-256 kernels against the number of chains (blocks)
 // in flight: single launches of n blocks, and k concurrent 1024-block
 // launches on their own streams (the pipelined put's launch pattern).
-// Blocks are 917,504 bytes (one Qwen2.5-7B KV block); 4096 distinct blocks
-// (3.76 GB, far larger than L2) are reused round robin beyond that.
+// Blocks are 917,504 bytes (one Qwen2.5-7B KV block); `distinct` source
+// blocks (default 4096 = 3.76 GB, far larger than L2) are reused round robin
+// beyond that.
 //
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Iinclude \
 //        -Ikcj-cascade-v6_b200/csrc -o sha256_chains kcj-cascade-v6_b200/csrc/bench/sha256_chains.cu
-//   ./sha256_chains [max_blocks = 65536]
+//   ./sha256_chains [max_blocks = 65536] [distinct = 4096]
 //
 // Prints whether both kernels give equal digests, then GB/s (block bytes /
-// CUDA-event time) per configuration. Device memory: 3.76 GB of blocks plus
-// 32 B of digest and 16 B of job per block.
+// CUDA-event time) per configuration. Device memory: 917,504 B per distinct
+// block, 32 B of digest and 16 B of job per block.
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -36,12 +37,12 @@ using namespace chains_bench;
 
 int main(int argc, char **argv) {
   const int nmax = argc > 1 ? atoi(argv[1]) : 65536;
-  if (nmax < 2048 || nmax > (1 << 20)) {
-    fprintf(stderr, "max_blocks must be in [2048, 1048576]\n");
+  const int nu = argc > 2 ? atoi(argv[2]) : 4096;  // distinct source blocks
+  if (nmax < 2048 || nmax > (1 << 20) || nu < 1 || nu > 65536) {
+    fprintf(stderr, "max_blocks must be in [2048, 1048576], distinct blocks in [1, 65536]\n");
     return 1;
   }
   const uint64_t S = 917504;
-  const int nu = 4096;  // distinct blocks
   uint8_t *buf = nullptr;
   HashJob *jobs = nullptr;
   uint32_t *dig[2] = {nullptr, nullptr};

@@ -448,6 +448,12 @@ int Store::place_batch(const std::vector<HKey> &keys, AsyncPut &b) {
 }
 
 int Store::place_until(uint64_t ticket) {
+  // batches still queued for a launch start hashing now, beside the ones
+  // whose placements come first
+  if (open_slot >= 0 && !aput.empty() && aput.front().ticket <= ticket) {
+    const int rc = launch_open_slot();
+    if (rc) return rc;
+  }
   while (!aput.empty() && aput.front().ticket <= ticket) {
     int rc;
     if (dht) {  // groups of up to kDhtGroup batches, the same on every rank

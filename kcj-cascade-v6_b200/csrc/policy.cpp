@@ -108,7 +108,7 @@ void Policy::protect(const HKey &k) {
   auto it = map_.find(k);
   if (it == map_.end() || it->second.pending) return;
   it->second.pending = 1;
-  pending_.push_back(k);
+  pending_.push_back(&it->second);
 }
 
 void Policy::clear() {
@@ -225,7 +225,7 @@ bool Policy::demote_one(std::vector<TierMove> &moves, std::vector<HKey> &dropped
   mm.tier = kTierDram;
   mm.off = doff;
   mm.pending = 1;  // moved by this plan: not a DRAM victim inside it
-  pending_.push_back(v);
+  pending_.push_back(&mm);
   return true;
 }
 
@@ -247,7 +247,10 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
   for (int i = 0; i < n; ++i) {
     const HKey &k = keys[i];
     const uint64_t size = sizes[i];
-    if (map_.count(k)) {
+    // one hash lookup: a new key's entry is filled below (it is in no LRU
+    // list yet, so the demotions that make room never see it) or erased
+    const auto ins = map_.try_emplace(k);
+    if (!ins.second) {
       // DistributedStore::put: dedup hit (distributed_backend.cpp:604-608).
       // With dedup disabled the GPU tier still refuses a second copy
       // (gpu_backend.cu:302-304) but nothing is counted.
@@ -281,11 +284,12 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
       }
     }
     if (off == UINT64_MAX) {
+      map_.erase(ins.first);
       plan.status[i] = 2;
       continue;
     }
     if (tier != kTierDram) pack = false;
-    BlockMeta m;
+    BlockMeta &m = ins.first->second;
     m.off = off;
     m.size = pack ? (size & ~1ull) : size;
     m.tier = tier;
@@ -296,8 +300,7 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
     auto &lst = lru_[tier][pf];
     lst.push_front(k);
     m.lru = lst.begin();
-    map_.emplace(k, m);
-    pending_.push_back(k);
+    pending_.push_back(&m);
     if (tier == kTierHbm) {
       hbm_used_ += size;
     } else {
@@ -310,10 +313,7 @@ void Policy::plan_put(const HKey *keys, const uint64_t *sizes, const uint8_t *pr
 }
 
 void Policy::commit() {
-  for (const HKey &k : pending_) {
-    auto it = map_.find(k);
-    if (it != map_.end()) it->second.pending = 0;
-  }
+  for (BlockMeta *m : pending_) m->pending = 0;
   pending_.clear();
   for (const auto &e : deferred_free_) dram_.free(e.first, e.second);
   deferred_free_.clear();
@@ -324,7 +324,7 @@ bool Policy::plan_promote(const HKey &k, std::vector<TierMove> &moves,
   auto it = map_.find(k);
   if (it == map_.end() || it->second.tier != kTierDram) return false;
   it->second.pending = 1;  // protect the source while making room
-  pending_.push_back(k);
+  pending_.push_back(&it->second);
   const uint64_t size = it->second.size;
   if (!make_hbm_room(size, moves, dropped)) return false;
   const uint64_t hoff = hbm_.alloc(size);

@@ -230,7 +230,7 @@ class Policy {
   std::unordered_map<HKey, BlockMeta, HKeyHash> map_;
   // LRU lists, front = most recent: [tier][prefix]
   std::list<HKey> lru_[2][2];
-  std::vector<HKey> pending_;
+  std::vector<BlockMeta *> pending_;  // marked pending until commit (never erased before it)
   std::vector<std::pair<uint64_t, uint64_t>> deferred_free_;  // DRAM extents freed at commit
   uint64_t clock_ = 0;
   uint64_t pinned_ = 0;  // blocks with pins > 0
