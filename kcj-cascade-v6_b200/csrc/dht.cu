@@ -561,7 +561,7 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
   std::vector<uint64_t> oloc(nrecv);
   dht_owner_plan(policy, okeys.data(), osizes.data(), oprefix.data(), nrecv, cfg.dedup_enabled != 0, plan,
                  ostatus.data(), oloc.data());
-  plan_open = true;
+  plan_flag() = true;
   rc = run_moves(plan.moves, plan.dropped, st);
   if (rc) {
     policy.commit();

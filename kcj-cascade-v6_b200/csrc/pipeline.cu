@@ -19,11 +19,15 @@
 //    exactly: a block is a dedup hit iff its key was stored before it.
 //
 // On a DHT member the placement of a batch is the collective DHT put with
-// the digests as keys. Every rank must make the same sequence of calls, so
-// placement there is driven by batch counts alone (never by timing or block
-// counts, which differ between ranks): once more than kDhtPending batches
-// are pending the oldest kDhtGroup are placed together in one collective
-// step (owners keep the batch order), and a wait places the rest in groups.
+// the digests as keys, run by the store's placement thread so that the
+// caller keeps submitting (and the GPU keeps hashing) while a group's
+// exchanges, owner planning and peer stores run. Every rank must make the
+// same sequence of collectives, so batches are assigned to that thread by
+// counts alone (never by timing or block counts, which differ between
+// ranks): once more than kDhtPending batches are unassigned the oldest
+// kDhtGroup go as one group - one collective step, owners keep the batch
+// order - and a wait assigns the rest in groups. How many blocks hash at
+// once is the caller's local business (it waits on its own launches only).
 //
 // cb_get_batch_async serves the common case of a 1-GPU get without a device
 // round trip: when every requested block is in the HBM tier (or missing),
@@ -52,7 +56,7 @@ namespace {
 
 constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
 constexpr uint64_t kDefaultPipelineBlocks = 32768;  // blocks hashing at once (1 GPU)
-constexpr size_t kDhtPending = 40;               // DHT: batches submitted and not placed (every rank alike)
+constexpr size_t kDhtPending = 8;                // DHT: batches submitted and not yet assigned (every rank alike)
 constexpr size_t kDhtGroup = 8;                  // DHT: batches placed together in one collective step
 constexpr int kScatterLsuCtasPerSm = 4;          // LSU engine (copy_engine = 2): CTAs per SM beside the hashes
 
@@ -82,6 +86,7 @@ int Store::pipeline_init() {
 // not placed yet (clear(), destruction).
 void Store::drop_pipeline() {
   if (!pipeline_ready) return;
+  placer_idle();  // assigned groups run (every rank runs them); a failure is already recorded
   for (HashSlot &h : hslots) {
     cudaStreamSynchronize(h.stream);
     h.users = 0;
@@ -104,6 +109,7 @@ void Store::drop_pipeline() {
 
 // Batches still queued are dropped (their outputs are never written).
 void Store::pipeline_release() {
+  placer_join();
   for (HashSlot &h : hslots) {
     if (h.stream) {
       cudaStreamSynchronize(h.stream);
@@ -240,11 +246,17 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
     }
     if (open_slot < 0) {
       const int s = hslot_next;
-      while (hslots[s].users > 0) {  // its batches are the oldest in flight: place them
-        rc = place_oldest();
+      if (dht) {  // its batch is long assigned: wait until the placement thread has placed it
+        rc = dht_slot_free(s);
         if (rc) return rc;
+      } else {
+        while (hslots[s].users > 0) {  // its batches are the oldest in flight: place them
+          rc = place_oldest();
+          if (rc) return rc;
+        }
       }
       HashSlot &h = hslots[s];
+      if (h.launched && !h.finished) hashing_blocks -= (uint64_t)h.n;  // placed, so hashed
       const int cap = std::max(n, kLaunchBlocks);
       const size_t bytes = digest_offset(cap) + 32ull * cap;
       CB_TRY_CUDA(h.h.ensure(bytes), "pinned hash slot");
@@ -276,10 +288,26 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
   *ticket = b.ticket;
   inflight_blocks += (uint64_t)n;
   aput.push_back(std::move(b));
-  if (dht) {  // counts only: every rank places the same groups at the same call
+  if (dht) {
+    // assignment by counts only: every rank assigns the same groups at the
+    // same call
     if (aput.size() > kDhtPending) {
-      rc = place_dht_group(kDhtGroup);
+      rc = assign_dht_group(kDhtGroup);
       if (rc) return rc;
+    }
+    // at most `limit` blocks hash at once: wait for this GPU's own oldest
+    // launch (no collective depends on it)
+    const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultPipelineBlocks;
+    for (;;) {
+      refresh_hashing();
+      if (hashing_blocks <= limit) break;
+      HashSlot *oldest = nullptr;
+      for (int k = 1; k <= kHashSlots && !oldest; ++k) {  // launch order = slot ring order
+        HashSlot &h = hslots[(hslot_next + k - 1) % kHashSlots];
+        if (h.launched && !h.finished) oldest = &h;
+      }
+      if (!oldest) break;
+      CB_TRY_CUDA(cudaEventSynchronize(oldest->done), "pipelined hash");
     }
     return CB_OK;
   }
@@ -311,7 +339,7 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
   return CB_OK;
 }
 
-// DHT member: the `count` oldest batches in one collective put. Their
+// Placement thread: one group of batches in one collective put. Their
 // blocks go out as one request batch, each tagged with its batch's position
 // in the group; owners apply them in (batch, source rank, index) order, so
 // dedup decisions and statuses equal those of one collective step per batch,
@@ -320,10 +348,11 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
 // the blocks it places itself, so a new block that finds no HBM room goes to
 // the owner's DRAM tier (through the outbox) where a per-batch step could
 // have demoted an earlier batch's block of the same group instead.
-int Store::place_dht_group(size_t count) {
-  count = std::min(count, aput.size());
+// The thread only reads the batches' hash slots (their digests and events);
+// the caller's fields of those slots are left to the caller.
+int Store::place_dht_batches(std::vector<AsyncPut> &g) {
   size_t total = 0;
-  for (size_t j = 0; j < count; ++j) total += aput[j].sizes.size();
+  for (const AsyncPut &b : g) total += b.sizes.size();
   std::vector<uint64_t> ptrs, sizes;
   std::vector<uint8_t> prefix, keys16;
   std::vector<uint16_t> step;
@@ -332,21 +361,13 @@ int Store::place_dht_group(size_t count) {
   prefix.reserve(total);
   step.reserve(total);
   keys16.reserve(16 * total);
-  for (size_t j = 0; j < count; ++j) {
-    AsyncPut &b = aput[j];
+  for (size_t j = 0; j < g.size(); ++j) {
+    AsyncPut &b = g[j];
     const size_t n = b.sizes.size();
     const uint8_t *dig = nullptr;
     if (b.slot >= 0) {
       HashSlot &h = hslots[b.slot];
-      if (!h.launched) {
-        const int rc = launch_open_slot();
-        if (rc) return rc;
-      }
       CB_TRY_CUDA(cudaEventSynchronize(h.done), "pipelined hash");
-      if (!h.finished) {
-        h.finished = true;
-        hashing_blocks -= (uint64_t)h.n;
-      }
       dig = static_cast<const uint8_t *>(h.h.ptr) + digest_offset(h.cap) + 32ull * b.off;
     }
     for (size_t i = 0; i < n; ++i) {
@@ -363,23 +384,128 @@ int Store::place_dht_group(size_t count) {
                          keys16.data(), (int)total, CB_MEM_DEVICE, kout.data(), sout.data(), put_stream, step.data());
   if (rc) return rc;
   size_t off = 0;
-  for (size_t j = 0; j < count; ++j) {
-    AsyncPut &b = aput.front();
+  for (AsyncPut &b : g) {
     const size_t n = b.sizes.size();
     if (b.keys_out) memcpy(b.keys_out, kout.data() + 16 * off, 16 * n);
     if (b.status_out) memcpy(b.status_out, sout.data() + off, n);
     off += n;
-    if (b.slot >= 0) hslots[b.slot].users--;
-    inflight_blocks -= (uint64_t)n;
-    placed_ticket = b.ticket;
-    aput.pop_front();
   }
   return CB_OK;
 }
 
+// Caller: the `count` oldest unassigned batches go to the placement thread
+// as one group (started on first use).
+int Store::assign_dht_group(size_t count) {
+  count = std::min(count, aput.size());
+  if (!count) return CB_OK;
+  std::vector<AsyncPut> g;
+  g.reserve(count);
+  for (size_t j = 0; j < count; ++j) {
+    inflight_blocks -= (uint64_t)aput.front().sizes.size();
+    g.push_back(std::move(aput.front()));
+    aput.pop_front();
+  }
+  std::lock_guard<std::mutex> lk(pmu);
+  if (!placer.joinable()) {
+    placer_stop = false;
+    placer = std::thread([this] { placer_loop(); });
+    placer_id = placer.get_id();  // set under pmu, which the thread takes before any work
+  }
+  pgroups.push_back(std::move(g));
+  pcv.notify_all();
+  return CB_OK;
+}
+
+void Store::placer_loop() {
+  std::unique_lock<std::mutex> lk(pmu);
+  cudaSetDevice(device);
+  for (;;) {
+    pcv.wait(lk, [&] { return placer_stop || !pgroups.empty(); });
+    if (pgroups.empty()) return;  // asked to stop with nothing left
+    std::vector<AsyncPut> g = std::move(pgroups.front());
+    pgroups.pop_front();
+    placer_busy = true;
+    const bool skip = placer_rc != 0;  // after a failure nothing more is placed
+    lk.unlock();
+    int rc = CB_OK;
+    if (!skip) {
+      try {
+        rc = place_dht_batches(g);
+      } catch (const std::bad_alloc &) {
+        rc = fail(CB_ERR_NOSPACE, "host allocation failed");
+      } catch (const std::exception &ex) {
+        rc = fail(CB_ERR_STATE, "%s", ex.what());
+      }
+    }
+    const std::string err = rc ? last_error_copy() : std::string();
+    lk.lock();
+    for (AsyncPut &b : g)
+      if (b.slot >= 0) hslots[b.slot].users--;
+    if (rc) {
+      placer_rc = rc;
+      placer_err = err;
+    } else if (!skip && !g.empty()) {
+      placed_ticket = g.back().ticket;
+    }
+    placer_busy = false;
+    pcv.notify_all();
+  }
+}
+
+// Caller: waits until every assigned group is placed. A failure of the
+// placement thread is returned once; the store's state is then lost (its
+// metadata may be ahead of its memory and its peers') until clear().
+int Store::placer_idle() {
+  std::unique_lock<std::mutex> lk(pmu);
+  if (!placer.joinable()) return CB_OK;
+  pcv.wait(lk, [&] { return pgroups.empty() && !placer_busy; });
+  if (!placer_rc) return CB_OK;
+  const int rc = placer_rc;
+  placer_rc = 0;
+  if (lost.empty()) lost = placer_err;
+  {
+    std::lock_guard<std::mutex> g(err_mu);
+    last_error = placer_err;
+  }
+  return rc;
+}
+
+// Caller: hash slot s may be reused once the thread has placed its batch.
+int Store::dht_slot_free(int s) {
+  for (;;) {
+    bool assigned = true;
+    for (const AsyncPut &b : aput) assigned &= b.slot != s;
+    if (assigned) break;
+    const int rc = assign_dht_group(kDhtGroup);
+    if (rc) return rc;
+  }
+  std::unique_lock<std::mutex> lk(pmu);
+  pcv.wait(lk, [&] { return hslots[s].users == 0 || placer_rc != 0; });
+  if (!placer_rc) return CB_OK;
+  lk.unlock();
+  return placer_idle();
+}
+
+void Store::placer_join() {
+  {
+    std::lock_guard<std::mutex> lk(pmu);
+    if (!placer.joinable()) return;
+    placer_stop = true;
+    pcv.notify_all();
+  }
+  placer.join();  // runs what is assigned first
+  std::lock_guard<std::mutex> lk(pmu);
+  placer = std::thread();
+  placer_id = std::thread::id();
+  placer_rc = 0;
+}
+
 // Places the oldest submitted batch (waiting for its digests if need be).
 int Store::place_oldest() {
-  if (dht) return place_dht_group(1);
+  if (dht) {
+    const int rc = assign_dht_group(1);
+    return rc ? rc : placer_idle();
+  }
   AsyncPut &b = aput.front();
   const int n = (int)b.sizes.size();
   std::vector<HKey> keys(n);
@@ -459,13 +585,13 @@ int Store::place_until(uint64_t ticket) {
     if (dht) {  // groups of up to kDhtGroup batches, the same on every rank
       size_t cnt = 0;
       while (cnt < aput.size() && cnt < kDhtGroup && aput[cnt].ticket <= ticket) ++cnt;
-      rc = place_dht_group(cnt);
+      rc = assign_dht_group(cnt);
     } else {
       rc = place_oldest();
     }
     if (rc) return rc;
   }
-  return CB_OK;
+  return dht ? placer_idle() : CB_OK;
 }
 
 // Device work of the placements made so far is complete; a device-side

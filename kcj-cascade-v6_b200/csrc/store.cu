@@ -125,6 +125,7 @@ int Store::fail(int code, const char *fmt, ...) {
   va_start(ap, fmt);
   vsnprintf(buf, sizeof buf, fmt, ap);
   va_end(ap);
+  std::lock_guard<std::mutex> g(err_mu);
   last_error = buf;
   return code;
 }
@@ -1285,7 +1286,7 @@ int Store::evict(uint64_t bytes, uint64_t *evicted, cudaStream_t st) {
   std::vector<TierMove> moves;
   std::vector<HKey> dropped;
   const uint64_t freed = policy.plan_evict(bytes, moves, dropped);
-  plan_open |= !moves.empty() || !dropped.empty();
+  plan_flag() |= !moves.empty() || !dropped.empty();
   int rc = run_moves(moves, dropped, st);
   policy.commit();
   if (rc) return rc;
@@ -1394,14 +1395,21 @@ cudaStream_t pick_stream(Store *s, void *stream) {
 // settle. kAny calls (statistics, barriers, syncs) run in that state and
 // settle; kFree calls (hashing, KV compression, view releases, clear, which
 // settles by itself) neither.
-enum Access { kData, kAsync, kAny, kFree };
+// kSubmit: a pipelined put's submission - the one call that runs beside a
+// DHT member's placement thread; every other call first waits until that
+// thread is idle.
+enum Access { kData, kAsync, kAny, kFree, kSubmit };
 
 template <class F>
 int guarded(cb_store *h, F f, Access access = kData) {
   if (!h || !h->s) return CB_ERR_ARG;
   Store *s = h->s;
   std::lock_guard<std::mutex> g(s->mu);
-  if ((access == kData || access == kAsync) && !s->lost.empty())
+  if (access != kSubmit) {
+    const int prc = s->placer_idle();  // a failure of the placement thread is this call's error
+    if (prc) return prc;
+  }
+  if ((access == kData || access == kAsync || access == kSubmit) && !s->lost.empty())
     return s->fail(CB_ERR_STATE, "store state lost after a failed call (%s); clear() resets it", s->lost.c_str());
   s->plan_open = false;
   int rc;
@@ -1418,7 +1426,7 @@ int guarded(cb_store *h, F f, Access access = kData) {
   } catch (const std::exception &ex) {
     rc = s->fail(CB_ERR_STATE, "%s", ex.what());
   }
-  if (rc != CB_OK && s->plan_open && s->lost.empty()) s->lost = s->last_error;
+  if (rc != CB_OK && s->plan_open && s->lost.empty()) s->lost = s->last_error_copy();
   s->plan_open = false;
   return rc;
 }
@@ -1455,7 +1463,7 @@ int cb_create(const cb_config *cfg, cb_store **out) {
   s->copy_engine = cfg->copy_engine == 2 ? 2 : 1;
   int rc = s->init();
   if (rc) {
-    cb::g_create_error = s->last_error;
+    cb::g_create_error = s->last_error_copy();
     delete s;
     return rc;
   }
@@ -1477,7 +1485,7 @@ const char *cb_last_error(const cb_store *h) {
   static thread_local std::string copy;
   if (!h || !h->s) return cb::g_create_error.c_str();
   std::lock_guard<std::mutex> g(h->s->mu);
-  copy = h->s->last_error;
+  copy = h->s->last_error_copy();
   return copy.c_str();
 }
 
@@ -1507,13 +1515,16 @@ int cb_put_batch_async(cb_store *h, const void *const *ptrs, const uint64_t *siz
     std::vector<uint64_t> p(n);
     for (int i = 0; i < n; ++i) p[i] = (uint64_t)ptrs[i];
     return s->put_async(p.data(), sizes, is_prefix, keys_in, n, keys_out, status_out, ticket_out, st);
-  }, kAsync);
+  }, kSubmit);
 }
 
 int cb_put_wait(cb_store *h, uint64_t ticket, uint64_t *placed_out) {
   return guarded(h, [&](Store *s) -> int {
     const int rc = s->put_wait(ticket ? ticket : UINT64_MAX);
-    if (placed_out) *placed_out = s->placed_ticket;
+    if (placed_out) {
+      std::lock_guard<std::mutex> g(s->pmu);
+      *placed_out = s->placed_ticket;
+    }
     return rc;
   }, kAsync);
 }
@@ -1521,6 +1532,7 @@ int cb_put_wait(cb_store *h, uint64_t ticket, uint64_t *placed_out) {
 int cb_put_placed(cb_store *h, uint64_t *placed_out) {
   if (!h || !h->s || !placed_out) return CB_ERR_ARG;
   std::lock_guard<std::mutex> g(h->s->mu);
+  std::lock_guard<std::mutex> g2(h->s->pmu);  // the placement thread advances it
   *placed_out = h->s->placed_ticket;
   return CB_OK;
 }

@@ -3,10 +3,13 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <condition_variable>
 #include <deque>
 #include <functional>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include <nvtx3/nvToolsExt.h>
@@ -78,12 +81,19 @@ struct Store {
   Policy policy;
   PutPlan put_plan;
   std::mutex mu;
+  std::mutex err_mu;  // last_error: also written by the placement thread
   std::string last_error;
+  std::string last_error_copy() {
+    std::lock_guard<std::mutex> g(err_mu);
+    return last_error;
+  }
   // The host metadata records a batch's placements and tier moves when the
   // batch is planned. A call that fails after planning (plan_open still set
   // when it returns) may leave metadata that its memory does not match, so
   // the store refuses data calls (`lost` holds the first error) until clear().
   bool plan_open = false;
+  bool placer_plan_open = false;  // the placement thread's own flag (its failures always lose the state)
+  bool &plan_flag() { return std::this_thread::get_id() == placer_id ? placer_plan_open : plan_open; }
   std::string lost;
   int fake_move_failures = 0;  // CB_SELFTEST_FAIL_MOVES: host-side injection
 
@@ -101,7 +111,7 @@ struct Store {
   // stream; the pairs are read after the batch's final synchronisation
   // (resolve_prof), so profiling does not serialise streams.
   bool profile = false;
-  uint64_t launches = 0;
+  std::atomic<uint64_t> launches{0};
   static constexpr int kProfKinds = 5;
   uint64_t prof_ns[kProfKinds] = {}, prof_bytes[kProfKinds] = {}, prof_launches[kProfKinds] = {};
   struct ProfRec {
@@ -244,7 +254,26 @@ struct Store {
   static constexpr int kScratchSlots = 16;
   HashSlot hslots[kHashSlots];
   int hslot_next = 0;
-  std::deque<AsyncPut> aput;         // submitted, not placed (submission order)
+  std::deque<AsyncPut> aput;         // submitted, not placed (submission order); DHT: not yet assigned
+  // DHT member: groups of pipelined batches are placed (collective DHT put)
+  // by a placement thread of the store, in assignment order, while the
+  // caller keeps submitting and the GPU keeps hashing. Assignment is
+  // count-based, the same on every rank, so every rank's thread runs the
+  // same sequence of collectives. Every other call that needs the store's
+  // state or its communicator first waits until the thread is idle.
+  std::thread placer;
+  std::thread::id placer_id;
+  std::mutex pmu;                    // guards the fields below and hslots[].users of a DHT member
+  std::condition_variable pcv;
+  std::deque<std::vector<AsyncPut>> pgroups;  // assigned, not placed (oldest first)
+  bool placer_busy = false, placer_stop = false;
+  int placer_rc = 0;                 // first failure of the thread (the state is then lost)
+  std::string placer_err;
+  int assign_dht_group(size_t count);  // caller: the `count` oldest unassigned batches to the thread
+  int placer_idle();                 // caller: waits until nothing is assigned; reports a failure
+  void placer_loop();
+  void placer_join();
+  int place_dht_batches(std::vector<AsyncPut> &g);  // placement thread
   int open_slot = -1;                // slot collecting batches not launched yet
   uint64_t next_ticket = 1, placed_ticket = 0;
   uint64_t inflight_blocks = 0;      // blocks submitted and not placed
@@ -312,7 +341,7 @@ struct Store {
   int dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t *is_prefix,
               const uint8_t *keys_in, int n, int mem_kind, uint8_t *keys_out,
               uint8_t *status_out, cudaStream_t st, const uint16_t *step = nullptr);
-  int place_dht_group(size_t count);
+  int dht_slot_free(int s);  // caller: waits until hash slot s is placed
   int dht_get(const uint8_t *keys, int n, void *const *outs, const uint64_t *caps, int mem_kind,
               uint64_t *sizes_out, uint8_t *found_out, cudaStream_t st);
   int dht_contains(const uint8_t *keys, int n, uint8_t *found_out, cudaStream_t st);
