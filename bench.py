@@ -48,7 +48,7 @@ NVLINK_PEER_GBS = 770.0  # measured peer copy per direction per GPU on this pool
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--steps", type=int, default=8)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="b200", choices=["b200", "reference"])
     p.add_argument("--blocks", type=int, default=65536)
@@ -105,7 +105,7 @@ class ClockSampler:
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                      "--format=csv,noheader,nounits", "-lms", "200"],
+                                      "--format=csv,noheader,nounits", "-lms", "50"],
                                      stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         time.sleep(0.3)
         return self
@@ -135,7 +135,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
         return {"sm_mhz": float(np.median([r[0] for r in rows])), "sm_max_mhz": rows[0][1],
-                "samples": len(rows), "reasons": reasons}
+                "sm_mhz_min": float(min(r[0] for r in rows)), "samples": len(rows), "reasons": reasons}
 
 
 # --------------------------------------------------------------- workload
