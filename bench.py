@@ -59,6 +59,9 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="cpu_baseline: repeat passes over the sample until this much put + get time is timed")
     p.add_argument("--copy-engine", type=int, default=0)
+    p.add_argument("--hash-sms", type=int, default=0,
+                   help="SMs the pipelined puts' SHA-256 may occupy (0 = the library default: all on one GPU, "
+                        "all but 8 on a DHT member)")
     p.add_argument("--no-profile", action="store_true",
                    help="no per-launch CUDA events in the store (roofline fields then come out empty)")
     p.add_argument("--pipeline-blocks", type=int, default=0,
@@ -183,6 +186,7 @@ def make_store(args, device_index, capacity, dht=False):
     cfg.index_log2 = 18 if not dht else 20
     cfg.hash_lanes = args.hash_lanes
     cfg.pipeline_blocks = args.pipeline_blocks
+    cfg.hash_sms = args.hash_sms
     cfg.profile = not getattr(args, "no_profile", False)  # per-kernel CUDA-event timing for the roofline fields
     cfg.dht = dht        # N>1: one hash-sharded store over all ranks
     return cascade_cpp.DistributedStore(cfg)
@@ -1031,6 +1035,7 @@ def config_dict(args):
             "blocks": args.blocks, "block_bytes": args.block_bytes, "batch": args.batch,
             "put": "pipelined batch_put (cb_put_batch_async): each batch's SHA-256 launched at submission, up to "
                    f"{args.pipeline_blocks or 32768} blocks hashing at once, batches placed in submission order",
+            "hash_sms": args.hash_sms or "library default (all SMs on one GPU; all but 8 on a DHT member)",
             "get": "stream-ordered batch_get (cb_get_batch_async)",
             "l2": "inputs (the distinct blocks, ~45 GB) resident in HBM, >> 126 MB L2 (no flush needed)",
             "copy_engine": {0: "tma", 1: "tma", 2: "lsu"}[args.copy_engine]}

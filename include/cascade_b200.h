@@ -84,6 +84,11 @@ typedef struct cb_config {
   int32_t reserved32;
   uint64_t pipeline_blocks;     /* cb_put_batch_async: blocks whose SHA-256
                                    runs at once (0 = 32768)                 */
+  int32_t hash_sms;             /* SMs the pipelined puts' SHA-256 launches
+                                   may occupy (a green context; the rest stay
+                                   free for collectives and copies): 0 = all
+                                   on one GPU, all but 8 on a DHT member    */
+  int32_t reserved32b;
 } cb_config;
 
 /* cb_config.promotion_rule. CB_PROMOTE_EVERY_HIT: every DRAM-tier hit of a

@@ -471,6 +471,7 @@ class DistributedConfig:
         self.hash_lanes = 32          # reserved (the SHA-256 kernel runs 32 chains per warp)
         self.collective_timeout_ms = 0  # DHT: abort a collective after this long (0 = 600 s)
         self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 32768)
+        self.hash_sms = 0             # pipelined puts: SMs their SHA-256 may use (0 = all; DHT: all but 8)
 
 
 class CascadeConfig:
@@ -501,6 +502,7 @@ class CascadeConfig:
         self.index_log2 = 16
         self.staging_bytes = 1 << 30
         self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 32768)
+        self.hash_sms = 0             # pipelined puts: SMs their SHA-256 may use (0 = all; DHT: all but 8)
 
 
 class _Record:
@@ -864,6 +866,7 @@ class DistributedStore(_StoreBase):
         c.prefix_replication = 1 if cfg.prefix_replication else 0
         c.collective_timeout_ms = int(cfg.collective_timeout_ms)
         c.pipeline_blocks = int(cfg.pipeline_blocks)
+        c.hash_sms = int(getattr(cfg, "hash_sms", 0))
         self._init_native(c)
         self._rank, self._world = 0, 1
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -949,6 +952,7 @@ class CascadeStore(_StoreBase):
         c.staging_bytes = int(cfg.staging_bytes)
         c.kv_compression = 1 if cfg.kv_compression else 0
         c.pipeline_blocks = int(cfg.pipeline_blocks)
+        c.hash_sms = int(getattr(cfg, "hash_sms", 0))
         self._init_native(c)
 
     def get_stats(self) -> CascadeStats:

@@ -66,6 +66,8 @@ class cb_config(C.Structure):
         ("promotion_rule", C.c_int32),
         ("reserved32", C.c_int32),
         ("pipeline_blocks", C.c_uint64),
+        ("hash_sms", C.c_int32),
+        ("reserved32b", C.c_int32),
     ]
 
 

@@ -43,6 +43,7 @@
 // settles (cb_put_wait, cb_sync, and every synchronous data call): that call
 // returns the error. A failed placement leaves the host metadata ahead of
 // the pool, so the store then refuses data calls until cb_clear.
+#include <cuda.h>  // green-context types; the functions come from cudaGetDriverEntryPoint
 #include <string.h>
 
 #include <algorithm>
@@ -64,10 +65,76 @@ inline size_t digest_offset(int cap) { return align_up(sizeof(HashJob) * (size_t
 
 }  // namespace
 
+namespace {
+
+constexpr int kDhtSpareSms = 8;  // DHT member: SMs kept free of hash launches by default
+
+template <class F>
+F driver_fn(const char *name) {
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &fn, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return reinterpret_cast<F>(fn);
+}
+
+}  // namespace
+
+// A green context of at least `sms` SMs for the hash streams. Returns CB_OK
+// with green == null when the driver offers no such partition (the hash
+// streams then use every SM).
+int Store::make_hash_green_context(int sms) {
+  using GetDev = CUresult (*)(CUdevice *, int);
+  using GetRes = CUresult (*)(CUdevice, CUdevResource *, CUdevResourceType);
+  using Split = CUresult (*)(CUdevResource *, unsigned *, const CUdevResource *, CUdevResource *, unsigned, unsigned);
+  using Desc = CUresult (*)(CUdevResourceDesc *, CUdevResource *, unsigned);
+  using Create = CUresult (*)(CUgreenCtx *, CUdevResourceDesc, CUdevice, unsigned);
+  auto get_dev = driver_fn<GetDev>("cuDeviceGet");
+  auto get_res = driver_fn<GetRes>("cuDeviceGetDevResource");
+  auto split = driver_fn<Split>("cuDevSmResourceSplitByCount");
+  auto desc_fn = driver_fn<Desc>("cuDevResourceGenerateDesc");
+  auto create = driver_fn<Create>("cuGreenCtxCreate");
+  if (!get_dev || !get_res || !split || !desc_fn || !create) return CB_OK;
+  CUdevice dev;
+  CUdevResource all{}, part{}, rest{};
+  unsigned nb = 1;
+  CUdevResourceDesc desc;
+  CUgreenCtx g = nullptr;
+  if (get_dev(&dev, device) != CUDA_SUCCESS || get_res(dev, &all, CU_DEV_RESOURCE_TYPE_SM) != CUDA_SUCCESS ||
+      split(&part, &nb, &all, &rest, 0, (unsigned)sms) != CUDA_SUCCESS || nb < 1 ||
+      desc_fn(&desc, &part, 1) != CUDA_SUCCESS || create(&g, desc, dev, CU_GREEN_CTX_DEFAULT_STREAM) != CUDA_SUCCESS)
+    return CB_OK;
+  green = g;
+  hash_sm_count = (int)part.sm.smCount;
+  return CB_OK;
+}
+
+cudaError_t Store::create_hash_stream(cudaStream_t &s) {
+  if (green) {
+    using StreamCreate = CUresult (*)(CUstream *, CUgreenCtx, unsigned, int);
+    auto fn = driver_fn<StreamCreate>("cuGreenCtxStreamCreate");
+    CUstream cs = nullptr;
+    if (fn && fn(&cs, static_cast<CUgreenCtx>(green), CU_STREAM_NON_BLOCKING, 0) == CUDA_SUCCESS) {
+      s = reinterpret_cast<cudaStream_t>(cs);
+      return cudaSuccess;
+    }
+    return cudaErrorInvalidResourceHandle;
+  }
+  return cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+}
+
 int Store::pipeline_init() {
   if (pipeline_ready) return CB_OK;
+  if (!hash_sm_count) {
+    hash_sm_count = num_sms;
+    const int want = cfg.hash_sms > 0 ? cfg.hash_sms : (dht ? num_sms - kDhtSpareSms : 0);
+    if (want > 0 && want < num_sms) {
+      const int rc = make_hash_green_context(want);
+      if (rc) return rc;
+    }
+  }
   for (HashSlot &h : hslots) {
-    if (!h.stream) CB_TRY_CUDA(cudaStreamCreateWithFlags(&h.stream, cudaStreamNonBlocking), "hash stream");
+    if (!h.stream) CB_TRY_CUDA(create_hash_stream(h.stream), "hash stream");
     if (!h.done) CB_TRY_CUDA(cudaEventCreateWithFlags(&h.done, cudaEventDisableTiming), "event");
   }
   for (ScratchSlot &s : sslots)
@@ -136,6 +203,12 @@ void Store::pipeline_release() {
   }
   if (ev_submit) cudaEventDestroy(ev_submit);
   ev_submit = nullptr;
+  if (green) {  // after its streams
+    using Destroy = CUresult (*)(CUgreenCtx);
+    if (auto fn = driver_fn<Destroy>("cuGreenCtxDestroy")) fn(static_cast<CUgreenCtx>(green));
+    green = nullptr;
+  }
+  hash_sm_count = 0;
   if (d_err_get) cudaFree(d_err_get);
   d_err_get = nullptr;
   aput.clear();

@@ -281,6 +281,13 @@ struct Store {
   void refresh_hashing();            // notes launches that finished (does not wait)
   bool front_ready() const;          // the oldest batch can be placed without waiting
   cudaStream_t put_stream = nullptr; // placements of pipelined puts
+  // Hash streams may live in a green context holding part of the SMs, so
+  // that collectives and copies always find free SMs beside a GPU full of
+  // hash CTAs (cb_config.hash_sms). hash_sm_count = SMs they may use.
+  void *green = nullptr;             // CUgreenCtx, or null: ordinary streams on every SM
+  int hash_sm_count = 0;
+  int make_hash_green_context(int sms);
+  cudaError_t create_hash_stream(cudaStream_t &s);
   ScratchSlot sslots[kScratchSlots];
   int sslot_next = 0;
   bool pipeline_ready = false;

@@ -287,3 +287,34 @@ def test_pipelined_ids_match_the_golden_vectors():
             store.wait_puts()
             assert [k.tobytes().hex() for k in keys] == [v["block_id"] for v in vec], (shift, batch)
             store.close()
+
+
+def test_hash_launches_confined_to_part_of_the_sms():
+    """cb_config.hash_sms: the pipelined puts' SHA-256 launches run on hash
+    streams of a green context holding part of the SMs (the rest stay free
+    for collectives and copies). IDs, statuses, dedup counts and every byte
+    read back equal the reference scenario's."""
+    sc = next(s for s in load("store_scenarios.json")["scenarios"] if s["name"] == "mix_qwen7b_128")
+    src, is_prefix = W.dedup_mix(sc["n_blocks"], sc["n_prefix"], sc["dup_frac"], sc["mix_seed"])
+    uniq = {int(s): W.kv_block_fp16(sc["block_seed_base"] + int(s), sc["size"]) for s in np.unique(src)}
+    buf, ptrs, sizes = dev_blocks([uniq[int(s)] for s in src])
+    store = make_store(hash_sms=64)
+    n = len(src)
+    keys = np.zeros((n, 16), np.uint8)
+    status = np.full(n, 9, np.uint8)
+    prefix = is_prefix.astype(np.uint8)
+    for i in range(0, n, 16):
+        store.put_ptrs_async(ptrs[i:i + 16], sizes[i:i + 16], keys_out=keys[i:i + 16], status_out=status[i:i + 16],
+                             prefix=prefix[i:i + 16])
+    store.wait_puts()
+    assert [k.tobytes().hex() for k in keys] == sc["ids"]
+    assert status.tolist() == sc["status"]
+    assert store.get_stats().dedup_hits == sc["ref_dedup_hits"]
+    uids = list(dict.fromkeys(sc["ids"]))
+    outs = [torch.empty(sc["size"], dtype=torch.uint8, device=DEV) for _ in uids]
+    found, _ = store.batch_get(uids, outs)
+    assert all(found)
+    by_id = {sc["ids"][j]: uniq[int(src[j])] for j in range(n)}
+    for u, o in zip(uids, outs):
+        assert np.array_equal(o.cpu().numpy(), by_id[u])
+    store.close()
