@@ -535,7 +535,7 @@ def main():
             "bytes_per_launch": int(sha_bytes_launch),
             "launches": int(d("sha_launches")),
             "achieved_is": "block bytes hashed / put-phase time (CUDA events on the caller's stream); up to "
-                           f"{args.pipeline_blocks or 32768} blocks hash at once in overlapping launches",
+                           f"{args.pipeline_blocks or ('65536' if world > 1 else '32768')} blocks hash at once in overlapping launches",
             "binding": {"pipe": "integer ALU (rotates, shifts, 3-input logic of SHA-256)",
                         "peak_gbs": round(alu_peak, 1), "frac": round(sha_achieved / alu_peak, 4),
                         "sm_mhz": sm_mhz, "sms": n_sms,
@@ -1037,7 +1037,8 @@ def config_dict(args):
                         f"{args.batch}) + batch_get all unique in uniform random order",
             "blocks": args.blocks, "block_bytes": args.block_bytes, "batch": args.batch,
             "put": "pipelined batch_put (cb_put_batch_async): each batch's SHA-256 launched at submission, up to "
-                   f"{args.pipeline_blocks or 32768} blocks hashing at once, batches placed in submission order",
+                   f"{args.pipeline_blocks or 'the library default of (32768 on one GPU, 65536 on a DHT member)'} "
+                   "blocks hashing at once, batches placed in submission order",
             "hash_sms": args.hash_sms or "library default (all SMs on one GPU; all but 8 on a DHT member)",
             "get": "stream-ordered batch_get (cb_get_batch_async)",
             "l2": "inputs (the distinct blocks, ~45 GB) resident in HBM, >> 126 MB L2 (no flush needed)",
