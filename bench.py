@@ -59,6 +59,9 @@ def parse():
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="cpu_baseline: repeat passes over the sample until this much put + get time is timed")
     p.add_argument("--copy-engine", type=int, default=0)
+    p.add_argument("--layout", choices=["shuffled", "stream"], default="shuffled",
+                   help="where the caller's distinct blocks sit in its buffer: shuffled (the default, like the CPU "
+                        "reference arm) or in the order of their first occurrence in the put stream")
     p.add_argument("--hash-sms", type=int, default=0,
                    help="SMs the pipelined puts' SHA-256 may occupy (0 = the library default: all on one GPU, "
                         "all but 8 on a DHT member)")
@@ -162,7 +165,15 @@ def gpu_blocks(args, rank, device):
     for o in range(0, flat.numel(), chunk):
         n = min(chunk, flat.numel() - o)
         flat[o:o + n] = torch.randn(n, generator=g, device=device, dtype=torch.float16)
-    pos = np.searchsorted(uniq, src)
+    if getattr(args, "layout", "shuffled") == "stream":
+        # distinct blocks stored in the order of their first occurrence in
+        # the put stream (copies still point at their originals)
+        _, first = np.unique(src, return_index=True)
+        slot = np.empty(len(uniq), np.int64)
+        slot[np.argsort(first)] = np.arange(len(uniq))
+        pos = slot[np.searchsorted(uniq, src)]
+    else:  # the distinct blocks at shuffled places, like the CPU reference arm's buffer
+        pos = np.searchsorted(uniq, src)
     ptrs = np.uint64(pool.data_ptr()) + pos.astype(np.uint64) * np.uint64(size)
     return pool, ptrs.astype(np.uint64), is_prefix.astype(np.uint8)
 
@@ -1036,6 +1047,9 @@ def config_dict(args):
                         f"byte-identical copies of 64 prefix blocks; step = clear + batch_put all (batch "
                         f"{args.batch}) + batch_get all unique in uniform random order",
             "blocks": args.blocks, "block_bytes": args.block_bytes, "batch": args.batch,
+            "layout": {"shuffled": "distinct blocks at shuffled places of one buffer (as in the CPU reference arm)",
+                       "stream": "distinct blocks in the order of their first occurrence in the put stream"}[
+                           getattr(args, "layout", "shuffled")],
             "put": "pipelined batch_put (cb_put_batch_async): each batch's SHA-256 launched at submission, up to "
                    f"{args.pipeline_blocks or 'the library default of (32768 on one GPU, 65536 on a DHT member)'} "
                    "blocks hashing at once, batches placed in submission order",
