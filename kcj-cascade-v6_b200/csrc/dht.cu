@@ -351,6 +351,8 @@ int Store::dht_attach(int r, int W, const uint8_t *uid) {
   memcpy(&id, uid, sizeof id);
   ncclConfig_t nc = NCCL_CONFIG_INITIALIZER;
   nc.blocking = 0;
+  nc.minCTAs = 1;
+  nc.maxCTAs = kDhtNcclCtas;  // every collective fits on the SMs the hash launches leave free
   int rc = dht_nccl(ncclCommInitRankConfig(&dht->comm, W, id, r, &nc), "ncclCommInitRankConfig");
   if (rc) {
     delete dht;

@@ -68,8 +68,6 @@ inline size_t digest_offset(int cap) { return align_up(sizeof(HashJob) * (size_t
 
 namespace {
 
-constexpr int kDhtSpareSms = 8;  // DHT member: SMs kept free of hash launches by default
-
 template <class F>
 F driver_fn(const char *name) {
   void *fn = nullptr;
@@ -136,7 +134,7 @@ int Store::pipeline_init() {
   }
   for (HashSlot &h : hslots) {
     if (!h.stream) CB_TRY_CUDA(create_hash_stream(h.stream), "hash stream");
-    if (!h.done) CB_TRY_CUDA(cudaEventCreateWithFlags(&h.done, cudaEventDisableTiming), "event");
+    h.h.flags = cudaHostAllocPortable | cudaHostAllocMapped;
   }
   for (ScratchSlot &s : sslots)
     if (!s.done) CB_TRY_CUDA(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming), "event");
@@ -183,7 +181,6 @@ void Store::pipeline_release() {
       cudaStreamSynchronize(h.stream);
       cudaStreamDestroy(h.stream);
     }
-    if (h.done) cudaEventDestroy(h.done);
     h.h.release();
     h.d.release();
     h = HashSlot{};
@@ -264,19 +261,24 @@ int Store::launch_open_slot() {
   const HashJob *jobs = reinterpret_cast<const HashJob *>(hp);
   for (int i = 0; i < h.n; ++i) bytes += jobs[i].size;
   CB_TRY_CUDA(cudaMemcpyAsync(dp, hp, sizeof(HashJob) * h.n, cudaMemcpyHostToDevice, h.stream), "H2D jobs");
-  // Not bracketed by timing events even when profiling: timing events around
-  // dozens of concurrent launches on their own streams halved the hashing
-  // throughput on B200. Their bytes and count are kept; a caller times the
-  // hashing as a whole (the put phase) on its own stream.
-  CB_TRY_CUDA(launch_sha256_batch(reinterpret_cast<const HashJob *>(dp), h.n,
-                                  reinterpret_cast<uint32_t *>(dp + o_dig), hash_lanes, d_err, h.stream, nullptr,
-                                  /*many_chains=*/true),
+  // The kernel is the last operation on its stream: it writes the digests
+  // straight into the slot's mapped host buffer, and completion is read from
+  // the stream itself (cudaStreamQuery / cudaStreamSynchronize). An
+  // operation queued after a long kernel (a D2H copy, an event record, the
+  // timing events of profiling) blocks the hardware queue it shares with
+  // other streams until the kernel ends: with dozens of hash streams that
+  // held back the placements' copies and a DHT member's collectives for tens
+  // of milliseconds (and, as timing events, halved the hashing throughput).
+  // Bytes and launch counts are kept; a caller times the hashing as a whole
+  // (the put phase) on its own stream.
+  void *hdig = nullptr;
+  CB_TRY_CUDA(cudaHostGetDevicePointer(&hdig, hp + o_dig, 0), "mapped digests");
+  CB_TRY_CUDA(launch_sha256_batch(reinterpret_cast<const HashJob *>(dp), h.n, static_cast<uint32_t *>(hdig),
+                                  hash_lanes, d_err, h.stream, nullptr, /*many_chains=*/true),
               "sha256 launch");
   launches++;
   prof_bytes[0] += bytes;
   prof_launches[0]++;
-  CB_TRY_CUDA(cudaMemcpyAsync(hp + o_dig, dp + o_dig, 32ull * h.n, cudaMemcpyDeviceToHost, h.stream), "D2H digests");
-  CB_TRY_CUDA(cudaEventRecord(h.done, h.stream), "event");
   h.launched = true;
   h.finished = false;
   hashing_blocks += (uint64_t)h.n;
@@ -286,7 +288,7 @@ int Store::launch_open_slot() {
 void Store::refresh_hashing() {
   for (HashSlot &h : hslots) {
     if (!h.launched || h.finished) continue;
-    if (cudaEventQuery(h.done) != cudaSuccess) continue;  // not ready (or an error the wait reports)
+    if (cudaStreamQuery(h.stream) != cudaSuccess) continue;  // not ready (or an error the wait reports)
     h.finished = true;
     hashing_blocks -= (uint64_t)h.n;
   }
@@ -381,7 +383,7 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
         if (h.launched && !h.finished) oldest = &h;
       }
       if (!oldest) break;
-      CB_TRY_CUDA(cudaEventSynchronize(oldest->done), "pipelined hash");
+      CB_TRY_CUDA(cudaStreamSynchronize(oldest->stream), "pipelined hash");
     }
     return CB_OK;
   }
@@ -408,7 +410,7 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
       }
     }
     if (!oldest) break;
-    CB_TRY_CUDA(cudaEventSynchronize(oldest->done), "pipelined hash");
+    CB_TRY_CUDA(cudaStreamSynchronize(oldest->stream), "pipelined hash");
   }
   return CB_OK;
 }
@@ -441,7 +443,7 @@ int Store::place_dht_batches(std::vector<AsyncPut> &g) {
     const uint8_t *dig = nullptr;
     if (b.slot >= 0) {
       HashSlot &h = hslots[b.slot];
-      CB_TRY_CUDA(cudaEventSynchronize(h.done), "pipelined hash");
+      CB_TRY_CUDA(cudaStreamSynchronize(h.stream), "pipelined hash");
       dig = static_cast<const uint8_t *>(h.h.ptr) + digest_offset(h.cap) + 32ull * b.off;
     }
     for (size_t i = 0; i < n; ++i) {
@@ -590,7 +592,7 @@ int Store::place_oldest() {
       rc = launch_open_slot();  // b is among the open slot's batches
       if (rc) return rc;
     }
-    CB_TRY_CUDA(cudaEventSynchronize(h.done), "pipelined hash");
+    CB_TRY_CUDA(cudaStreamSynchronize(h.stream), "pipelined hash");
     if (!h.finished) {
       h.finished = true;
       hashing_blocks -= (uint64_t)h.n;

@@ -91,7 +91,7 @@ cudaError_t PinnedBuf::ensure(size_t bytes) {
   ptr = nullptr;
   cap = 0;
   const size_t want = std::max<size_t>(align_up(bytes + bytes / 2, 4096), 1 << 20);
-  cudaError_t e = cudaHostAlloc(&ptr, want, cudaHostAllocPortable);
+  cudaError_t e = cudaHostAlloc(&ptr, want, flags);
   if (e == cudaSuccess) cap = want;
   return e;
 }

@@ -40,6 +40,7 @@ struct Trace {
 struct PinnedBuf {
   void *ptr = nullptr;
   size_t cap = 0;
+  unsigned flags = cudaHostAllocPortable;  // cudaHostAlloc flags of the next allocation
   cudaError_t ensure(size_t bytes);
   void release();
 };
@@ -52,6 +53,15 @@ struct DevBuf {
 };
 
 struct DhtState;  // dht.cu
+
+// A DHT member keeps kDhtSpareSms SMs free of hash launches (green context,
+// cb_config.hash_sms = 0), and its NCCL communicator runs every collective
+// with at most kDhtNcclCtas CTAs, so that a collective issued while the hash
+// CTAs fill their SMs runs at once on the spare ones: an NCCL kernel whose
+// CTAs (channels) cannot all be resident waits, on both ranks, until hash
+// CTAs retire.
+constexpr int kDhtSpareSms = 8;
+constexpr int kDhtNcclCtas = 4;
 
 struct Store {
   explicit Store(const cb_config &c);
@@ -225,10 +235,9 @@ struct Store {
   // tier moves, scatter, index insert) strictly in submission order, which
   // keeps the sequential dedup rule of put_batch exactly.
   struct HashSlot {
-    PinnedBuf h;  // [HashJob x n][digests n x 32]
+    PinnedBuf h;  // [HashJob x n][digests n x 32], mapped: the kernel writes the digests here
     DevBuf d;
     cudaStream_t stream = nullptr;
-    cudaEvent_t done = nullptr;  // digests are in h
     int n = 0;                   // blocks of the launch
     int cap = 0;                 // blocks the slot's buffers hold
     int users = 0;               // batches of the launch not placed yet
