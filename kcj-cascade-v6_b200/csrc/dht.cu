@@ -614,12 +614,15 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
               "D2H rep");
   rc = dht_sync(st);
   if (rc) return rc;
-  // 6. writers copy new blocks into the owners' pools
+  // 6. writers copy new blocks into the owners' pools: local destinations
+  // through the TMA engine on st (one issuing lane per SM, so it runs beside
+  // the hash CTAs), peer destinations through the LSU engine on peer_stream
+  // (many warps keep NVLink stores in flight), both at once.
   std::vector<PutRep> mine(static_cast<const PutRep *>(dht->h_send.ptr), static_cast<const PutRep *>(dht->h_send.ptr) + n);
-  std::vector<CopyDesc> desc;
-  std::vector<uint32_t> us;
-  uint32_t total = 0;
-  uint64_t bytes = 0;
+  std::vector<CopyDesc> ldesc, rdesc;
+  std::vector<uint32_t> lus, rus;
+  uint32_t ltotal = 0, rtotal = 0;
+  uint64_t lbytes = 0, rbytes = 0;
   std::vector<uint8_t> status(n, CB_PUT_FAILED);
   for (int j = 0; j < n; ++j) {
     const int i = order[j];
@@ -636,33 +639,64 @@ int Store::dht_put(const void *const *ptrs, const uint64_t *sizes, const uint8_t
     } else {
       dst = dht->pool[owner] + (mine[j].loc & kLocOffMask);
     }
-    if (owner != me) peer_bytes_written += sizes[i];
-    us.push_back(total);
-    desc.push_back(CopyDesc{dptr[i], dst, sizes[i], owner == me ? 0u : 1u});
-    total += (uint32_t)((sizes[i] + kCopyUnit - 1) / kCopyUnit);
-    bytes += sizes[i];
+    const uint32_t units = (uint32_t)((sizes[i] + kCopyUnit - 1) / kCopyUnit);
+    if (owner == me && mem_kind != CB_MEM_HOST) {
+      lus.push_back(ltotal);
+      ldesc.push_back(CopyDesc{dptr[i], dst, sizes[i], 0u});
+      ltotal += units;
+      lbytes += sizes[i];
+    } else {
+      if (owner != me) peer_bytes_written += sizes[i];
+      rus.push_back(rtotal);
+      rdesc.push_back(CopyDesc{dptr[i], dst, sizes[i], owner == me ? 0u : 1u});
+      rtotal += units;
+      rbytes += sizes[i];
+    }
   }
-  if (!desc.empty()) {
-    us.push_back(total);
-    const size_t o_us = align_up(sizeof(CopyDesc) * desc.size(), 256);
-    const size_t need = o_us + 4 * us.size();
-    CB_TRY_CUDA(h_scratch.ensure(need), "pinned");
-    CB_TRY_CUDA(d_scratch.ensure(need), "device");
+  if (!ldesc.empty() || !rdesc.empty()) {
+    if (!peer_stream) CB_TRY_CUDA(cudaStreamCreateWithFlags(&peer_stream, cudaStreamNonBlocking), "peer stream");
+    if (!ev_peer_in) CB_TRY_CUDA(cudaEventCreateWithFlags(&ev_peer_in, cudaEventDisableTiming), "event");
+    if (!ev_peer_out) CB_TRY_CUDA(cudaEventCreateWithFlags(&ev_peer_out, cudaEventDisableTiming), "event");
+    lus.push_back(ltotal);
+    rus.push_back(rtotal);
+    Layout L;
+    const size_t o_ld = L.add(sizeof(CopyDesc) * ldesc.size());
+    const size_t o_lu = L.add(4 * lus.size());
+    const size_t o_rd = L.add(sizeof(CopyDesc) * rdesc.size());
+    const size_t o_ru = L.add(4 * rus.size());
+    CB_TRY_CUDA(h_scratch.ensure(L.off), "pinned");
+    CB_TRY_CUDA(d_scratch.ensure(L.off), "device");
     uint8_t *h = static_cast<uint8_t *>(h_scratch.ptr);
-    memcpy(h, desc.data(), sizeof(CopyDesc) * desc.size());
-    memcpy(h + o_us, us.data(), 4 * us.size());
+    if (!ldesc.empty()) memcpy(h + o_ld, ldesc.data(), sizeof(CopyDesc) * ldesc.size());
+    memcpy(h + o_lu, lus.data(), 4 * lus.size());
+    if (!rdesc.empty()) memcpy(h + o_rd, rdesc.data(), sizeof(CopyDesc) * rdesc.size());
+    memcpy(h + o_ru, rus.data(), 4 * rus.size());
     uint8_t *d = static_cast<uint8_t *>(d_scratch.ptr);
-    CB_TRY_CUDA(cudaMemcpyAsync(d, h, need, cudaMemcpyHostToDevice, st), "H2D scatter");
-    const int nd = (int)desc.size();
-    CB_TRY_CUDA(timed(1, bytes, st,
-                      [&] {
-                        // peer stores: the LSU engine keeps far more bytes in
-                        // flight than one TMA lane per SM can for plain stores
-                        return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d),
-                                                 reinterpret_cast<const uint32_t *>(d + o_us), nd, total, 2, d_err,
-                                                 num_sms, st);
-                      }),
-                "scatter");
+    CB_TRY_CUDA(cudaMemcpyAsync(d, h, L.off, cudaMemcpyHostToDevice, st), "H2D scatter");
+    if (!rdesc.empty()) {
+      CB_TRY_CUDA(cudaEventRecord(ev_peer_in, st), "event");
+      CB_TRY_CUDA(cudaStreamWaitEvent(peer_stream, ev_peer_in, 0), "wait");
+      const int nr = (int)rdesc.size();
+      CB_TRY_CUDA(timed(1, rbytes, peer_stream,
+                        [&] {
+                          return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_rd),
+                                                   reinterpret_cast<const uint32_t *>(d + o_ru), nr, rtotal, 2,
+                                                   d_err, num_sms, peer_stream);
+                        }),
+                  "peer scatter");
+      CB_TRY_CUDA(cudaEventRecord(ev_peer_out, peer_stream), "event");
+    }
+    if (!ldesc.empty()) {
+      const int nl = (int)ldesc.size();
+      CB_TRY_CUDA(timed(1, lbytes, st,
+                        [&] {
+                          return launch_batch_copy(reinterpret_cast<const CopyDesc *>(d + o_ld),
+                                                   reinterpret_cast<const uint32_t *>(d + o_lu), nl, ltotal,
+                                                   copy_engine, d_err, num_sms, st);
+                        }),
+                  "local scatter");
+    }
+    if (!rdesc.empty()) CB_TRY_CUDA(cudaStreamWaitEvent(st, ev_peer_out, 0), "join");
   }
   // 7. closing barrier: every writer's copies precede every later op
   CB_TRY_CUDA(dht->d_misc.ensure(256), "device");

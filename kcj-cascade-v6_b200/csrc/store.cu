@@ -194,6 +194,12 @@ Store::~Store() {
     cudaStreamSynchronize(move_stream);
     cudaStreamDestroy(move_stream);
   }
+  if (peer_stream) {
+    cudaStreamSynchronize(peer_stream);
+    cudaStreamDestroy(peer_stream);
+  }
+  if (ev_peer_in) cudaEventDestroy(ev_peer_in);
+  if (ev_peer_out) cudaEventDestroy(ev_peer_out);
   if (ev_move_in) cudaEventDestroy(ev_move_in);
   if (ev_move_done) cudaEventDestroy(ev_move_done);
   for (cudaEvent_t e : prof_events) cudaEventDestroy(e);
@@ -331,17 +337,7 @@ int Store::read_error_word(unsigned *word, cudaStream_t st) {
 
 // ------------------------------------------------------------ packing
 
-// Lays out several device arrays in one pinned buffer so each call needs one
-// H2D copy; offsets are 256-byte aligned.
-struct Layout {
-  size_t off = 0;
-  size_t add(size_t bytes) {
-    off = align_up(off, 256);
-    const size_t o = off;
-    off += bytes;
-    return o;
-  }
-};
+
 
 // Copy descriptors + unit prefix for a list of (src, dst, size, flags).
 static uint32_t units_of(uint64_t size) {

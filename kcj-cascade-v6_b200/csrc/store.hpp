@@ -74,6 +74,10 @@ struct Store {
   int copy_engine = 1;  // 1 TMA bulk, 2 LSU
   int hash_lanes = 32;  // chains per warp in the SHA-256 kernel
   cudaStream_t own_stream = nullptr;
+  // DHT puts: the peer stores of a put run on peer_stream beside the local
+  // stores (TMA engine) on the put's stream; ev_peer_in/out join them.
+  cudaStream_t peer_stream = nullptr;
+  cudaEvent_t ev_peer_in = nullptr, ev_peer_out = nullptr;
 
   uint8_t *pool = nullptr;  // HBM slab pool
   uint64_t pool_bytes = 0;
@@ -374,6 +378,17 @@ struct Store {
 };
 
 inline uint64_t align_up(uint64_t x, uint64_t a) { return (x + a - 1) / a * a; }
+
+// Offsets of the parts of one scratch buffer, each 256-byte aligned.
+struct Layout {
+  size_t off = 0;
+  size_t add(size_t bytes) {
+    off = align_up(off, 256);
+    const size_t o = off;
+    off += bytes;
+    return o;
+  }
+};
 
 // dht.cu: the DHT's host-side routing and owner planning (also exported for
 // host-only use through cb_dht_route / cb_dht_plan_put).
