@@ -7,7 +7,7 @@
 //
 //   nvcc -gencode arch=compute_100a,code=sm_100a -O3 -std=c++17 -Iinclude \
 //        -Ikcj-cascade-v6_b200/csrc -o sha256_chains kcj-cascade-v6_b200/csrc/bench/sha256_chains.cu
-//   ./sha256_chains [max_blocks = 65536] [distinct = 4096]
+//   ./sha256_chains [max_blocks = 65536] [distinct = 4096] [shuffled = 0]
 //
 // Prints whether both kernels give equal digests, then GB/s (block bytes /
 // CUDA-event time) per configuration. Device memory: 917,504 B per distinct
@@ -38,6 +38,7 @@ using namespace chains_bench;
 int main(int argc, char **argv) {
   const int nmax = argc > 1 ? atoi(argv[1]) : 65536;
   const int nu = argc > 2 ? atoi(argv[2]) : 4096;  // distinct source blocks
+  const int shuffled = argc > 3 ? atoi(argv[3]) : 0;  // 1: chains read blocks in a shuffled order
   if (nmax < 2048 || nmax > (1 << 20) || nu < 1 || nu > 65536) {
     fprintf(stderr, "max_blocks must be in [2048, 1048576], distinct blocks in [1, 65536]\n");
     return 1;
@@ -57,6 +58,14 @@ int main(int argc, char **argv) {
   fill_blocks<<<1184, 256>>>(reinterpret_cast<uint32_t *>(buf), nu * S / 4);
   std::vector<HashJob> hj(nmax);
   for (int i = 0; i < nmax; ++i) hj[i] = HashJob{(uint64_t)(uintptr_t)(buf + (uint64_t)(i % nu) * S), S};
+  if (shuffled) {  // the i-th chain reads a block at a random place of the buffer
+    uint64_t x = 88172645463325252ull;
+    for (int i = nmax - 1; i > 0; --i) {
+      x ^= x << 13; x ^= x >> 7; x ^= x << 17;
+      const int j = (int)(x % (uint64_t)(i + 1));
+      const HashJob t = hj[i]; hj[i] = hj[j]; hj[j] = t;
+    }
+  }
   cudaMemcpy(jobs, hj.data(), nmax * sizeof(HashJob), cudaMemcpyHostToDevice);
 
   for (int v = 0; v < 2; ++v)
