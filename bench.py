@@ -68,7 +68,7 @@ def parse():
     p.add_argument("--no-profile", action="store_true",
                    help="no per-launch CUDA events in the store (roofline fields then come out empty)")
     p.add_argument("--pipeline-blocks", type=int, default=0,
-                   help="pipelined puts: blocks hashing at once (0 = the library default, 32768)")
+                   help="pipelined puts: blocks hashing at once (0 = the library default, 65536)")
     p.add_argument("--hash-lanes", type=int, default=32, help="reserved; the SHA-256 kernel runs 32 chains per warp")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -546,7 +546,7 @@ def main():
             "bytes_per_launch": int(sha_bytes_launch),
             "launches": int(d("sha_launches")),
             "achieved_is": "block bytes hashed / put-phase time (CUDA events on the caller's stream); up to "
-                           f"{args.pipeline_blocks or ('65536' if world > 1 else '32768')} blocks hash at once in overlapping launches",
+                           f"{args.pipeline_blocks or '65536'} blocks hash at once in overlapping launches",
             "binding": {"pipe": "integer ALU (rotates, shifts, 3-input logic of SHA-256)",
                         "peak_gbs": round(alu_peak, 1), "frac": round(sha_achieved / alu_peak, 4),
                         "sm_mhz": sm_mhz, "sms": n_sms,
@@ -1051,7 +1051,7 @@ def config_dict(args):
                        "stream": "distinct blocks in the order of their first occurrence in the put stream"}[
                            getattr(args, "layout", "shuffled")],
             "put": "pipelined batch_put (cb_put_batch_async): each batch's SHA-256 launched at submission, up to "
-                   f"{args.pipeline_blocks or 'the library default of (32768 on one GPU, 65536 on a DHT member)'} "
+                   f"{args.pipeline_blocks or 'the library default of 65536'} "
                    "blocks hashing at once, batches placed in submission order",
             "hash_sms": args.hash_sms or "library default (all SMs on one GPU; all but 8 on a DHT member)",
             "get": "stream-ordered batch_get (cb_get_batch_async)",

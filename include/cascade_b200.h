@@ -83,7 +83,7 @@ typedef struct cb_config {
                                    moves back to HBM: CB_PROMOTE_*          */
   int32_t reserved32;
   uint64_t pipeline_blocks;     /* cb_put_batch_async: blocks whose SHA-256
-                                   runs at once (0 = 32768; DHT member 65536) */
+                                   runs at once (0 = 65536) */
   int32_t hash_sms;             /* SMs the pipelined puts' SHA-256 launches
                                    may occupy (a green context; the rest stay
                                    free for collectives and copies): 0 = all

@@ -470,7 +470,7 @@ class DistributedConfig:
         self.profile = False          # time every kernel with CUDA events (stats *_ns)
         self.hash_lanes = 32          # reserved (the SHA-256 kernel runs 32 chains per warp)
         self.collective_timeout_ms = 0  # DHT: abort a collective after this long (0 = 600 s)
-        self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 32768; DHT 65536)
+        self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 65536)
         self.hash_sms = 0             # pipelined puts: SMs their SHA-256 may use (0 = all; DHT: all but 8)
 
 
@@ -501,7 +501,7 @@ class CascadeConfig:
         self.copy_engine = 0
         self.index_log2 = 16
         self.staging_bytes = 1 << 30
-        self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 32768; DHT 65536)
+        self.pipeline_blocks = 0      # pipelined puts: blocks hashing at once (0 = 65536)
         self.hash_sms = 0             # pipelined puts: SMs their SHA-256 may use (0 = all; DHT: all but 8)
 
 

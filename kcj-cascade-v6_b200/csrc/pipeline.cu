@@ -56,8 +56,10 @@ namespace cb {
 namespace {
 
 constexpr int kLaunchBlocks = 1024;              // queued small batches share a launch up to this size
-constexpr uint64_t kDefaultPipelineBlocks = 32768;     // blocks hashing at once (1 GPU)
-constexpr uint64_t kDefaultDhtPipelineBlocks = 65536;  // blocks hashing at once (DHT member)
+// blocks hashing at once by default (device-resident inputs; host blocks are
+// placed at submission): 65,536 chains keep ~3.5 warps on every SM
+// sub-partition, where the hash kernel reaches its ALU-bound rate
+constexpr uint64_t kDefaultPipelineBlocks = 65536;
 constexpr size_t kDhtPending = 8;                // DHT: batches submitted and not yet assigned (every rank alike)
 constexpr size_t kDhtGroup = 8;                  // DHT: batches placed together in one collective step
 constexpr int kScatterLsuCtasPerSm = 4;          // LSU engine (copy_engine = 2): CTAs per SM beside the hashes
@@ -373,7 +375,7 @@ int Store::put_async(const uint64_t *ptrs, const uint64_t *sizes, const uint8_t 
     }
     // at most `limit` blocks hash at once: wait for this GPU's own oldest
     // launch (no collective depends on it)
-    const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultDhtPipelineBlocks;
+    const uint64_t limit = cfg.pipeline_blocks ? cfg.pipeline_blocks : kDefaultPipelineBlocks;
     for (;;) {
       refresh_hashing();
       if (hashing_blocks <= limit) break;
