@@ -289,6 +289,34 @@ def test_pipelined_ids_match_the_golden_vectors():
             store.close()
 
 
+def test_pipelined_ids_of_ragged_warps():
+    """The many-chain kernel copies two 64-byte chunks of each of a warp's 32
+    blocks at a time through shared memory, up to the shortest block of the
+    warp, and each lane then reads the rest of its own block; a warp with an
+    unaligned block reads all of it lane by lane. IDs of 1024 blocks of
+    2-12 KB (sizes not multiples of 64; about 1 in 40 at an address that is
+    not a multiple of 16) equal the oracle's, in one launch and over batches
+    of 96."""
+    rng = np.random.default_rng(4242)
+    n = 1024
+    sizes = rng.integers(2048, 12289, n)
+    shifts = np.where(rng.integers(0, 40, n) == 0, rng.integers(1, 16, n), 0)
+    blocks = [rng.integers(0, 256, int(s), dtype=np.uint8) for s in sizes]
+    arrays = [np.concatenate([np.zeros(int(sh), np.uint8), b]) for sh, b in zip(shifts, blocks)]
+    buf, ptrs, _ = dev_blocks(arrays)
+    ptrs = (ptrs + shifts.astype(np.uint64)).astype(np.uint64)
+    sz = sizes.astype(np.uint64)
+    want = [O.block_id(b) for b in blocks]
+    for batch in (n, 96):
+        store = make_store(dedup_enabled=False)
+        keys = np.zeros((n, 16), np.uint8)
+        for i in range(0, n, batch):
+            store.put_ptrs_async(ptrs[i:i + batch], sz[i:i + batch], keys_out=keys[i:i + batch])
+        store.wait_puts()
+        assert [k.tobytes().hex() for k in keys] == want, batch
+        store.close()
+
+
 def test_hash_launches_confined_to_part_of_the_sms():
     """cb_config.hash_sms: the pipelined puts' SHA-256 launches run on hash
     streams of a green context holding part of the SMs (the rest stay free
